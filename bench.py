@@ -1,0 +1,405 @@
+"""Benchmark: Pairformer block time at N_token = 1024, bf16, on B200.
+
+Workload: a 48-block Pairformer trunk, N_token = 1024,
+c_pair = 128, c_single = 384, random-init weights ~N(0, 0.02) (LayerNorm
+gamma = 1, beta = 0), pair and single ~N(0, 1), pair mask = outer product of a
+sequence mask with a padded tail of 64 tokens, seed 3.  One step = one pass of
+the trunk (48 blocks); the metric is ms per block = step time / 48.
+
+  value  device-resident: pair / single already in HBM, CUDA events around
+         exactly K steps on the launching stream (max over ranks).
+  e2e    the same metric through the public module API with host buffers:
+         every step copies pair / single / masks from pinned host memory and
+         reads pair / single back, inside the timed region.
+  roofline  the dominant kernels timed live with CUDA events (same shapes as
+         inside the block): the triangle-attention flash kernel and the
+         triangle contraction GEMM, FLOPs / time against the measured bf16 peak.
+  cpu_baseline  the CPU oracle (a restatement of the reference torch path) on
+         this host's cores, one block at N = 256 in float32, scaled to N = 1024
+         by the algorithmic FLOP ratio.
+
+`--impl reference` times that CPU path alone on the same metric (the reference
+arm); under torchrun only rank 0 runs it.
+
+Multi-GPU (--gpus N under torchrun): replicas only in this version — every
+rank runs the full trunk on its own copy ("scaling": "weak" over independent
+trunks, one per GPU); value = the per-block time of the slowest rank.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Pairformer block ms at N_tok=1024 bf16"
+UNIT = "ms/block"
+N_TOKEN = 1024
+N_BLOCKS = 48
+C_PAIR, C_SINGLE = 128, 384
+SEED = 3
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
+                "bf16_tflops_sustained": data.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def _inputs(n: int, seed: int):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    pair = torch.randn(n, n, C_PAIR, generator=g)
+    single = torch.randn(n, C_SINGLE, generator=g)
+    seq_mask = torch.ones(n)
+    seq_mask[-64:] = 0
+    pair_mask = seq_mask[:, None] * seq_mask[None, :]
+    return pair, pair_mask, single, seq_mask
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"xfb_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        smax = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def _dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64,
+                     device="cuda" if dist.get_backend() == "nccl" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(sample_n: int = 256, threads: int | None = None) -> dict:
+    """Times the CPU oracle (reference torch path restated) on one block at
+    sample_n in float32 and scales it to N_TOKEN by the FLOP ratio."""
+    import torch
+
+    import oracle
+    from xfold_cpu_b200.nn import PairformerBlock, init_params_
+
+    if threads:
+        torch.set_num_threads(threads)
+    cores = torch.get_num_threads()
+    block = PairformerBlock(c_pair=C_PAIR, c_single=C_SINGLE)
+    init_params_(block, seed=SEED)
+    params = {k: v.detach().clone() for k, v in block.state_dict().items()}
+    pair, pair_mask, single, seq_mask = _inputs(sample_n, SEED)
+    with torch.inference_mode():
+        oracle.pairformer_block(pair, pair_mask, single, seq_mask, params)  # warm-up
+        t0 = time.perf_counter()
+        oracle.pairformer_block(pair, pair_mask, single, seq_mask, params)
+        dt = time.perf_counter() - t0
+    scale = (oracle.pairformer_block_flops(N_TOKEN)["total"]
+             / oracle.pairformer_block_flops(sample_n)["total"])
+    return {"value": dt * scale * 1e3, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": (f"1 Pairformer block at N={sample_n} fp32 (torch CPU oracle of the "
+                       f"reference torch path), {dt:.2f} s, scaled x{scale:.1f} by FLOPs to N={N_TOKEN}")}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(sample_n=256, threads=threads)
+        if i >= args.warmup:
+            samples.append(r["value"])
+    value = sum(samples) / len(samples)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value * N_BLOCKS,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "48-block Pairformer trunk, N_token=1024 (sampled)",
+                       "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR,
+                       "c_single": C_SINGLE, "seed": SEED},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": r["sample"]},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
+    """Times the triangle-attention flash kernel and the triangle contraction
+    GEMM on the block's shapes with CUDA events on the launching stream."""
+    import torch
+
+    import oracle
+    from xfold_cpu_b200 import native
+
+    n, c, heads, d = N_TOKEN, C_PAIR, 4, 32
+    g = torch.Generator(device=dev).manual_seed(11)
+    q = (torch.randn(n, heads, n, d, device=dev, generator=g) * 0.2).bfloat16()
+    k = (torch.randn(n, heads, n, d, device=dev, generator=g) * 0.2).bfloat16()
+    v = torch.randn(n, heads, n, d, device=dev, generator=g).bfloat16()
+    bias = torch.randn(heads, n, n, device=dev, generator=g).bfloat16()
+    seq = torch.ones(n, device=dev)
+    seq[-64:] = 0
+    mask = seq[:, None] * seq[None, :]
+    a = torch.randn(c, n, n, device=dev, generator=g).bfloat16()
+    b = torch.randn(c, n, n, device=dev, generator=g).bfloat16()
+    stream = torch.cuda.current_stream(dev)
+    results = {}
+    for name, fn, flops in (
+        ("flash_attn", lambda: native.dot_product_attention(q, k, v, mask, bias, q_pre_scaled=True),
+         4.0 * heads * n ** 3 * d),
+        ("triangle_contraction", lambda: native.gemm(a, b, out_dtype=torch.bfloat16),
+         2.0 * c * n ** 3),
+    ):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(max(steps, 5)):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e-3)
+        t = sum(times) / len(times)
+        achieved = flops / t / 1e12
+        results[name] = {"bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
+                         "ms_per_launch": round(t * 1e3, 4),
+                         "flops_per_launch": flops}
+    del q, k, v, bias, a, b
+    return results
+
+
+def run_cuda(args) -> None:
+    import torch
+
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local if torch.cuda.device_count() > local else 0)
+    torch.cuda.set_device(dev)
+    from xfold_cpu_b200 import _capi, native
+    from xfold_cpu_b200.nn import PairformerBlock, init_params_
+
+    native.check_device(dev)
+    peaks = _peaks()
+    n_tok, n_blocks = args.n, args.blocks
+    blocks = []
+    for i in range(n_blocks):
+        blk = PairformerBlock(c_pair=C_PAIR, c_single=C_SINGLE).eval()
+        init_params_(blk, seed=SEED * 1000 + i)
+        blocks.append(blk.to(dev))
+    pair_h, pair_mask_h, single_h, seq_mask_h = _inputs(n_tok, SEED)
+    pair_h, pair_mask_h = pair_h.pin_memory(), pair_mask_h.pin_memory()
+    single_h, seq_mask_h = single_h.pin_memory(), seq_mask_h.pin_memory()
+    pair = pair_h.to(dev)
+    single = single_h.to(dev)
+    pair_mask = pair_mask_h.to(dev)
+    seq_mask = seq_mask_h.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def trunk(p, s, pm, sm):
+        for blk in blocks:
+            blk(p, pm, s, sm)
+        return p, s
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            trunk(pair, single, pair_mask, seq_mask)
+        torch.cuda.synchronize(dev)
+        if _capi.device_error(clear=True):
+            raise RuntimeError("a device wait expired during warm-up")
+
+        # ---- device-resident timing
+        sampler = ClockSampler(dev.index if dev.index is not None else 0)
+        launches0 = _capi.launch_count()
+        _barrier(world)
+        torch.cuda.synchronize(dev)
+        sampler.start()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            trunk(pair, single, pair_mask, seq_mask)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        clocks = sampler.stop()
+        _barrier(world)
+        launches = (_capi.launch_count() - launches0) // args.steps
+        step_ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+        if args.skip_extras:
+            if rank == 0:
+                print(json.dumps({"profile_run": True, "n_token": n_tok, "blocks": n_blocks,
+                                  "ms_per_block": step_ms / n_blocks, "gpu_launches": int(launches)}))
+            return
+        # ---- end-to-end through the module API with host buffers
+        out_pair = torch.empty_like(pair_h).pin_memory()
+        out_single = torch.empty_like(single_h).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in (pair_h, single_h, pair_mask_h, seq_mask_h))
+        d2h = out_pair.numel() * 4 + out_single.numel() * 4
+        _barrier(world)
+        torch.cuda.synchronize(dev)
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            p = pair_h.to(dev, non_blocking=True)
+            s = single_h.to(dev, non_blocking=True)
+            pm = pair_mask_h.to(dev, non_blocking=True)
+            sm = seq_mask_h.to(dev, non_blocking=True)
+            p, s = trunk(p, s, pm, sm)
+            out_pair.copy_(p, non_blocking=True)
+            out_single.copy_(s, non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+        if _capi.device_error(clear=True):
+            raise RuntimeError("a device wait expired during the timed region")
+        finite = bool(torch.isfinite(out_pair).all() and torch.isfinite(out_single).all())
+
+        roof = _kernel_roofline(dev, args.steps, peaks) if rank == 0 else {}
+
+    if rank != 0:
+        return
+    base = cpu_baseline(sample_n=256) if world == 1 else None
+    dominant = max(roof.values(), key=lambda r: r["ms_per_launch"]) if roof else None
+    line = {
+        "metric": METRIC, "value": round(step_ms / n_blocks, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) pair/single, random-init N(0,0.02) weights)",
+        "config": {"workload": "48-block Pairformer trunk, N_token=1024 (BASELINE config C4)",
+                   "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR, "c_single": C_SINGLE,
+                   "heads_pair": 4, "heads_single": 16, "seed": SEED, "mask": "64-token padded tail",
+                   "l2": "inputs larger than L2 (pair f32 = 512 MiB)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "e2e": {"value": round(e2e_ms / n_blocks, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "note": "step = one 48-block trunk pass; host pinned in/out"},
+        "gpu_launches": int(launches),
+        "roofline": ({**{k: v for k, v in dominant.items()},
+                      "kernel": [k for k, v in roof.items() if v is dominant][0],
+                      "peak_source": peaks["source"]} if dominant else None),
+        "kernels": roof,
+        "clocks": clocks,
+        "cpu_baseline": base,
+        "finite": finite,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
+    ap.add_argument("--blocks", type=int, default=N_BLOCKS,
+                    help="trunk depth (48 for the metric; fewer only for profiling)")
+    ap.add_argument("--n", type=int, default=N_TOKEN,
+                    help="N_token (1024 for the metric; smaller only for profiling)")
+    ap.add_argument("--skip-extras", action="store_true",
+                    help="profiling mode: no e2e pass, kernel roofline or CPU baseline")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+    try:
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,240 @@
+/*
+ * xfold_b200 — C ABI of the B200 (sm_100a) Pairformer / diffusion hot path.
+ *
+ * This is the drop-in boundary for xfold's `cuda` operator backend.  It
+ * exposes the operators of the reference's native extension `af3_kernels._C`
+ * (af3_kernels/src/csrc/bindings.cpp:10-49) with plain pointers, sizes and a
+ * CUDA stream instead of ATen tensors, plus fused module-level entry points
+ * (grid self-attention, transition, single/diffusion self-attention) that the
+ * reference composes in Python.
+ *
+ * Conventions
+ *   - All pointers are device pointers on the current CUDA device; `stream` is
+ *     a cudaStream_t (NULL = legacy default stream).  Nothing synchronises.
+ *   - Dtype codes: XFB_F32 = 0, XFB_BF16 = 1.
+ *   - Weights are bf16 in nn.Linear layout [out_features][in_features]
+ *     (K-major: what the tensor cores read).  The reference's bridge passes
+ *     weight.T instead (xfold/fastnn/native.py:61); this ABI does not need the
+ *     transposed copy.  LayerNorm weights/biases are f32 [C]; NULL bias = none,
+ *     NULL weight = no affine.
+ *   - `weights_packed` mirrors the reference's `weights_packed` /
+ *     `weight_packed` flags: 0 = the separate nn.Linear weights are passed and
+ *     packed into the workspace on every call; 1 = `packed` points to the
+ *     buffer made once by the matching xfb_pack_* call (separate pointers
+ *     ignored, may be NULL).
+ *   - Scratch: each operator needs `xfb_*_workspace(...)` bytes of device
+ *     memory passed as (workspace, workspace_bytes); it is not retained.
+ *   - Outputs: `out` receives the update (accumulate = 0, the reference's
+ *     "return the update only" contract, triangle_multiplication.cpp:71) or
+ *     adds it into an f32 residual stream in place (accumulate = 1, the
+ *     `pair += op(pair)` of xfold/nn/pairformer.py:96-100).
+ *   - Return value: XFB_OK or an error code; xfb_last_error() describes the
+ *     last failure of the calling thread.  XFB_ERR_INVALID is a shape / dtype /
+ *     alignment error (the reference raises RuntimeError from TORCH_CHECK).
+ */
+#ifndef XFOLD_B200_H_
+#define XFOLD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XFB_API __attribute__((visibility("default")))
+
+enum {
+  XFB_OK = 0,
+  XFB_ERR_INVALID = 1,   /* bad argument (shape, dtype, alignment, workspace too small) */
+  XFB_ERR_CUDA = 2,      /* CUDA runtime / driver error (launch, tensor map) */
+  XFB_ERR_DEVICE = 3,    /* device is not sm_100 */
+  XFB_ERR_TIMEOUT = 4    /* a device-side bounded wait expired (see xfb_device_error) */
+};
+
+enum { XFB_F32 = 0, XFB_BF16 = 1, XFB_U8 = 2 };
+
+/* Message for the last error returned on this thread ("" if none). */
+XFB_API const char* xfb_last_error(void);
+
+/* Number of kernels launched by this library so far (process-wide). */
+XFB_API uint64_t xfb_launch_count(void);
+
+/* JSON description of the build and device (arch, SM count, nvcc flags).
+ * Counterpart of af3_kernels runtime_info() (bindings.cpp:13-20). */
+XFB_API int xfb_runtime_info(char* buf, int64_t buf_len);
+
+/* Preflight: the current device must be compute capability 10.0 and the
+ * kernels must load.  Mirrors the native-backend checks of
+ * run_alphafold.py:401-427 / xfold/fastnn/native.py:7-18. */
+XFB_API int xfb_check_device(void);
+
+/* Reads (and with clear != 0 resets) the device error word written by kernels
+ * whose bounded waits expired.  Synchronises the device. */
+XFB_API int xfb_device_error(int clear, uint32_t* code);
+
+/* Self-test of the bounded-wait path: one thread waits on an mbarrier nothing
+ * arrives on, gives up after `timeout_ns` and records code 0x1ff. */
+XFB_API int xfb_selftest_wait_timeout(int64_t timeout_ns, void* stream);
+
+/* ---------------------------------------------------------------- primitives */
+
+/* y[rows][cols] (bf16) = LayerNorm(x) * weight + bias over the last dim.
+ * cols in {64, 128, 384, 768}.  Replaces fastnn.LayerNorm
+ * (xfold/fastnn/layer_norm.py:55-80).  x: f32 or bf16. */
+XFB_API int xfb_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                           const float* weight, const float* bias, double eps, void* y,
+                           void* stream);
+
+/* y[m][n] = x[m][k] @ weight[n][k]^T (+ bias), bf16 in, f32 accumulate, output
+ * rounded like an autocast linear.  y_dtype f32 or bf16; accumulate = 1 adds into
+ * an f32 y.  Replaces af3_kernels linear (matrix.cpp:119-129).
+ * Requires k % 8 == 0 and n % 8 == 0. */
+XFB_API int xfb_linear(const void* x, int64_t m, int64_t k, const void* weight, int64_t n,
+                       const float* bias, void* y, int y_dtype, int accumulate, void* stream);
+
+/* Batched GEMM, bf16 in, f32 accumulate: c[b][i][j] = sum_k A_b(i, k) B_b(j, k).
+ * K-major operands: a [batch][m][k], b [batch][n][k]; MN-major (a_mn_major =
+ * b_mn_major = 1): a [batch][k][m], b [batch][k][n].  c [batch][m][n], f32 or bf16.
+ * Counterpart of af3_kernels gemm (bindings.cpp:26, tools.cpp); it is the
+ * triangle contraction kernel on its own. */
+XFB_API int xfb_gemm(const void* a, const void* b, void* c, int64_t batch, int64_t m, int64_t n,
+                     int64_t k, int a_mn_major, int b_mn_major, int c_dtype, void* stream);
+
+/* Packs transition1.weight [2n][k] (first n rows: SiLU gate) for the GLU kernel. */
+XFB_API int64_t xfb_pack_glu_weight_bytes(int64_t n, int64_t k);
+XFB_API int xfb_pack_glu_weight(const void* weight, int w_dtype, int64_t n, int64_t k,
+                                void* packed, void* stream);
+
+/* y[m][n] = silu(x @ W[:n]^T) * (x @ W[n:]^T), bf16.  weight = transition1.weight
+ * [2n][k] (unpacked) or the packed buffer.  Replaces af3_kernels
+ * gated_linear_unit (gated_linear_unit.cpp:78-121), whose weight is W^T [k][2n].
+ * Requires n % 64 == 0, k % 8 == 0. */
+XFB_API int64_t xfb_gated_linear_unit_workspace(int64_t m, int64_t k, int64_t n);
+XFB_API int xfb_gated_linear_unit(const void* x, int64_t m, int64_t k, const void* weight,
+                                  int64_t n, int weights_packed, void* y, void* workspace,
+                                  int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- triangle multiplication */
+
+/* Packed projection ‖ gate ‖ gating_linear weights for the fused input projection. */
+XFB_API int64_t xfb_pack_triangle_weights_bytes(int64_t c);
+XFB_API int xfb_pack_triangle_weights(const void* projection, const void* gate,
+                                      const void* gating_linear, int w_dtype, int64_t c,
+                                      void* packed, void* stream);
+
+/* TriangleMultiplication update for pair [n][n][c] (f32 or bf16, contiguous):
+ *   x = LN(pair); p = (x W_p^T) * mask * sigmoid(x W_g^T); a = p[..., 0::2], b = p[..., 1::2]
+ *   z[c][i][j] = sum_k a[c][i][k] b[c][j][k]   (outgoing)
+ *              = sum_k a[c][k][j] b[c][k][i]   (incoming)
+ *   update = (LN_center(z) W_o^T) * sigmoid(x W_gl^T)
+ * mask: f32 [n][n] or NULL.  Weights: projection, gate [2c][c]; output_weight,
+ * gating_weight [c][c].  out: update (out_dtype f32/bf16, accumulate 0) or
+ * pair += update (f32, accumulate 1).  c in {64, 128}.
+ * Replaces af3_kernels triangle_multiplication (triangle_multiplication.cpp:6-73,
+ * signature bindings.cpp:35-43) and TriangleMultiplication._forward_torch
+ * (xfold/nn/triangle_multiplication.py:71-105). */
+XFB_API int64_t xfb_triangle_multiplication_workspace(int64_t n, int64_t c);
+XFB_API int xfb_triangle_multiplication(
+    const void* pair, int pair_dtype, int64_t n, int64_t c, const float* mask, int outgoing,
+    const float* left_weight, const float* left_bias, const void* projection, const void* gate,
+    const float* center_weight, const float* center_bias, const void* output_weight,
+    const void* gating_weight, double left_eps, double center_eps, int weights_packed,
+    const void* packed, void* out, int out_dtype, int accumulate, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/* out[B][H][nq][dv] (bf16) = softmax(q k^T * d^-0.5 + bias, mask) v.
+ * q [B][H][nq][d], k [B][H][nk][d], v [B][H][nk][d] bf16 contiguous, d = dv <= 64.
+ * mask: key mask [B or 1][nk] (mask_dtype XFB_F32 or XFB_U8, nonzero = keep),
+ *   mask_batched = 0 for a shared [nk] mask, or NULL; masked keys get logit -1e9.
+ * bias: [B or 1][H][nq][nk] (bias_dtype f32 or bf16), bias_batched = 0 when shared
+ *   across B, or NULL.
+ * q_pre_scaled = 1 when q already carries the d^-0.5 factor (reference bridge,
+ * xfold/fastnn/attention.py:21-29).  Replaces af3_kernels dot_product_attention
+ * (dot_product_attention.cpp:110-174) and fastnn.dot_product_attention_torch
+ * (xfold/fastnn/attention.py:45-66). */
+XFB_API int64_t xfb_dot_product_attention_workspace(int64_t B, int64_t H, int64_t nq,
+                                                    int64_t nk, int64_t d);
+XFB_API int xfb_dot_product_attention(const void* q, const void* k, const void* v, int64_t B,
+                                      int64_t H, int64_t nq, int64_t nk, int64_t d,
+                                      const void* mask, int mask_dtype, int mask_batched,
+                                      const void* bias, int bias_dtype, int bias_batched,
+                                      int q_pre_scaled, void* out, void* workspace,
+                                      int64_t workspace_bytes, void* stream);
+
+/* Packed q ‖ k ‖ v ‖ gating_query weights [4c][c]. */
+XFB_API int64_t xfb_pack_attention_weights_bytes(int64_t c);
+XFB_API int xfb_pack_attention_weights(const void* q_w, const void* k_w, const void* v_w,
+                                       const void* gate_w, int w_dtype, int64_t c,
+                                       void* packed, void* stream);
+
+/* GridSelfAttention update for pair [n][n][c] (triangle attention around the
+ * starting node, transpose = 0, or the ending node, transpose = 1):
+ *   x = LN(pair); bias[h][i][j] = x[i][j] . w_b[h]  (before any transpose)
+ *   per batch row r: softmax(q k^T / sqrt(d) + bias, pair_mask[r][:]) v, gated by
+ *   sigmoid(x W_gate^T), then output_projection.
+ * mask: f32 [n][n] or NULL (row r is the key mask of batch row r in both
+ * directions, as xfold/nn/attention.py:100).  bias_weight [heads][c].
+ * c in {64, 128}, c / heads in {16, 32}.  Replaces GridSelfAttention.forward
+ * (xfold/nn/attention.py:80-105). */
+XFB_API int64_t xfb_grid_self_attention_workspace(int64_t n, int64_t c, int64_t heads);
+XFB_API int xfb_grid_self_attention(
+    const void* pair, int pair_dtype, int64_t n, int64_t c, int64_t heads, const float* mask,
+    int transpose, const float* norm_weight, const float* norm_bias, double eps,
+    const void* bias_weight, const void* q_w, const void* k_w, const void* v_w,
+    const void* gate_w, const void* output_w, int weights_packed, const void* packed,
+    void* out, int out_dtype, int accumulate, void* workspace, int64_t workspace_bytes,
+    void* stream);
+
+/* ---------------------------------------------------------------- transitions */
+
+/* GLU transition x[rows][c] -> update (Transition, xfold/nn/primitives.py:33-37;
+ * DiffusionTransition, xfold/nn/diffusion_transformer.py:124-128):
+ *   y = LN(x) [* mod_scale + mod_shift]; h = silu(y W1[:fc]^T) * (y W1[fc:]^T);
+ *   update = (h W2^T) [* out_gate]
+ * w1 = transition1.weight [2fc][c] (or packed), w2 = transition2.weight [c][fc].
+ * mod_scale / mod_shift / out_gate: bf16 [rows][c] or NULL (adaptive
+ * conditioning, already passed through sigmoid where the reference does).
+ * c in {64, 128, 384, 768}; f*c % 64 == 0. */
+XFB_API int64_t xfb_transition_workspace(int64_t rows, int64_t c, int64_t factor);
+XFB_API int xfb_transition(const void* x, int x_dtype, int64_t rows, int64_t c,
+                           int64_t factor, const float* norm_weight, const float* norm_bias,
+                           double eps, const void* mod_scale, const void* mod_shift,
+                           const void* w1, int weights_packed, const void* w2,
+                           const void* out_gate, void* out, int out_dtype, int accumulate,
+                           void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- single attention */
+
+/* SelfAttention with pair bias for x [n][c] (xfold/nn/diffusion_transformer.py:184-217):
+ *   y = LN(x) [* mod_scale + mod_shift]; q = y Wq^T + q_bias, k, v, gate;
+ *   o = softmax(q k^T / sqrt(d) + pair_logits, seq_mask) v * sigmoid(gate);
+ *   update = (o Wo^T) [* out_gate]
+ * pair_logits: bf16 [heads][n][n] or NULL; mask: f32 [n] or NULL;
+ * packed = xfb_pack_attention_weights of (q, k, v, gating_query) when
+ * weights_packed; wo = adaptive_zero_init.transition2.weight [c][c].
+ * c in {128, 384, 768}, c / heads <= 64. */
+XFB_API int64_t xfb_self_attention_workspace(int64_t n, int64_t c, int64_t heads);
+XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c, int64_t heads,
+                               const float* mask, const void* pair_logits,
+                               const float* norm_weight, const float* norm_bias, double eps,
+                               const void* mod_scale, const void* mod_shift, const void* q_w,
+                               const float* q_bias, const void* k_w, const void* v_w,
+                               const void* gate_w, int weights_packed, const void* packed,
+                               const void* wo, const void* out_gate, void* out, int out_dtype,
+                               int accumulate, void* workspace, int64_t workspace_bytes,
+                               void* stream);
+
+/* Pair-logit projection for the single track (xfold/nn/pairformer.py:103-106):
+ * logits[h][i][j] = LN(pair)[i][j] . w[h], bf16 [heads][n][n], heads <= 16. */
+XFB_API int xfb_pair_logits(const void* pair, int pair_dtype, int64_t n, int64_t c,
+                            int64_t heads, const float* norm_weight, const float* norm_bias,
+                            double eps, const void* w, void* logits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XFOLD_B200_H_ */

@@ -1,0 +1,152 @@
+"""Module parity on the GPU: the `cuda` modules against the CPU oracle on the
+same state_dict and inputs (bf16 path vs float32 oracle, tolerance 1e-2 on the
+update, max|delta| / max|ref|)."""
+
+import pytest
+import torch
+
+import oracle
+from xfold_cpu_b200 import _capi
+from xfold_cpu_b200.nn import (DiffusionTransformer, GridSelfAttention, PairformerBlock,
+                               SelfAttention, Transition, TriangleMultiplication, init_params_)
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+DEV = torch.device("cuda")
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    _capi.device_error(clear=True)
+    yield
+    torch.cuda.synchronize()
+    assert _capi.device_error(clear=True) == 0
+
+
+def _params(module):
+    return {k: v.detach().cpu().clone() for k, v in module.state_dict().items()}
+
+
+def _masks(n, tail, seed=0):
+    seq = torch.ones(n)
+    seq[-tail:] = 0
+    return seq, seq[:, None] * seq[None, :]
+
+
+@pytest.mark.parametrize("n", [48, 130])
+def test_pairformer_block(n):
+    torch.manual_seed(0)
+    block = PairformerBlock().eval()
+    init_params_(block, seed=1, perturb_layer_norm=True)
+    g = torch.Generator().manual_seed(2)
+    pair = torch.randn(n, n, 128, generator=g)
+    single = torch.randn(n, 384, generator=g)
+    seq, pmask = _masks(n, 5)
+    ref_p, ref_s = oracle.pairformer_block(pair, pmask, single, seq, _params(block))
+    block = block.to(DEV)
+    p, s = pair.to(DEV), single.to(DEV)
+    with torch.inference_mode():
+        block(p, pmask.to(DEV), s, seq.to(DEV))
+    assert oracle.relative_error(p.cpu() - pair, ref_p - pair) < TOL
+    assert oracle.relative_error(s.cpu() - single, ref_s - single) < TOL
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_triangle_module_forward_and_accumulate(outgoing):
+    n = 96
+    mod = TriangleMultiplication(128, _outgoing=outgoing).eval()
+    init_params_(mod, seed=3, perturb_layer_norm=True)
+    g = torch.Generator().manual_seed(4)
+    pair = torch.randn(n, n, 128, generator=g)
+    _, pmask = _masks(n, 7)
+    ref = oracle.triangle_multiplication(pair, pmask, _params(mod), outgoing)
+    mod = mod.to(DEV)
+    with torch.inference_mode():
+        upd = mod(pair.to(DEV), pmask.to(DEV))
+        assert upd.dtype == torch.bfloat16 and upd.shape == pair.shape
+        assert oracle.relative_error(upd.float().cpu(), ref) < TOL
+        p = pair.to(DEV)
+        mod.accumulate_(p, pmask.to(DEV))
+    assert oracle.relative_error(p.cpu() - pair, ref) < TOL
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+def test_grid_attention_module(transpose):
+    n = 80
+    mod = GridSelfAttention(128, 4, transpose=transpose).eval()
+    init_params_(mod, seed=5, std=0.05, perturb_layer_norm=True)
+    g = torch.Generator().manual_seed(6)
+    pair = torch.randn(n, n, 128, generator=g)
+    _, pmask = _masks(n, 9)
+    ref = oracle.grid_self_attention(pair, pmask, _params(mod), transpose, 4)
+    mod = mod.to(DEV)
+    with torch.inference_mode():
+        upd = mod(pair.to(DEV), pmask.to(DEV))
+    assert oracle.relative_error(upd.float().cpu(), ref) < TOL
+
+
+def test_transition_module_single_width():
+    n = 333
+    mod = Transition(384).eval()
+    init_params_(mod, seed=7, perturb_layer_norm=True)
+    x = torch.randn(n, 384, generator=torch.Generator().manual_seed(8))
+    ref = oracle.transition(x, _params(mod))
+    mod = mod.to(DEV)
+    with torch.inference_mode():
+        upd = mod(x.to(DEV))
+    assert oracle.relative_error(upd.float().cpu(), ref) < TOL
+
+
+def test_conditioned_self_attention():
+    n, c = 160, 768
+    mod = SelfAttention(c, 384, 16, use_single_cond=True).eval()
+    init_params_(mod, seed=9, std=0.05, perturb_layer_norm=True)
+    g = torch.Generator().manual_seed(10)
+    x = torch.randn(n, c, generator=g)
+    cond = torch.randn(n, 384, generator=g)
+    logits = torch.randn(16, n, n, generator=g)
+    seq, _ = _masks(n, 3)
+    ref = oracle.self_attention(x, seq, logits.bfloat16().float(), _params(mod), cond, 16, True)
+    mod = mod.to(DEV)
+    with torch.inference_mode():
+        upd = mod(x.to(DEV), seq.to(DEV), logits.to(DEV), cond.to(DEV))
+    assert oracle.relative_error(upd.float().cpu(), ref) < TOL
+
+
+def test_diffusion_transformer_two_blocks():
+    n, c = 96, 768
+    mod = DiffusionTransformer(c_act=c, num_blocks=2, super_block_size=2).eval()
+    init_params_(mod, seed=11, std=0.05, perturb_layer_norm=True)
+    g = torch.Generator().manual_seed(12)
+    act = torch.randn(n, c, generator=g)
+    cond = torch.randn(n, 384, generator=g)
+    pair_cond = torch.randn(n, n, 128, generator=g)
+    seq, _ = _masks(n, 4)
+    params = _params(mod)
+    ref = act.clone()
+    pa = oracle.layer_norm(pair_cond, params["pair_input_layer_norm.weight"],
+                           params["pair_input_layer_norm.bias"])
+    logits = oracle.linear(pa, params["pair_logits_projection.0.weight"]).reshape(n, n, 2, 16)
+    logits = logits.permute(2, 3, 0, 1)
+    for j in range(2):
+        ref += oracle.self_attention(ref, seq, logits[j].bfloat16().float(), params, cond, 16, True,
+                                     prefix=f"self_attention.{j}.")
+        ref += oracle.diffusion_transition(ref, cond, params, True, prefix=f"transition_block.{j}.")
+    mod = mod.to(DEV)
+    a = act.to(DEV)
+    with torch.inference_mode():
+        mod(a, seq.to(DEV), cond.to(DEV), pair_cond.to(DEV))
+    assert oracle.relative_error(a.cpu() - act, ref - act) < TOL
+
+
+def test_unsupported_backend_raises():
+    from xfold_cpu_b200.fastnn import config
+
+    mod = Transition(128).to(DEV)
+    config.gated_linear_unit_implementation = "torch"
+    try:
+        with pytest.raises(ValueError):
+            mod(torch.randn(4, 128, device=DEV))
+    finally:
+        config.gated_linear_unit_implementation = "cuda"

@@ -1,0 +1,1131 @@
+// extern "C" entry points of libxfold_b200.so (declared in include/xfold_b200.h).
+//
+// Single translation unit: it includes every kernel header so the device
+// error word and all template instantiations live in one module.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include "../../include/xfold_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "layer_norm.cuh"
+
+#ifndef XFB_NVCC_FLAGS
+#define XFB_NVCC_FLAGS "unknown"
+#endif
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define XFB_REQUIRE(cond, msg)                                        \
+  do {                                                                \
+    if (!(cond)) return fail(XFB_ERR_INVALID, std::string(msg));      \
+  } while (0)
+
+#define XFB_CUDA(call)                                                                     \
+  do {                                                                                     \
+    cudaError_t e_ = (call);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      return fail(XFB_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));       \
+  } while (0)
+
+#define XFB_TRY(expr)           \
+  do {                          \
+    int rc_ = (expr);           \
+    if (rc_ != XFB_OK) return rc_; \
+  } while (0)
+
+#define XFB_LAUNCHED()                                                                 \
+  do {                                                                                 \
+    g_launches.fetch_add(1, std::memory_order_relaxed);                                \
+    cudaError_t e_ = cudaGetLastError();                                               \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(XFB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+// Number of kernels this library has launched (all devices, all threads).
+std::atomic<unsigned long long> g_launches{0};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+int64_t pad_pitch(int64_t n) { return round_up(n, 8); }
+
+// ------------------------------------------------------------------ device info
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+int current_device(int* dev) {
+  XFB_CUDA(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(XFB_ERR_INVALID, "device index out of range");
+  return XFB_OK;
+}
+
+int sm_count(int* out) {
+  int dev;
+  XFB_TRY(current_device(&dev));
+  std::call_once(g_dev_once[dev], [dev]() {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = v;
+  });
+  *out = g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+  return XFB_OK;
+}
+
+// ------------------------------------------------------------------ tensor maps
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encoder() {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  if (g_encode == nullptr) return fail(XFB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  return XFB_OK;
+}
+
+// 3-D bf16 tensor map: element (x, y, z) at base + x*2 + y*stride1 + z*stride2.
+int make_map(CUtensorMap* map, const void* base, uint64_t dx, uint64_t dy, uint64_t dz,
+             uint64_t stride1, uint64_t stride2, uint32_t bx, uint32_t by,
+             CUtensorMapSwizzle swz) {
+  XFB_TRY(get_encoder());
+  if (!aligned16(base)) return fail(XFB_ERR_INVALID, "TMA operand base is not 16-byte aligned");
+  if (stride1 % 16 != 0 || stride2 % 16 != 0)
+    return fail(XFB_ERR_INVALID, "TMA operand row stride is not a multiple of 16 bytes");
+  if (dz == 1) stride2 = std::max<uint64_t>(stride2, stride1 * dy);
+  stride2 = round_up(static_cast<int64_t>(stride2), 16);
+  cuuint64_t dims[3] = {dx, dy, dz};
+  cuuint64_t strides[2] = {stride1, stride2};
+  cuuint32_t box[3] = {bx, by, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof(buf),
+             "cuTensorMapEncodeTiled failed (%d): dims %llu %llu %llu strides %llu %llu box %u %u",
+             static_cast<int>(r), (unsigned long long)dx, (unsigned long long)dy,
+             (unsigned long long)dz, (unsigned long long)stride1, (unsigned long long)stride2, bx,
+             by);
+    return fail(XFB_ERR_CUDA, buf);
+  }
+  return XFB_OK;
+}
+
+template <class Kernel>
+int set_smem(Kernel kernel, int bytes) {
+  XFB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return XFB_OK;
+}
+
+// ------------------------------------------------------------------ GEMM launcher
+
+// A: K-major -> element (m, k) at A[bat*a_bs + m*lda + k]; MN-major -> A[bat*a_bs + k*lda + m].
+// B: K-major -> element (n, k) at B[bat*b_bs + n*ldb + k]; MN-major -> B[bat*b_bs + k*ldb + n].
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+int run_gemm(const void* A, int64_t lda, int64_t a_bs, const void* B, int64_t ldb, int64_t b_bs,
+             int64_t M, int64_t N, int64_t K, int64_t batch, const Epi& epi, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || batch <= 0) return XFB_OK;
+  if (K <= 0) return fail(XFB_ERR_INVALID, "GEMM with empty reduction dimension");
+  if (M > (1ll << 31) - 256 || N > (1 << 30)) return fail(XFB_ERR_INVALID, "GEMM too large");
+  CUtensorMap ta, tb;
+  if (A_MN) {
+    XFB_TRY(make_map(&ta, A, M, K, batch, lda * 2, a_bs * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B));
+  } else {
+    XFB_TRY(make_map(&ta, A, K, M, batch, lda * 2, a_bs * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  if (B_MN) {
+    XFB_TRY(make_map(&tb, B, N, K, batch, ldb * 2, b_bs * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B));
+  } else {
+    XFB_TRY(make_map(&tb, B, K, N, batch, ldb * 2, b_bs * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  xfb::GemmShape sh;
+  sh.M = static_cast<int>(M);
+  sh.N = static_cast<int>(N);
+  sh.K = static_cast<int>(K);
+  sh.batch = static_cast<int>(batch);
+  sh.m_tiles = static_cast<int>((M + 127) / 128);
+  sh.n_tiles = static_cast<int>((N + BN - 1) / BN);
+  sh.k_blocks = static_cast<int>((K + 63) / 64);
+  const int64_t total = static_cast<int64_t>(sh.m_tiles) * sh.n_tiles * sh.batch;
+  if (total > (1ll << 31) - 1) return fail(XFB_ERR_INVALID, "GEMM has too many tiles");
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int grid = static_cast<int>(std::min<int64_t>(total, sms));
+  using L = xfb::GemmSmem<BN, STAGES>;
+  auto kernel = xfb::gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, Epi>;
+  XFB_TRY(set_smem(kernel, L::kLaunchBytes));
+  kernel<<<grid, xfb::kGemmThreads, L::kLaunchBytes, st>>>(ta, tb, sh, epi);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+// Row-major K-major GEMM with a plain (linear) epilogue, BN = 128.
+int linear_core(const bf16* x, int64_t m, int64_t k, int64_t ldx, const bf16* w, int64_t n,
+                const float* bias, const bf16* gate, int64_t ld_gate, void* out, int out_f32,
+                int accumulate, int64_t ld_out, cudaStream_t st) {
+  xfb::EpiLinear<128> epi;
+  epi.out = out;
+  epi.ld_out = ld_out;
+  epi.bstride_out = 0;
+  epi.out_f32 = out_f32;
+  epi.accumulate = accumulate;
+  epi.bias = bias;
+  epi.gate = gate;
+  epi.ld_gate = ld_gate;
+  epi.M = static_cast<int>(m);
+  epi.N = static_cast<int>(n);
+  return run_gemm<128, 6, false, false>(x, ldx, 0, w, k, 0, m, n, k, 1, epi, st);
+}
+
+// ------------------------------------------------------------------ LayerNorm launcher
+
+int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t ldx,
+                   const float* w, const float* b, double eps, bf16* y, int64_t ldy,
+                   const bf16* mod_scale, const bf16* mod_shift, const bf16* wh, int heads,
+                   bf16* head_out, int64_t head_ld, cudaStream_t st) {
+  if (rows <= 0) return XFB_OK;
+  XFB_REQUIRE(x_dtype == XFB_F32 || x_dtype == XFB_BF16, "LayerNorm input must be f32 or bf16");
+  XFB_REQUIRE(heads >= 0 && heads <= 16, "head projection supports at most 16 heads");
+  XFB_REQUIRE(aligned16(x) && (y == nullptr || aligned16(y)), "LayerNorm buffers must be 16-byte aligned");
+  xfb::LnArgs a;
+  a.x = x;
+  a.rows = rows;
+  a.ldx = ldx;
+  a.w = w;
+  a.b = b;
+  a.eps = static_cast<float>(eps);
+  a.y = y;
+  a.ldy = ldy;
+  a.mod_scale = mod_scale;
+  a.mod_shift = mod_shift;
+  a.wh = heads > 0 ? wh : nullptr;
+  a.heads = heads;
+  a.head_out = head_out;
+  a.head_ld = head_ld;
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int64_t warps = (rows + 0);
+  const int blocks = static_cast<int>(std::min<int64_t>((warps + 7) / 8, int64_t(sms) * 16));
+  const dim3 block(256);
+#define XFB_LN_CASE(C, T, HP)                                        \
+  xfb::ln_rows_kernel<C, T, HP><<<blocks, block, 0, st>>>(a);        \
+  XFB_LAUNCHED();                                                    \
+  return XFB_OK;
+#define XFB_LN_HEADS(C, T)                          \
+  if (heads == 0) { XFB_LN_CASE(C, T, 0) }          \
+  if (heads <= 4) { XFB_LN_CASE(C, T, 4) }          \
+  XFB_LN_CASE(C, T, 16)
+#define XFB_LN_NOHEADS(C, T) XFB_LN_CASE(C, T, 0)
+#define XFB_LN_TYPES_NOHEADS(C)                                          \
+  XFB_REQUIRE(heads == 0, "head projection requires C <= 128");          \
+  if (x_dtype == XFB_F32) { XFB_LN_NOHEADS(C, float) }                   \
+  XFB_LN_NOHEADS(C, bf16)
+#define XFB_LN_TYPES(C)                                                  \
+  if (x_dtype == XFB_F32) { XFB_LN_HEADS(C, float) }                     \
+  XFB_LN_HEADS(C, bf16)
+  switch (c) {
+    case 64: { XFB_LN_TYPES(64) }
+    case 128: { XFB_LN_TYPES(128) }
+    case 384: { XFB_LN_TYPES_NOHEADS(384) }
+    case 768: { XFB_LN_TYPES_NOHEADS(768) }
+    default:
+      return fail(XFB_ERR_INVALID, "LayerNorm width must be 64, 128, 384 or 768");
+  }
+#undef XFB_LN_TYPES
+#undef XFB_LN_TYPES_NOHEADS
+#undef XFB_LN_NOHEADS
+#undef XFB_LN_HEADS
+#undef XFB_LN_CASE
+}
+
+// ------------------------------------------------------------------ weight packing
+
+// mode 0: triangle (proj/gate interleaved by 64 rows, then gating_linear)
+// mode 1: GLU (gate/value interleaved by 64 rows)
+// mode 2: concatenation of four [c][c] matrices
+__global__ void pack_weights_kernel(const void* s0, const void* s1, const void* s2,
+                                    const void* s3, int src_f32, int mode, int64_t c_or_n,
+                                    int64_t k, int64_t rows, bf16* dst) {
+  const int64_t total = rows * k;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / k;
+    const int64_t col = idx - r * k;
+    const void* src = nullptr;
+    int64_t srow = 0;
+    if (mode == 0) {
+      const int64_t c = c_or_n;
+      if (r < 4 * c) {
+        const int64_t t = r / 128, w = r % 128;
+        src = (w < 64) ? s0 : s1;
+        srow = 64 * t + (w % 64);
+      } else {
+        src = s2;
+        srow = r - 4 * c;
+      }
+    } else if (mode == 1) {
+      const int64_t n = c_or_n;
+      const int64_t t = r / 128, w = r % 128;
+      src = s0;
+      srow = (w < 64) ? 64 * t + w : n + 64 * t + (w - 64);
+    } else {
+      const int64_t c = c_or_n;
+      const int64_t which = r / c;
+      src = which == 0 ? s0 : which == 1 ? s1 : which == 2 ? s2 : s3;
+      srow = r - which * c;
+    }
+    const int64_t off = srow * k + col;
+    const float v = src_f32 ? reinterpret_cast<const float*>(src)[off]
+                            : __bfloat162float(reinterpret_cast<const bf16*>(src)[off]);
+    dst[idx] = __float2bfloat16_rn(v);
+  }
+}
+
+int launch_pack(const void* s0, const void* s1, const void* s2, const void* s3, int w_dtype,
+                int mode, int64_t c_or_n, int64_t k, int64_t rows, void* dst, cudaStream_t st) {
+  XFB_REQUIRE(w_dtype == XFB_F32 || w_dtype == XFB_BF16, "weights must be f32 or bf16");
+  const int64_t total = rows * k;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  pack_weights_kernel<<<blocks, 256, 0, st>>>(s0, s1, s2, s3, w_dtype == XFB_F32, mode, c_or_n,
+                                              k, rows, static_cast<bf16*>(dst));
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+// Head-wise repack (and optional scale) of [BH][n][d] into [BH][n][dp] with zero padding.
+__global__ void repack_heads_kernel(const bf16* src, int64_t bh_n, int d, int dp, float scale,
+                                    int do_scale, bf16* dst) {
+  const int64_t total = bh_n * dp;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / dp;
+    const int e = static_cast<int>(idx - r * dp);
+    float v = 0.f;
+    if (e < d) {
+      v = __bfloat162float(src[r * d + e]);
+      if (do_scale) v = xfb::bf16r(v * scale);
+    }
+    dst[idx] = __float2bfloat16_rn(v);
+  }
+}
+
+// ------------------------------------------------------------------ workspace carving
+
+struct Carver {
+  uint8_t* base;
+  int64_t used = 0;
+  int64_t cap;
+  template <typename T>
+  T* take(int64_t count) {
+    used = round_up(used, 256);
+    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+    used += count * static_cast<int64_t>(sizeof(T));
+    return p;
+  }
+};
+
+int check_workspace(const Carver& cv, const void* ws, int64_t ws_bytes) {
+  if (cv.used > ws_bytes) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "workspace too small: need %lld bytes, got %lld",
+             (long long)cv.used, (long long)ws_bytes);
+    return fail(XFB_ERR_INVALID, buf);
+  }
+  if (cv.used > 0 && (reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return fail(XFB_ERR_INVALID, "workspace must be 256-byte aligned");
+  return XFB_OK;
+}
+
+// ------------------------------------------------------------------ attention launcher
+
+template <int DP, int BMODE>
+int launch_flash(const bf16* q, const bf16* k, const bf16* v, const xfb::AttnArgs& args,
+                 cudaStream_t st) {
+  CUtensorMap tq, tk, tv, tb;
+  const CUtensorMapSwizzle swz = DP == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  const int64_t bh = static_cast<int64_t>(args.B) * args.H;
+  XFB_TRY(make_map(&tq, q, DP, args.nq, bh, DP * 2, int64_t(args.nq) * DP * 2, DP, 128, swz));
+  XFB_TRY(make_map(&tk, k, DP, args.nk, bh, DP * 2, int64_t(args.nk) * DP * 2, DP, 128, swz));
+  XFB_TRY(make_map(&tv, v, DP, args.nk, bh, DP * 2, int64_t(args.nk) * DP * 2, DP, 128, swz));
+  if (BMODE == xfb::kBiasTma) {
+    const int64_t z = args.bias_batched ? bh : args.H;
+    XFB_TRY(make_map(&tb, args.bias, args.nk, args.nq, z, args.bias_sq * 2, args.bias_sh * 2, 64,
+                     128, CU_TENSOR_MAP_SWIZZLE_128B));
+  } else {
+    memset(&tb, 0, sizeof(tb));
+  }
+  using L = xfb::AttnSmem<DP>;
+  auto kernel = xfb::flash_attn_kernel<DP, BMODE>;
+  XFB_TRY(set_smem(kernel, L::kLaunchBytes));
+  dim3 grid(static_cast<unsigned>((args.nq + 127) / 128), static_cast<unsigned>(bh));
+  kernel<<<grid, xfb::kAttnThreads, L::kLaunchBytes, st>>>(tq, tk, tv, tb, args);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+// Picks the bias path: TMA-streamed bf16 tiles when the layout allows it
+// (row stride nk with nk % 8 == 0, contiguous heads, 16-byte aligned), else
+// per-thread global loads.
+int run_flash(int dp, int bias_dtype, const bf16* q, const bf16* k, const bf16* v,
+              const xfb::AttnArgs& args, cudaStream_t st) {
+  XFB_REQUIRE(args.nk <= xfb::AttnSmem<32>::kMaxKeys, "attention supports at most 8192 keys");
+  XFB_REQUIRE(static_cast<int64_t>(args.B) * args.H <= 65535, "attention batch*heads too large");
+  int mode = xfb::kBiasGlobalBf16;
+  if (args.bias != nullptr) {
+    if (bias_dtype == XFB_F32) {
+      mode = xfb::kBiasGlobalF32;
+    } else if (args.bias_sq == args.nk && args.nk % 8 == 0 && aligned16(args.bias) &&
+               (args.bias_sh * 2) % 16 == 0 &&
+               (!args.bias_batched || args.bias_sb == args.H * args.bias_sh)) {
+      mode = xfb::kBiasTma;
+    }
+  }
+  if (dp == 32) {
+    if (mode == xfb::kBiasTma) return launch_flash<32, xfb::kBiasTma>(q, k, v, args, st);
+    if (mode == xfb::kBiasGlobalF32) return launch_flash<32, xfb::kBiasGlobalF32>(q, k, v, args, st);
+    return launch_flash<32, xfb::kBiasGlobalBf16>(q, k, v, args, st);
+  }
+  if (mode == xfb::kBiasTma) return launch_flash<64, xfb::kBiasTma>(q, k, v, args, st);
+  if (mode == xfb::kBiasGlobalF32) return launch_flash<64, xfb::kBiasGlobalF32>(q, k, v, args, st);
+  return launch_flash<64, xfb::kBiasGlobalBf16>(q, k, v, args, st);
+}
+
+int head_pitch(int64_t d) { return d <= 32 ? 32 : 64; }
+
+}  // namespace
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+XFB_API const char* xfb_last_error(void) { return g_last_error.c_str(); }
+
+XFB_API uint64_t xfb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+XFB_API int xfb_runtime_info(char* buf, int64_t buf_len) {
+  int dev = -1, sms = 0, major = 0, minor = 0, rt = 0, drv = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  }
+  cudaRuntimeGetVersion(&rt);
+  cudaDriverGetVersion(&drv);
+  cudaGetLastError();
+  char tmp[1024];
+  snprintf(tmp, sizeof(tmp),
+           "{\"library\": \"xfold_b200\", \"target\": \"sm_100a\", \"device\": %d, "
+           "\"compute_capability\": \"%d.%d\", \"sm_count\": %d, \"cuda_runtime\": %d, "
+           "\"cuda_driver\": %d, \"nvcc_flags\": \"%s\"}",
+           dev, major, minor, sms, rt, drv, XFB_NVCC_FLAGS);
+  if (buf == nullptr || buf_len <= 0) return fail(XFB_ERR_INVALID, "buffer required");
+  snprintf(buf, static_cast<size_t>(buf_len), "%s", tmp);
+  return XFB_OK;
+}
+
+XFB_API int xfb_check_device(void) {
+  int dev;
+  XFB_TRY(current_device(&dev));
+  int major = 0, minor = 0;
+  XFB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  XFB_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+  if (major != 10 || minor != 0) {
+    char buf[128];
+    snprintf(buf, sizeof(buf), "device %d has compute capability %d.%d; sm_100 (B200) required",
+             dev, major, minor);
+    return fail(XFB_ERR_DEVICE, buf);
+  }
+  cudaFuncAttributes attr;
+  XFB_CUDA(cudaFuncGetAttributes(&attr, xfb::flash_attn_kernel<32, xfb::kBiasTma>));
+  XFB_TRY(get_encoder());
+  return XFB_OK;
+}
+
+XFB_API int xfb_device_error(int clear, uint32_t* code) {
+  unsigned int v = 0;
+  XFB_CUDA(cudaMemcpyFromSymbol(&v, xfb_dev_error, sizeof(v)));
+  if (code) *code = v;
+  if (clear) {
+    unsigned int zero = 0;
+    XFB_CUDA(cudaMemcpyToSymbol(xfb_dev_error, &zero, sizeof(zero)));
+  }
+  return XFB_OK;
+}
+
+}  // extern "C"
+
+namespace {
+__global__ void wait_timeout_selftest_kernel(int64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    xfb::mbar_init(&bar, 1);
+    xfb::fence_mbar_init();
+    const uint32_t addr = xfb::smem_u32(&bar);
+    const uint64_t start = xfb::global_ns();
+    // Nothing ever arrives on `bar`: the wait must give up on its own.
+    while (!xfb::mbar_try_wait(addr, 0)) {
+      if (xfb::global_ns() - start > static_cast<uint64_t>(timeout_ns)) {
+        xfb::record_error(xfb::kErrWaitTest);
+        break;
+      }
+    }
+  }
+}
+}  // namespace
+
+extern "C" {
+
+XFB_API int xfb_selftest_wait_timeout(int64_t timeout_ns, void* stream) {
+  XFB_REQUIRE(timeout_ns > 0 && timeout_ns <= 5000000000ll, "timeout must be in (0, 5 s]");
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+// ---------------------------------------------------------------- primitives
+
+XFB_API int xfb_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                           const float* weight, const float* bias, double eps, void* y,
+                           void* stream) {
+  XFB_REQUIRE(rows >= 0, "rows must be non-negative");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  return run_layer_norm(x, x_dtype, rows, cols, cols, weight, bias, eps, static_cast<bf16*>(y),
+                        cols, nullptr, nullptr, nullptr, 0, nullptr, 0,
+                        static_cast<cudaStream_t>(stream));
+}
+
+XFB_API int xfb_linear(const void* x, int64_t m, int64_t k, const void* weight, int64_t n,
+                       const float* bias, void* y, int y_dtype, int accumulate, void* stream) {
+  XFB_REQUIRE(m >= 0 && k > 0 && n > 0, "linear expects m >= 0, k > 0, n > 0");
+  XFB_REQUIRE(k % 8 == 0 && n % 8 == 0, "linear requires k and n to be multiples of 8");
+  XFB_REQUIRE(y_dtype == XFB_F32 || y_dtype == XFB_BF16, "linear output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || y_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(aligned16(y), "linear output must be 16-byte aligned");
+  return linear_core(static_cast<const bf16*>(x), m, k, k, static_cast<const bf16*>(weight), n,
+                     bias, nullptr, 0, y, y_dtype == XFB_F32, accumulate, n,
+                     static_cast<cudaStream_t>(stream));
+}
+
+XFB_API int64_t xfb_pack_glu_weight_bytes(int64_t n, int64_t k) { return 2 * n * k * 2; }
+
+XFB_API int xfb_pack_glu_weight(const void* weight, int w_dtype, int64_t n, int64_t k,
+                                void* packed, void* stream) {
+  XFB_REQUIRE(n > 0 && n % 64 == 0, "GLU hidden width must be a positive multiple of 64");
+  return launch_pack(weight, nullptr, nullptr, nullptr, w_dtype, 1, n, k, 2 * n, packed,
+                     static_cast<cudaStream_t>(stream));
+}
+
+XFB_API int64_t xfb_gated_linear_unit_workspace(int64_t m, int64_t k, int64_t n) {
+  (void)m;
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(2 * n * k);
+  return cv.used;
+}
+
+XFB_API int xfb_gated_linear_unit(const void* x, int64_t m, int64_t k, const void* weight,
+                                  int64_t n, int weights_packed, void* y, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(m >= 0 && k > 0, "GLU expects m >= 0 and k > 0");
+  XFB_REQUIRE(n > 0 && n % 64 == 0, "GLU hidden width must be a positive multiple of 64");
+  XFB_REQUIRE(k % 8 == 0, "GLU input width must be a multiple of 8");
+  XFB_REQUIRE(aligned16(y), "GLU output must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bf16* w = static_cast<const bf16*>(weight);
+  if (!weights_packed) {
+    Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+    bf16* pk = cv.take<bf16>(2 * n * k);
+    XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+    XFB_TRY(launch_pack(weight, nullptr, nullptr, nullptr, XFB_BF16, 1, n, k, 2 * n, pk, st));
+    w = pk;
+  }
+  xfb::EpiGLU<128> epi;
+  epi.out = static_cast<bf16*>(y);
+  epi.ld_out = n;
+  epi.M = static_cast<int>(m);
+  epi.N_out = static_cast<int>(n);
+  return run_gemm<128, 6, false, false>(x, k, 0, w, k, 0, m, 2 * n, k, 1, epi, st);
+}
+
+XFB_API int xfb_gemm(const void* a, const void* b, void* c, int64_t batch, int64_t m, int64_t n,
+                     int64_t k, int a_mn_major, int b_mn_major, int c_dtype, void* stream) {
+  XFB_REQUIRE(batch >= 0 && m >= 0 && n >= 0 && k > 0, "gemm expects batch, m, n >= 0, k > 0");
+  XFB_REQUIRE(c_dtype == XFB_F32 || c_dtype == XFB_BF16, "gemm output must be f32 or bf16");
+  XFB_REQUIRE(aligned16(c), "gemm output must be 16-byte aligned");
+  const int64_t lda = a_mn_major ? m : k;
+  const int64_t ldb = b_mn_major ? n : k;
+  XFB_REQUIRE(lda % 8 == 0 && ldb % 8 == 0, "gemm leading dimensions must be multiples of 8");
+  XFB_REQUIRE(c_dtype == XFB_F32 ? n % 4 == 0 : n % 8 == 0, "gemm output rows must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  xfb::EpiLinear<256> epi;
+  epi.out = c;
+  epi.ld_out = n;
+  epi.bstride_out = m * n;
+  epi.out_f32 = c_dtype == XFB_F32;
+  epi.accumulate = 0;
+  epi.bias = nullptr;
+  epi.gate = nullptr;
+  epi.ld_gate = 0;
+  epi.M = static_cast<int>(m);
+  epi.N = static_cast<int>(n);
+  const int64_t a_bs = m * k, b_bs = n * k;
+  if (!a_mn_major && !b_mn_major)
+    return run_gemm<256, 4, false, false>(a, lda, a_bs, b, ldb, b_bs, m, n, k, batch, epi, st);
+  if (a_mn_major && b_mn_major)
+    return run_gemm<256, 4, true, true>(a, lda, a_bs, b, ldb, b_bs, m, n, k, batch, epi, st);
+  return fail(XFB_ERR_INVALID, "gemm supports both operands K-major or both MN-major");
+}
+
+// ---------------------------------------------------------------- triangle multiplication
+
+XFB_API int64_t xfb_pack_triangle_weights_bytes(int64_t c) { return (5 * c) * c * 2; }
+
+XFB_API int xfb_pack_triangle_weights(const void* projection, const void* gate,
+                                      const void* gating_linear, int w_dtype, int64_t c,
+                                      void* packed, void* stream) {
+  XFB_REQUIRE(c == 64 || c == 128, "triangle multiplication supports c in {64, 128}");
+  return launch_pack(projection, gate, gating_linear, nullptr, w_dtype, 0, c, c, 5 * c, packed,
+                     static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+struct TriWs {
+  bf16 *x, *a, *b, *g, *z, *packed;
+};
+void tri_layout(Carver& cv, int64_t n, int64_t c, bool need_pack, TriWs* w) {
+  const int64_t pitch = pad_pitch(n);
+  w->x = cv.take<bf16>(n * n * c);
+  w->a = cv.take<bf16>(c * n * pitch);
+  w->b = cv.take<bf16>(c * n * pitch);
+  w->z = cv.take<bf16>(c * n * pitch);
+  w->g = cv.take<bf16>(n * n * c);
+  w->packed = need_pack ? cv.take<bf16>(5 * c * c) : nullptr;
+}
+}  // namespace
+
+XFB_API int64_t xfb_triangle_multiplication_workspace(int64_t n, int64_t c) {
+  Carver cv{nullptr, 0, 0};
+  TriWs w;
+  tri_layout(cv, n, c, true, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_triangle_multiplication(
+    const void* pair, int pair_dtype, int64_t n, int64_t c, const float* mask, int outgoing,
+    const float* left_weight, const float* left_bias, const void* projection, const void* gate,
+    const float* center_weight, const float* center_bias, const void* output_weight,
+    const void* gating_weight, double left_eps, double center_eps, int weights_packed,
+    const void* packed, void* out, int out_dtype, int accumulate, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(n >= 0, "pair side must be non-negative");
+  XFB_REQUIRE(c == 64 || c == 128, "triangle multiplication supports c in {64, 128}");
+  XFB_REQUIRE(std::isfinite(left_eps) && left_eps >= 0 && std::isfinite(center_eps) &&
+                  center_eps >= 0,
+              "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(output_weight != nullptr, "output_weight is required");
+  XFB_REQUIRE(weights_packed ? packed != nullptr
+                             : (projection && gate && gating_weight),
+              "triangle weights missing");
+  if (n == 0) return XFB_OK;
+  XFB_REQUIRE(n * n <= (1ll << 31) - 256, "pair too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  TriWs w;
+  tri_layout(cv, n, c, !weights_packed, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t pitch = pad_pitch(n);
+  const int64_t M = n * n;
+  const bf16* wcat = static_cast<const bf16*>(packed);
+  if (!weights_packed) {
+    XFB_TRY(launch_pack(projection, gate, gating_weight, nullptr, XFB_BF16, 0, c, c, 5 * c,
+                        w.packed, st));
+    wcat = w.packed;
+  }
+  // 1. x = LN(pair)
+  XFB_TRY(run_layer_norm(pair, pair_dtype, M, c, c, left_weight, left_bias, left_eps, w.x, c,
+                         nullptr, nullptr, nullptr, 0, nullptr, 0, st));
+  // 2. fused projection ‖ gate ‖ output gate -> a, b (channel-major), g
+  {
+    xfb::EpiTriProj epi;
+    epi.a = w.a;
+    epi.b = w.b;
+    epi.g = w.g;
+    epi.mask = mask;
+    epi.chan_stride = n * pitch;
+    epi.n = static_cast<int>(n);
+    epi.pitch = static_cast<int>(pitch);
+    epi.c = static_cast<int>(c);
+    epi.M = static_cast<int>(M);
+    epi.n_proj_tiles = static_cast<int>(2 * c / 64);
+    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, wcat, c, 0, M, 5 * c, c, 1, epi, st)));
+  }
+  // 3. per-channel contraction z[ch] = a[ch] b[ch]^T (outgoing) or b[ch]^T a[ch] (incoming)
+  {
+    xfb::EpiLinear<256> epi;
+    epi.out = w.z;
+    epi.ld_out = pitch;
+    epi.bstride_out = n * pitch;
+    epi.out_f32 = 0;
+    epi.accumulate = 0;
+    epi.bias = nullptr;
+    epi.gate = nullptr;
+    epi.ld_gate = 0;
+    epi.M = static_cast<int>(n);
+    epi.N = static_cast<int>(n);
+    if (outgoing) {
+      XFB_TRY((run_gemm<256, 4, false, false>(w.a, pitch, n * pitch, w.b, pitch, n * pitch, n, n,
+                                              n, c, epi, st)));
+    } else {
+      XFB_TRY((run_gemm<256, 4, true, true>(w.b, pitch, n * pitch, w.a, pitch, n * pitch, n, n,
+                                            n, c, epi, st)));
+    }
+  }
+  // 4. centre LayerNorm over channels (channel-major in, row-major out; x is reused)
+  {
+    int sms;
+    XFB_TRY(sm_count(&sms));
+    const int blocks = static_cast<int>(std::min<int64_t>((M + 127) / 128, int64_t(sms) * 8));
+    if (c == 128) {
+      xfb::ln_channel_major_kernel<128><<<blocks, 128, 0, st>>>(
+          w.z, static_cast<int>(n), static_cast<int>(pitch), n * pitch, center_weight,
+          center_bias, static_cast<float>(center_eps), w.x);
+    } else {
+      xfb::ln_channel_major_kernel<64><<<blocks, 128, 0, st>>>(
+          w.z, static_cast<int>(n), static_cast<int>(pitch), n * pitch, center_weight,
+          center_bias, static_cast<float>(center_eps), w.x);
+    }
+    XFB_LAUNCHED();
+  }
+  // 5. update = (LN_c(z) W_o^T) * g  -> out (or pair += update)
+  XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
+  return linear_core(w.x, M, c, c, static_cast<const bf16*>(output_weight), c, nullptr, w.g, c,
+                     out, out_dtype == XFB_F32, accumulate, c, st);
+}
+
+// ---------------------------------------------------------------- attention
+
+XFB_API int64_t xfb_dot_product_attention_workspace(int64_t B, int64_t H, int64_t nq, int64_t nk,
+                                                    int64_t d) {
+  const int64_t dp = head_pitch(d);
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(B * H * nq * dp);
+  cv.take<bf16>(B * H * nk * dp);
+  cv.take<bf16>(B * H * nk * dp);
+  return cv.used;
+}
+
+XFB_API int xfb_dot_product_attention(const void* q, const void* k, const void* v, int64_t B,
+                                      int64_t H, int64_t nq, int64_t nk, int64_t d,
+                                      const void* mask, int mask_dtype, int mask_batched,
+                                      const void* bias, int bias_dtype, int bias_batched,
+                                      int q_pre_scaled, void* out, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(B >= 0 && H >= 0 && nq >= 0 && nk >= 0, "attention sizes must be non-negative");
+  XFB_REQUIRE(d > 0 && d <= 64, "attention head dimension must be in [1, 64]");
+  XFB_REQUIRE(mask == nullptr || mask_dtype == XFB_F32 || mask_dtype == XFB_U8,
+              "attention mask must be f32 or uint8/bool");
+  XFB_REQUIRE(bias == nullptr || bias_dtype == XFB_F32 || bias_dtype == XFB_BF16,
+              "attention bias must be f32 or bf16");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || H == 0 || nq == 0) return XFB_OK;
+  if (nk == 0) {
+    // Empty key set: the reference returns zeros (dot_product_attention.cpp:263-266).
+    XFB_CUDA(cudaMemsetAsync(out, 0, B * H * nq * d * sizeof(bf16), st));
+    return XFB_OK;
+  }
+  const int dp = head_pitch(d);
+  const float scale = 1.f / std::sqrt(static_cast<float>(d));
+  const bf16* qq = static_cast<const bf16*>(q);
+  const bf16* kk = static_cast<const bf16*>(k);
+  const bf16* vv = static_cast<const bf16*>(v);
+  const bool direct = (d == dp) && q_pre_scaled && aligned16(q) && aligned16(k) && aligned16(v);
+  if (!direct) {
+    Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+    bf16* q2 = cv.take<bf16>(B * H * nq * dp);
+    bf16* k2 = cv.take<bf16>(B * H * nk * dp);
+    bf16* v2 = cv.take<bf16>(B * H * nk * dp);
+    XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+    const int blocks = 2048;
+    repack_heads_kernel<<<blocks, 256, 0, st>>>(qq, B * H * nq, static_cast<int>(d), dp, scale,
+                                                q_pre_scaled ? 0 : 1, q2);
+    repack_heads_kernel<<<blocks, 256, 0, st>>>(kk, B * H * nk, static_cast<int>(d), dp, 1.f, 0,
+                                                k2);
+    repack_heads_kernel<<<blocks, 256, 0, st>>>(vv, B * H * nk, static_cast<int>(d), dp, 1.f, 0,
+                                                v2);
+    g_launches.fetch_add(2, std::memory_order_relaxed);  // q and k repacks
+    XFB_LAUNCHED();
+    qq = q2;
+    kk = k2;
+    vv = v2;
+  }
+  xfb::AttnArgs a;
+  a.B = static_cast<int>(B);
+  a.H = static_cast<int>(H);
+  a.nq = static_cast<int>(nq);
+  a.nk = static_cast<int>(nk);
+  a.d = static_cast<int>(d);
+  a.mask = mask;
+  a.mask_is_float = mask_dtype == XFB_F32;
+  a.mask_sb = mask_batched ? nk : 0;
+  a.bias = bias;
+  a.bias_sb = bias_batched ? H * nq * nk : 0;
+  a.bias_sh = nq * nk;
+  a.bias_sq = nk;
+  a.out = static_cast<bf16*>(out);
+  a.out_sb = H * nq * d;
+  a.out_sh = nq * d;
+  a.out_sq = d;
+  a.gate = nullptr;
+  a.gate_sb = a.gate_sh = a.gate_sq = 0;
+  a.bias_batched = bias_batched;
+  return run_flash(dp, bias_dtype, qq, kk, vv, a, st);
+}
+
+XFB_API int64_t xfb_pack_attention_weights_bytes(int64_t c) { return 4 * c * c * 2; }
+
+XFB_API int xfb_pack_attention_weights(const void* q_w, const void* k_w, const void* v_w,
+                                       const void* gate_w, int w_dtype, int64_t c,
+                                       void* packed, void* stream) {
+  XFB_REQUIRE(c > 0 && c % 8 == 0, "attention width must be a positive multiple of 8");
+  return launch_pack(q_w, k_w, v_w, gate_w, w_dtype, 2, c, c, 4 * c, packed,
+                     static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+struct GsaWs {
+  bf16 *x, *bias, *q, *k, *v, *g, *packed;
+};
+void gsa_layout(Carver& cv, int64_t n, int64_t c, int64_t heads, bool need_pack, GsaWs* w) {
+  const int64_t dp = head_pitch(c / heads);
+  w->x = cv.take<bf16>(n * n * c);
+  w->bias = cv.take<bf16>(heads * n * n);
+  w->q = cv.take<bf16>(n * heads * n * dp);
+  w->k = cv.take<bf16>(n * heads * n * dp);
+  w->v = cv.take<bf16>(n * heads * n * dp);
+  w->g = cv.take<bf16>(n * n * c);
+  w->packed = need_pack ? cv.take<bf16>(4 * c * c) : nullptr;
+}
+}  // namespace
+
+XFB_API int64_t xfb_grid_self_attention_workspace(int64_t n, int64_t c, int64_t heads) {
+  if (heads <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  GsaWs w;
+  gsa_layout(cv, n, c, heads, true, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_grid_self_attention(
+    const void* pair, int pair_dtype, int64_t n, int64_t c, int64_t heads, const float* mask,
+    int transpose, const float* norm_weight, const float* norm_bias, double eps,
+    const void* bias_weight, const void* q_w, const void* k_w, const void* v_w,
+    const void* gate_w, const void* output_w, int weights_packed, const void* packed,
+    void* out, int out_dtype, int accumulate, void* workspace, int64_t workspace_bytes,
+    void* stream) {
+  XFB_REQUIRE(n >= 0, "pair side must be non-negative");
+  XFB_REQUIRE(c == 64 || c == 128, "grid self-attention supports c in {64, 128}");
+  XFB_REQUIRE(heads > 0 && heads <= 16 && c % heads == 0, "heads must divide c (<= 16)");
+  const int64_t d = c / heads;
+  XFB_REQUIRE(d == 16 || d == 32, "grid self-attention head dim must be 16 or 32");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(bias_weight != nullptr && output_w != nullptr, "attention weights missing");
+  XFB_REQUIRE(weights_packed ? packed != nullptr : (q_w && k_w && v_w && gate_w),
+              "attention weights missing");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  if (n == 0) return XFB_OK;
+  XFB_REQUIRE(n <= 16384 && n * n <= (1ll << 31) - 256, "pair too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  GsaWs w;
+  gsa_layout(cv, n, c, heads, !weights_packed, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int dp = head_pitch(d);
+  const int64_t M = n * n;
+  const bf16* wcat = static_cast<const bf16*>(packed);
+  if (!weights_packed) {
+    XFB_TRY(launch_pack(q_w, k_w, v_w, gate_w, XFB_BF16, 2, c, c, 4 * c, w.packed, st));
+    wcat = w.packed;
+  }
+  // 1. x = LN(pair) and the pair bias (projected before any transpose)
+  XFB_TRY(run_layer_norm(pair, pair_dtype, M, c, c, norm_weight, norm_bias, eps, w.x, c, nullptr,
+                         nullptr, static_cast<const bf16*>(bias_weight),
+                         static_cast<int>(heads), w.bias, M, st));
+  // 2. q, k, v (head-major per batch row) and the squashed gate
+  if (d != dp) {
+    const int64_t bytes = n * heads * n * dp * 2;
+    XFB_CUDA(cudaMemsetAsync(w.q, 0, bytes, st));
+    XFB_CUDA(cudaMemsetAsync(w.k, 0, bytes, st));
+    XFB_CUDA(cudaMemsetAsync(w.v, 0, bytes, st));
+  }
+  {
+    xfb::EpiAttProj epi;
+    epi.q = w.q;
+    epi.k = w.k;
+    epi.v = w.v;
+    epi.g = w.g;
+    epi.n = static_cast<int>(n);
+    epi.c = static_cast<int>(c);
+    epi.heads = static_cast<int>(heads);
+    epi.d = static_cast<int>(d);
+    epi.dp = dp;
+    epi.transpose = transpose;
+    epi.M = static_cast<int>(M);
+    epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
+    epi.q_bias = nullptr;
+    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, wcat, c, 0, M, 4 * c, c, 1, epi, st)));
+  }
+  // 3. attention per batch row; output written back in pair order, gated (x reused)
+  {
+    xfb::AttnArgs a;
+    a.B = static_cast<int>(n);
+    a.H = static_cast<int>(heads);
+    a.nq = static_cast<int>(n);
+    a.nk = static_cast<int>(n);
+    a.d = static_cast<int>(d);
+    a.mask = mask;
+    a.mask_is_float = 1;
+    a.mask_sb = n;
+    a.bias = w.bias;
+    a.bias_sb = 0;
+    a.bias_sh = M;
+    a.bias_sq = n;
+    a.bias_batched = 0;
+    a.out = w.x;
+    a.gate = w.g;
+    if (!transpose) {  // batch row r = pair row i, token = column j
+      a.out_sb = n * c;
+      a.out_sq = c;
+    } else {  // batch row r = pair column j, token = row i
+      a.out_sb = c;
+      a.out_sq = n * c;
+    }
+    a.out_sh = d;
+    a.gate_sb = a.out_sb;
+    a.gate_sh = a.out_sh;
+    a.gate_sq = a.out_sq;
+    XFB_TRY(run_flash(dp, XFB_BF16, w.q, w.k, w.v, a, st));
+  }
+  // 4. output projection (+ residual)
+  XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
+  return linear_core(w.x, M, c, c, static_cast<const bf16*>(output_w), c, nullptr, nullptr, 0,
+                     out, out_dtype == XFB_F32, accumulate, c, st);
+}
+
+// ---------------------------------------------------------------- transition
+
+namespace {
+struct TrWs {
+  bf16 *x, *h, *packed;
+};
+void tr_layout(Carver& cv, int64_t rows, int64_t c, int64_t f, bool need_pack, TrWs* w) {
+  w->x = cv.take<bf16>(rows * c);
+  w->h = cv.take<bf16>(rows * f * c);
+  w->packed = need_pack ? cv.take<bf16>(2 * f * c * c) : nullptr;
+}
+}  // namespace
+
+XFB_API int64_t xfb_transition_workspace(int64_t rows, int64_t c, int64_t factor) {
+  Carver cv{nullptr, 0, 0};
+  TrWs w;
+  tr_layout(cv, rows, c, factor, true, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_transition(const void* x, int x_dtype, int64_t rows, int64_t c,
+                           int64_t factor, const float* norm_weight, const float* norm_bias,
+                           double eps, const void* mod_scale, const void* mod_shift,
+                           const void* w1, int weights_packed, const void* w2,
+                           const void* out_gate, void* out, int out_dtype, int accumulate,
+                           void* workspace, int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(rows >= 0 && factor > 0, "transition expects rows >= 0 and factor > 0");
+  XFB_REQUIRE(c == 64 || c == 128 || c == 384 || c == 768, "transition width must be 64/128/384/768");
+  XFB_REQUIRE((factor * c) % 64 == 0, "transition hidden width must be a multiple of 64");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(w1 != nullptr && w2 != nullptr, "transition weights missing");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
+  if (rows == 0) return XFB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  TrWs w;
+  tr_layout(cv, rows, c, factor, !weights_packed, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t hid = factor * c;
+  const bf16* w1p = static_cast<const bf16*>(w1);
+  if (!weights_packed) {
+    XFB_TRY(launch_pack(w1, nullptr, nullptr, nullptr, XFB_BF16, 1, hid, c, 2 * hid, w.packed, st));
+    w1p = w.packed;
+  }
+  XFB_TRY(run_layer_norm(x, x_dtype, rows, c, c, norm_weight, norm_bias, eps, w.x, c,
+                         static_cast<const bf16*>(mod_scale), static_cast<const bf16*>(mod_shift),
+                         nullptr, 0, nullptr, 0, st));
+  {
+    xfb::EpiGLU<128> epi;
+    epi.out = w.h;
+    epi.ld_out = hid;
+    epi.M = static_cast<int>(rows);
+    epi.N_out = static_cast<int>(hid);
+    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, w1p, c, 0, rows, 2 * hid, c, 1, epi, st)));
+  }
+  return linear_core(w.h, rows, hid, hid, static_cast<const bf16*>(w2), c, nullptr,
+                     static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32,
+                     accumulate, c, st);
+}
+
+// ---------------------------------------------------------------- single attention
+
+namespace {
+struct SaWs {
+  bf16 *x, *q, *k, *v, *g, *packed;
+};
+void sa_layout(Carver& cv, int64_t n, int64_t c, int64_t heads, bool need_pack, SaWs* w) {
+  const int64_t dp = head_pitch(c / heads);
+  w->x = cv.take<bf16>(n * c);
+  w->q = cv.take<bf16>(heads * n * dp);
+  w->k = cv.take<bf16>(heads * n * dp);
+  w->v = cv.take<bf16>(heads * n * dp);
+  w->g = cv.take<bf16>(n * c);
+  w->packed = need_pack ? cv.take<bf16>(4 * c * c) : nullptr;
+}
+}  // namespace
+
+XFB_API int64_t xfb_self_attention_workspace(int64_t n, int64_t c, int64_t heads) {
+  if (heads <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  SaWs w;
+  sa_layout(cv, n, c, heads, true, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c, int64_t heads,
+                               const float* mask, const void* pair_logits,
+                               const float* norm_weight, const float* norm_bias, double eps,
+                               const void* mod_scale, const void* mod_shift, const void* q_w,
+                               const float* q_bias, const void* k_w, const void* v_w,
+                               const void* gate_w, int weights_packed, const void* packed,
+                               const void* wo, const void* out_gate, void* out, int out_dtype,
+                               int accumulate, void* workspace, int64_t workspace_bytes,
+                               void* stream) {
+  XFB_REQUIRE(n >= 0, "token count must be non-negative");
+  XFB_REQUIRE(c == 128 || c == 384 || c == 768, "self-attention width must be 128, 384 or 768");
+  XFB_REQUIRE(heads > 0 && c % heads == 0 && c / heads <= 64, "heads must divide c, d <= 64");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(wo != nullptr, "output projection weight missing");
+  XFB_REQUIRE(weights_packed ? packed != nullptr : (q_w && k_w && v_w && gate_w),
+              "attention weights missing");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
+  if (n == 0) return XFB_OK;
+  XFB_REQUIRE(n <= 16384, "self-attention supports at most 16384 tokens");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  SaWs w;
+  sa_layout(cv, n, c, heads, !weights_packed, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t d = c / heads;
+  const int dp = head_pitch(d);
+  const bf16* wcat = static_cast<const bf16*>(packed);
+  if (!weights_packed) {
+    XFB_TRY(launch_pack(q_w, k_w, v_w, gate_w, XFB_BF16, 2, c, c, 4 * c, w.packed, st));
+    wcat = w.packed;
+  }
+  XFB_TRY(run_layer_norm(x, x_dtype, n, c, c, norm_weight, norm_bias, eps, w.x, c,
+                         static_cast<const bf16*>(mod_scale), static_cast<const bf16*>(mod_shift),
+                         nullptr, 0, nullptr, 0, st));
+  if (d != dp) {
+    const int64_t bytes = heads * n * dp * 2;
+    XFB_CUDA(cudaMemsetAsync(w.q, 0, bytes, st));
+    XFB_CUDA(cudaMemsetAsync(w.k, 0, bytes, st));
+    XFB_CUDA(cudaMemsetAsync(w.v, 0, bytes, st));
+  }
+  {
+    xfb::EpiAttProj epi;
+    epi.q = w.q;
+    epi.k = w.k;
+    epi.v = w.v;
+    epi.g = w.g;
+    epi.n = static_cast<int>(n);
+    epi.c = static_cast<int>(c);
+    epi.heads = static_cast<int>(heads);
+    epi.d = static_cast<int>(d);
+    epi.dp = dp;
+    epi.transpose = 0;
+    epi.M = static_cast<int>(n);
+    epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
+    epi.q_bias = q_bias;
+    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, wcat, c, 0, n, 4 * c, c, 1, epi, st)));
+  }
+  {
+    xfb::AttnArgs a;
+    a.B = 1;
+    a.H = static_cast<int>(heads);
+    a.nq = static_cast<int>(n);
+    a.nk = static_cast<int>(n);
+    a.d = static_cast<int>(d);
+    a.mask = mask;
+    a.mask_is_float = 1;
+    a.mask_sb = 0;
+    a.bias = pair_logits;
+    a.bias_sb = 0;
+    a.bias_sh = n * n;
+    a.bias_sq = n;
+    a.bias_batched = 0;
+    a.out = w.x;
+    a.out_sb = 0;
+    a.out_sh = d;
+    a.out_sq = c;
+    a.gate = w.g;
+    a.gate_sb = 0;
+    a.gate_sh = d;
+    a.gate_sq = c;
+    XFB_TRY(run_flash(dp, XFB_BF16, w.q, w.k, w.v, a, st));
+  }
+  return linear_core(w.x, n, c, c, static_cast<const bf16*>(wo), c, nullptr,
+                     static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32,
+                     accumulate, c, st);
+}
+
+XFB_API int xfb_pair_logits(const void* pair, int pair_dtype, int64_t n, int64_t c,
+                            int64_t heads, const float* norm_weight, const float* norm_bias,
+                            double eps, const void* w, void* logits, void* stream) {
+  XFB_REQUIRE(n >= 0 && heads > 0 && heads <= 16, "pair logits expect 1..16 heads");
+  XFB_REQUIRE(c == 64 || c == 128, "pair width must be 64 or 128");
+  if (n == 0) return XFB_OK;
+  return run_layer_norm(pair, pair_dtype, n * n, c, c, norm_weight, norm_bias, eps, nullptr, 0,
+                        nullptr, nullptr, static_cast<const bf16*>(w), static_cast<int>(heads),
+                        static_cast<bf16*>(logits), n * n, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

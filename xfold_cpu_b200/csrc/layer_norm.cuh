@@ -1,0 +1,266 @@
+// LayerNorm kernels (HBM-bound, one pass over the input).
+//
+// ln_rows_kernel: one warp per row of C channels, vectorised 16-byte loads,
+//   f32 statistics (mean, then variance of the centred values) with warp
+//   shuffles.  Writes bf16 y = LN(x)*w + b, optionally followed by the
+//   adaptive modulation y = scale*y + shift, and optionally a small head
+//   projection heads[h][row] = sum_c y[c] * wh[h][c] (the pair-bias / pair-logit
+//   projections, H <= 16) reduced with a transposing butterfly.
+//
+// ln_channel_major_kernel: one thread per position of a channel-major
+//   [C][n][pitch] bf16 tensor (the triangle contraction output); writes the
+//   normalised row-major [n*n][C] bf16 tensor the output projection reads.
+#pragma once
+
+#include "common.cuh"
+
+namespace xfb {
+
+template <typename T>
+__device__ __forceinline__ void load_vec4(const T* p, float (&v)[4]);
+
+template <>
+__device__ __forceinline__ void load_vec4<float>(const float* p, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = a.z;
+  v[3] = a.w;
+}
+
+template <>
+__device__ __forceinline__ void load_vec4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 a = *reinterpret_cast<const uint2*>(p);
+  v[0] = __uint_as_float(a.x << 16);
+  v[1] = __uint_as_float(a.x & 0xFFFF0000u);
+  v[2] = __uint_as_float(a.y << 16);
+  v[3] = __uint_as_float(a.y & 0xFFFF0000u);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+struct LnArgs {
+  const void* x;
+  int64_t rows;
+  int64_t ldx;
+  const float* w;      // [C] or null (no affine)
+  const float* b;      // [C] or null
+  float eps;
+  __nv_bfloat16* y;    // [rows][ldy] or null
+  int64_t ldy;
+  const __nv_bfloat16* mod_scale;  // [rows][C] (already squashed) or null
+  const __nv_bfloat16* mod_shift;  // [rows][C] or null
+  const __nv_bfloat16* wh;         // head projection [H][C] or null
+  int heads;
+  __nv_bfloat16* head_out;         // [H][head_ld]
+  int64_t head_ld;
+};
+
+// C = 32 * 4 * R channels: each lane holds R groups of 4 consecutive channels.
+template <int C, typename InT, int HP>
+__global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
+  static_assert(C % 128 == 0 || C == 64, "C must be 64 or a multiple of 128");
+  constexpr int R = (C >= 128) ? C / 128 : 1;
+  constexpr int V = (C >= 128) ? 4 : 2;  // channels per group
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+
+  // Head projection weights for this lane's channels (loaded once per warp).
+  float whr[HP > 0 ? HP : 1][R][V];
+  if constexpr (HP > 0) {
+#pragma unroll
+    for (int h = 0; h < HP; ++h)
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          const int ch = r * 32 * V + lane * V + e;
+          whr[h][r][e] = (h < a.heads) ? __bfloat162float(a.wh[h * C + ch]) : 0.f;
+        }
+  }
+  float wv[R][V], bv[R][V];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const int ch = r * 32 * V + lane * V + e;
+      wv[r][e] = a.w ? a.w[ch] : 1.f;
+      bv[r][e] = a.b ? a.b[ch] : 0.f;
+    }
+
+  for (int64_t row = warp_id; row < a.rows; row += warps_total) {
+    const InT* xr = reinterpret_cast<const InT*>(a.x) + row * a.ldx;
+    float v[R][V];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int ch = r * 32 * V + lane * V;
+      if constexpr (V == 4) {
+        load_vec4<InT>(xr + ch, v[r]);
+      } else {
+        v[r][0] = static_cast<float>(xr[ch]);
+        v[r][1] = static_cast<float>(xr[ch + 1]);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int e = 0; e < V; ++e) s += v[r][e];
+    const float mean = warp_sum(s) * (1.f / C);
+    float ss = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const float dlt = v[r][e] - mean;
+        ss += dlt * dlt;
+      }
+    const float var = warp_sum(ss) * (1.f / C);
+    const float rstd = rsqrtf(var + a.eps);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int e = 0; e < V; ++e) v[r][e] = (v[r][e] - mean) * rstd * wv[r][e] + bv[r][e];
+
+    if (a.mod_scale != nullptr) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          const int64_t off = row * C + r * 32 * V + lane * V + e;
+          const float sc = __bfloat162float(a.mod_scale[off]);
+          const float sh = a.mod_shift ? __bfloat162float(a.mod_shift[off]) : 0.f;
+          v[r][e] = sc * v[r][e] + sh;
+        }
+    }
+    // bf16 rounding of the normalised activations (the GEMM input)
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int e = 0; e < V; ++e) v[r][e] = bf16r(v[r][e]);
+
+    if (a.y != nullptr) {
+      __nv_bfloat16* yr = a.y + row * a.ldy;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int ch = r * 32 * V + lane * V;
+        if constexpr (V == 4) {
+          uint2 w;
+          w.x = pack_bf16x2(v[r][0], v[r][1]);
+          w.y = pack_bf16x2(v[r][2], v[r][3]);
+          *reinterpret_cast<uint2*>(yr + ch) = w;
+        } else {
+          *reinterpret_cast<uint32_t*>(yr + ch) = pack_bf16x2(v[r][0], v[r][1]);
+        }
+      }
+    }
+
+    if constexpr (HP > 0) {
+      float p[HP];
+#pragma unroll
+      for (int h = 0; h < HP; ++h) {
+        float acc = 0.f;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int e = 0; e < V; ++e) acc = fmaf(v[r][e], whr[h][r][e], acc);
+        p[h] = acc;
+      }
+      // Transposing butterfly: after log2(HP) halving steps lane L holds head
+      // bits taken from lane bits 4, 3, ... ; the remaining steps sum the rest.
+      int off = 16;
+#pragma unroll
+      for (int w = HP / 2; w >= 1; w >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < w; ++i) {
+          const float send = upper ? p[i] : p[i + w];
+          const float keep = upper ? p[i + w] : p[i];
+          p[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+        off >>= 1;
+      }
+      float tot = p[0];
+      for (int o = off; o >= 1; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      // lane L now holds head index formed by its top log2(HP) bits (bit 4 first)
+      const int shift = 5 - __ffs(HP) + 1;  // number of low bits summed away
+      if ((lane & ((1 << shift) - 1)) == 0) {
+        const int hidx = lane >> shift;
+        if (hidx < a.heads) a.head_out[hidx * a.head_ld + row] = __float2bfloat16_rn(tot);
+      }
+    }
+  }
+}
+
+// Channel-major LayerNorm: x(ch, i, j) = in[ch*chan_stride + i*pitch + j].
+template <int C>
+__global__ void __launch_bounds__(128) ln_channel_major_kernel(
+    const __nv_bfloat16* in, int n, int pitch, int64_t chan_stride, const float* w,
+    const float* b, float eps, __nv_bfloat16* y) {
+  const int64_t total = static_cast<int64_t>(n) * n;
+  for (int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; pos < total;
+       pos += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(pos / n);
+    const int j = static_cast<int>(pos - static_cast<int64_t>(i) * n);
+    const __nv_bfloat16* src = in + static_cast<int64_t>(i) * pitch + j;
+    float v[C];
+    float s = 0.f;
+#pragma unroll
+    for (int ch = 0; ch < C; ++ch) {
+      v[ch] = __bfloat162float(src[ch * chan_stride]);
+      s += v[ch];
+    }
+    const float mean = s * (1.f / C);
+    float ss = 0.f;
+#pragma unroll
+    for (int ch = 0; ch < C; ++ch) {
+      const float d = v[ch] - mean;
+      ss += d * d;
+    }
+    const float rstd = rsqrtf(ss * (1.f / C) + eps);
+    __nv_bfloat16* dst = y + pos * C;
+#pragma unroll
+    for (int ch = 0; ch < C; ch += 8) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float wv = w ? w[ch + e] : 1.f;
+        const float bv = b ? b[ch + e] : 0.f;
+        o[e] = (v[ch + e] - mean) * rstd * wv + bv;
+      }
+      uint4 pk;
+      pk.x = pack_bf16x2(o[0], o[1]);
+      pk.y = pack_bf16x2(o[2], o[3]);
+      pk.z = pack_bf16x2(o[4], o[5]);
+      pk.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(dst + ch) = pk;
+    }
+  }
+}
+
+// Row gather used to pack weights: dst[r][:] = src[map(r)][:] (bf16), zero rows
+// where map(r) < 0.  `src_is_f32` selects the source element type.
+__global__ void pack_rows_kernel(const void* src, int src_is_f32, const int* map, int rows,
+                                 int k, __nv_bfloat16* dst) {
+  const int64_t total = static_cast<int64_t>(rows) * k;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(idx / k);
+    const int c = static_cast<int>(idx - static_cast<int64_t>(r) * k);
+    const int s = map[r];
+    float v = 0.f;
+    if (s >= 0) {
+      v = src_is_f32 ? reinterpret_cast<const float*>(src)[static_cast<int64_t>(s) * k + c]
+                     : __bfloat162float(
+                           reinterpret_cast<const __nv_bfloat16*>(src)[static_cast<int64_t>(s) * k + c]);
+    }
+    dst[idx] = __float2bfloat16_rn(v);
+  }
+}
+
+}  // namespace xfb

@@ -1,0 +1,397 @@
+"""Torch-facing wrappers of the C ABI, one per operator of af3_kernels._C.
+
+Mirrors af3_kernels/src/af3_kernels/__init__.py (lazy loader + wrappers) and
+the pybind signatures of af3_kernels/src/csrc/bindings.cpp:10-49, with CUDA
+tensors instead of CPU tensors:
+
+    triangle_multiplication, dot_product_attention, gated_linear_unit, linear,
+    layer_norm, runtime_info
+
+plus the fused module-level operators grid_self_attention, transition,
+self_attention and pair_logits.  Tensors must live on one sm_100 device;
+weights are bf16 in nn.Linear layout [out, in] (see prepare_weight).  Work is
+enqueued on torch's current stream; nothing synchronises.  Scratch comes from
+torch's caching allocator and is released when the call returns.
+
+Errors: shape / dtype problems raise ValueError (the reference raises
+RuntimeError from TORCH_CHECK for the same cases, ValueError from its Python
+bridges); CUDA failures raise RuntimeError.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _capi
+
+_DTYPE_CODE = {torch.float32: _capi.F32, torch.bfloat16: _capi.BF16, torch.uint8: _capi.U8,
+               torch.bool: _capi.U8}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError as error:
+        raise ValueError(f"unsupported dtype {t.dtype}") from error
+
+
+def _check_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("the cuda backend requires CUDA tensors")
+        if t.layout != torch.strided:
+            raise ValueError("the cuda backend requires strided tensors")
+        if torch.is_grad_enabled() and t.requires_grad:
+            raise RuntimeError("the cuda backend supports inference only; disable gradients")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError("all tensors must be on the same device")
+    if device is None:
+        raise ValueError("no tensor given")
+    return device
+
+
+def _contig(t: torch.Tensor | None, dtype: torch.dtype | None = None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    t = t.detach()
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    return t.contiguous()
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def runtime_info() -> dict:
+    """Build and device description (af3_kernels runtime_info, bindings.cpp:13-20)."""
+    return _capi.runtime_info()
+
+
+def check_device(device: torch.device | int | None = None) -> None:
+    """Preflight for the cuda backend: sm_100 device and loadable kernels."""
+    if not torch.cuda.is_available():
+        raise ValueError("the cuda backend requires a CUDA device")
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        _capi.call("xfb_check_device")
+
+
+def prepare_weight(weight: torch.Tensor) -> torch.Tensor:
+    """bf16 contiguous copy of an nn.Linear weight [out, in] (no transpose)."""
+    return _contig(weight, torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- primitives
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
+               eps: float = 1e-5) -> torch.Tensor:
+    """bf16 LayerNorm over the last dimension (f32 statistics)."""
+    device = _check_cuda(x, weight, bias)
+    x = _contig(x)
+    cols = x.shape[-1]
+    y = torch.empty(x.shape, dtype=torch.bfloat16, device=device)
+    w, b = _contig(weight, torch.float32), _contig(bias, torch.float32)
+    _capi.call("xfb_layer_norm", _ptr(x), _code(x), x.numel() // max(cols, 1), cols, _ptr(w),
+               _ptr(b), float(eps), _ptr(y), _stream(device))
+    return y
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """x[..., k] @ weight[n, k]^T (+ bias) with bf16 inputs and f32 accumulation."""
+    device = _check_cuda(x, weight, bias)
+    x = _contig(x, torch.bfloat16)
+    weight = prepare_weight(weight)
+    k = x.shape[-1]
+    n = weight.shape[0]
+    if weight.shape[1] != k:
+        raise ValueError("linear weight must be [out, in] with in == x.shape[-1]")
+    y = torch.empty((*x.shape[:-1], n), dtype=out_dtype, device=device)
+    b = _contig(bias, torch.float32)
+    _capi.call("xfb_linear", _ptr(x), x.numel() // k, k, _ptr(weight), n, _ptr(b), _ptr(y),
+               _code(y), 0, _stream(device))
+    return y
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, mn_major: bool = False,
+         out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Batched bf16 GEMM (af3_kernels gemm, bindings.cpp:26).
+
+    K-major (mn_major=False): a [B, m, k], b [B, n, k] -> a @ b^T.
+    MN-major (mn_major=True): a [B, k, m], b [B, k, n] -> a^T @ b."""
+    device = _check_cuda(a, b)
+    a, b = _contig(a, torch.bfloat16), _contig(b, torch.bfloat16)
+    if a.dim() != 3 or b.dim() != 3 or a.shape[0] != b.shape[0]:
+        raise ValueError("gemm expects batched 3-D operands")
+    batch = a.shape[0]
+    if mn_major:
+        k, m = a.shape[1:]
+        n = b.shape[2]
+        if b.shape[1] != k:
+            raise ValueError("gemm reduction dimensions differ")
+    else:
+        m, k = a.shape[1:]
+        n = b.shape[1]
+        if b.shape[2] != k:
+            raise ValueError("gemm reduction dimensions differ")
+    c = torch.empty((batch, m, n), dtype=out_dtype, device=device)
+    _capi.call("xfb_gemm", _ptr(a), _ptr(b), _ptr(c), batch, m, n, k, int(mn_major),
+               int(mn_major), _code(c), _stream(device))
+    return c
+
+
+def pack_glu_weight(weight: torch.Tensor) -> torch.Tensor:
+    """Packs transition1.weight [2n, k] for gated_linear_unit(weight_packed=True)."""
+    device = _check_cuda(weight)
+    weight = _contig(weight)
+    n2, k = weight.shape
+    packed = torch.empty((n2, k), dtype=torch.bfloat16, device=device)
+    _capi.call("xfb_pack_glu_weight", _ptr(weight), _code(weight), n2 // 2, k, _ptr(packed),
+               _stream(device))
+    return packed
+
+
+def gated_linear_unit(x: torch.Tensor, weight: torch.Tensor,
+                      weight_packed: bool = False) -> torch.Tensor:
+    """silu(x @ W[:n]^T) * (x @ W[n:]^T) for W = transition1.weight [2n, k]."""
+    device = _check_cuda(x, weight)
+    x = _contig(x, torch.bfloat16)
+    weight = weight if weight_packed else prepare_weight(weight)
+    k = x.shape[-1]
+    n = weight.shape[0] // 2
+    m = x.numel() // k
+    y = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=device)
+    ws = _workspace(0 if weight_packed else _capi.load().xfb_gated_linear_unit_workspace(m, k, n),
+                    device)
+    _capi.call("xfb_gated_linear_unit", _ptr(x), m, k, _ptr(weight), n, 1 if weight_packed else 0,
+               _ptr(y), _ptr(ws), ws.numel(), _stream(device))
+    return y
+
+
+# ----------------------------------------------------------------------------- triangle mult.
+
+def pack_triangle_weights(projection: torch.Tensor, gate: torch.Tensor,
+                          gating_linear: torch.Tensor) -> torch.Tensor:
+    device = _check_cuda(projection, gate, gating_linear)
+    c = projection.shape[1]
+    tensors = [_contig(t, torch.bfloat16) for t in (projection, gate, gating_linear)]
+    packed = torch.empty((5 * c, c), dtype=torch.bfloat16, device=device)
+    _capi.call("xfb_pack_triangle_weights", *(_ptr(t) for t in tensors), _capi.BF16, c,
+               _ptr(packed), _stream(device))
+    return packed
+
+
+def triangle_multiplication(pair: torch.Tensor, mask: torch.Tensor | None, outgoing: bool,
+                            left_weight: torch.Tensor, left_bias: torch.Tensor | None,
+                            projection: torch.Tensor | None, gate: torch.Tensor | None,
+                            center_weight: torch.Tensor, center_bias: torch.Tensor | None,
+                            output_weight: torch.Tensor, gating_weight: torch.Tensor | None,
+                            left_eps: float = 1e-5, center_eps: float = 1e-5,
+                            weights_packed: bool = False, packed: torch.Tensor | None = None,
+                            out: torch.Tensor | None = None, accumulate: bool = False,
+                            out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """TriangleMultiplication update (af3_kernels triangle_multiplication,
+    triangle_multiplication.cpp:6-73).  Returns the update, or adds it into
+    `out` (f32 [N, N, C]) when accumulate=True."""
+    device = _check_cuda(pair, mask, left_weight, output_weight)
+    if pair.dim() != 3 or pair.shape[0] != pair.shape[1]:
+        raise ValueError("Triangle input must be [N, N, C].")
+    n, _, c = pair.shape
+    pair = _contig(pair)
+    if mask is not None:
+        mask = _contig(mask.expand(n, n) if mask.dim() <= 2 else mask, torch.float32)
+    if weights_packed:
+        if packed is None:
+            raise ValueError("weights_packed=True needs the packed buffer")
+    else:
+        projection, gate, gating_weight = (prepare_weight(t) for t in (projection, gate, gating_weight))
+    output_weight = prepare_weight(output_weight)
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate=True needs an output tensor")
+        out = torch.empty((n, n, c), dtype=out_dtype, device=device)
+    lw, lb = _contig(left_weight, torch.float32), _contig(left_bias, torch.float32)
+    cw, cb = _contig(center_weight, torch.float32), _contig(center_bias, torch.float32)
+    ws = _workspace(_capi.load().xfb_triangle_multiplication_workspace(n, c), device)
+    _capi.call("xfb_triangle_multiplication", _ptr(pair), _code(pair), n, c, _ptr(mask),
+               1 if outgoing else 0, _ptr(lw), _ptr(lb), _ptr(projection), _ptr(gate), _ptr(cw),
+               _ptr(cb), _ptr(output_weight), _ptr(gating_weight),
+               float(left_eps), float(center_eps), 1 if weights_packed else 0, _ptr(packed),
+               _ptr(out), _code(out), 1 if accumulate else 0, _ptr(ws), ws.numel(),
+               _stream(device))
+    return out
+
+
+# ----------------------------------------------------------------------------- attention
+
+def dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                          mask: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+                          q_pre_scaled: bool = False) -> torch.Tensor:
+    """softmax(q k^T / sqrt(d) + bias, mask) v for q, k, v [B, H, Q/K, D] (af3_kernels
+    dot_product_attention, dot_product_attention.cpp:110-174).
+
+    mask: rank 1 [K] or rank 2 [B, K] (any dtype, nonzero = keep), or a bool
+    tensor broadcastable to [B, 1, 1, K].  bias: broadcastable to [B, H, Q, K]
+    with the B dimension either B or 1."""
+    device = _check_cuda(q, k, v, mask, bias)
+    for t in (q, k, v):
+        if t.dim() != 4:
+            raise ValueError("attention expects [B, H, Q/K, D] tensors")
+    B, H, nq, d = q.shape
+    nk = k.shape[2]
+    if k.shape != (B, H, nk, d) or v.shape[:3] != (B, H, nk) or v.shape[3] != d:
+        raise ValueError("attention q/k/v shapes do not match (d == dv required)")
+    q, k, v = (_contig(t, torch.bfloat16) for t in (q, k, v))
+    mask_t, mask_code, mask_batched = None, _capi.F32, 0
+    if mask is not None:
+        if mask.dim() == 1:
+            mask_t = _contig(mask, torch.float32 if mask.is_floating_point() else torch.uint8)
+        elif mask.dim() == 2:
+            mask_t = _contig(mask.expand(B, nk), torch.float32 if mask.is_floating_point()
+                             else torch.uint8)
+            mask_batched = 1
+        else:
+            if mask.dtype != torch.bool:
+                raise ValueError("Attention masks of rank 0/3/4 must be boolean, as in the "
+                                 "PyTorch path.")
+            m4 = mask.reshape((1,) * (4 - mask.dim()) + tuple(mask.shape)) if mask.dim() < 4 else mask
+            if m4.shape[1] != 1 or m4.shape[2] != 1:
+                raise ValueError("the cuda attention supports key masks broadcast over heads "
+                                 "and queries only")
+            mask_t = _contig(m4.expand(B, 1, 1, nk).reshape(B, nk), torch.uint8)
+            mask_batched = 1
+        mask_code = _code(mask_t)
+    bias_t, bias_batched = None, 0
+    if bias is not None:
+        b4 = bias.reshape((1,) * (4 - bias.dim()) + tuple(bias.shape)) if bias.dim() < 4 else bias
+        bias_batched = 1 if b4.shape[0] != 1 else 0
+        full = (B if bias_batched else 1, H, nq, nk)
+        b4 = b4.expand(full)
+        bias_t = _contig(b4, torch.bfloat16 if b4.dtype == torch.bfloat16 else torch.float32)
+    out = torch.empty((B, H, nq, d), dtype=torch.bfloat16, device=device)
+    ws = _workspace(_capi.load().xfb_dot_product_attention_workspace(B, H, nq, nk, d), device)
+    _capi.call("xfb_dot_product_attention", _ptr(q), _ptr(k), _ptr(v), B, H, nq, nk, d,
+               _ptr(mask_t), mask_code, mask_batched, _ptr(bias_t),
+               _code(bias_t) if bias_t is not None else _capi.BF16, bias_batched,
+               1 if q_pre_scaled else 0, _ptr(out), _ptr(ws), ws.numel(), _stream(device))
+    return out
+
+
+def pack_attention_weights(q_w: torch.Tensor, k_w: torch.Tensor, v_w: torch.Tensor,
+                           gate_w: torch.Tensor) -> torch.Tensor:
+    device = _check_cuda(q_w, k_w, v_w, gate_w)
+    c = q_w.shape[1]
+    tensors = [_contig(t, torch.bfloat16) for t in (q_w, k_w, v_w, gate_w)]
+    packed = torch.empty((4 * c, c), dtype=torch.bfloat16, device=device)
+    _capi.call("xfb_pack_attention_weights", *(_ptr(t) for t in tensors), _capi.BF16, c,
+               _ptr(packed), _stream(device))
+    return packed
+
+
+def grid_self_attention(pair: torch.Tensor, mask: torch.Tensor | None, transpose: bool,
+                        norm_weight: torch.Tensor | None, norm_bias: torch.Tensor | None,
+                        eps: float, bias_weight: torch.Tensor, packed: torch.Tensor,
+                        output_weight: torch.Tensor, num_head: int,
+                        out: torch.Tensor | None = None, accumulate: bool = False,
+                        out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """GridSelfAttention update (xfold/nn/attention.py:80-105); `packed` is
+    pack_attention_weights(q, k, v, gating_query)."""
+    device = _check_cuda(pair, mask, bias_weight, packed, output_weight)
+    n, _, c = pair.shape
+    pair = _contig(pair)
+    if mask is not None:
+        mask = _contig(mask.expand(n, n), torch.float32)
+    if out is None:
+        out = torch.empty((n, n, c), dtype=out_dtype, device=device)
+    # Converted copies stay referenced until the launch is enqueued: a freed
+    # temporary's block can be handed to the next temporary before the kernel runs.
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    bw, ow = prepare_weight(bias_weight), prepare_weight(output_weight)
+    ws = _workspace(_capi.load().xfb_grid_self_attention_workspace(n, c, num_head), device)
+    _capi.call("xfb_grid_self_attention", _ptr(pair), _code(pair), n, c, num_head, _ptr(mask),
+               1 if transpose else 0, _ptr(nw), _ptr(nb), float(eps), _ptr(bw), None, None, None,
+               None, _ptr(ow), 1, _ptr(packed), _ptr(out), _code(out), 1 if accumulate else 0,
+               _ptr(ws), ws.numel(), _stream(device))
+    return out
+
+
+def transition(x: torch.Tensor, norm_weight: torch.Tensor | None,
+               norm_bias: torch.Tensor | None, eps: float, w1_packed: torch.Tensor,
+               w2: torch.Tensor, factor: int, mod_scale: torch.Tensor | None = None,
+               mod_shift: torch.Tensor | None = None, out_gate: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, accumulate: bool = False,
+               out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """GLU transition update (Transition / DiffusionTransition); w1_packed is
+    pack_glu_weight(transition1.weight), w2 = transition2.weight."""
+    device = _check_cuda(x, w1_packed, w2, mod_scale, mod_shift, out_gate)
+    c = x.shape[-1]
+    rows = x.numel() // c
+    x = _contig(x)
+    mod_scale, mod_shift, out_gate = (_contig(t, torch.bfloat16) for t in (mod_scale, mod_shift, out_gate))
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    w2 = prepare_weight(w2)
+    ws = _workspace(_capi.load().xfb_transition_workspace(rows, c, factor), device)
+    _capi.call("xfb_transition", _ptr(x), _code(x), rows, c, factor, _ptr(nw), _ptr(nb),
+               float(eps), _ptr(mod_scale), _ptr(mod_shift), _ptr(w1_packed), 1, _ptr(w2),
+               _ptr(out_gate), _ptr(out), _code(out), 1 if accumulate else 0, _ptr(ws),
+               ws.numel(), _stream(device))
+    return out
+
+
+def self_attention(x: torch.Tensor, mask: torch.Tensor | None, pair_logits: torch.Tensor | None,
+                   norm_weight: torch.Tensor | None, norm_bias: torch.Tensor | None, eps: float,
+                   packed: torch.Tensor, q_bias: torch.Tensor | None, wo: torch.Tensor,
+                   num_head: int, mod_scale: torch.Tensor | None = None,
+                   mod_shift: torch.Tensor | None = None, out_gate: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, accumulate: bool = False,
+                   out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """SelfAttention with pair bias (xfold/nn/diffusion_transformer.py:184-217)."""
+    device = _check_cuda(x, mask, pair_logits, packed, wo)
+    n, c = x.shape
+    x = _contig(x)
+    if mask is not None:
+        mask = _contig(mask.expand(n), torch.float32)
+    if pair_logits is not None:
+        pair_logits = _contig(pair_logits, torch.bfloat16)
+    mod_scale, mod_shift, out_gate = (_contig(t, torch.bfloat16) for t in (mod_scale, mod_shift, out_gate))
+    if out is None:
+        out = torch.empty((n, c), dtype=out_dtype, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    qb, wo = _contig(q_bias, torch.float32), prepare_weight(wo)
+    ws = _workspace(_capi.load().xfb_self_attention_workspace(n, c, num_head), device)
+    _capi.call("xfb_self_attention", _ptr(x), _code(x), n, c, num_head, _ptr(mask),
+               _ptr(pair_logits), _ptr(nw), _ptr(nb), float(eps), _ptr(mod_scale),
+               _ptr(mod_shift), None, _ptr(qb), None, None, None, 1, _ptr(packed), _ptr(wo),
+               _ptr(out_gate), _ptr(out), _code(out), 1 if accumulate else 0, _ptr(ws),
+               ws.numel(), _stream(device))
+    return out
+
+
+def pair_logits(pair: torch.Tensor, norm_weight: torch.Tensor | None,
+                norm_bias: torch.Tensor | None, eps: float, weight: torch.Tensor) -> torch.Tensor:
+    """[H, N, N] bf16 logits = LN(pair) @ weight^T, permuted (pairformer.py:103-106)."""
+    device = _check_cuda(pair, weight)
+    n, _, c = pair.shape
+    heads = weight.shape[0]
+    pair = _contig(pair)
+    logits = torch.empty((heads, n, n), dtype=torch.bfloat16, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    w = prepare_weight(weight)
+    _capi.call("xfb_pair_logits", _ptr(pair), _code(pair), n, c, heads, _ptr(nw), _ptr(nb),
+               float(eps), _ptr(w), _ptr(logits), _stream(device))
+    return logits

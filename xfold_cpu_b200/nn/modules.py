@@ -1,0 +1,380 @@
+"""xfold hot-path modules with the `cuda` backend.
+
+Each class mirrors the reference module of the same name: constructor
+arguments, submodule and parameter names (so a reference state_dict / AF3
+checkpoint mapping loads unchanged) and forward signature.  forward() returns
+the update like the reference; accumulate_() adds it into an f32 residual
+stream in place through the fused epilogue (the `x += op(x)` of the callers).
+
+  TriangleMultiplication   xfold/nn/triangle_multiplication.py:21-105
+  GridSelfAttention        xfold/nn/attention.py:26-105
+  Transition               xfold/nn/primitives.py:20-37
+  AdaptiveLayerNorm        xfold/nn/diffusion_transformer.py:27-64
+  AdaLNZero                xfold/nn/diffusion_transformer.py:67-95
+  DiffusionTransition      xfold/nn/diffusion_transformer.py:98-128
+  SelfAttention            xfold/nn/diffusion_transformer.py:131-217
+  DiffusionTransformer     xfold/nn/diffusion_transformer.py:220-272
+  PairformerBlock          xfold/nn/pairformer.py:26-114
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import native
+from ..fastnn import LayerNorm, WeightCache
+from ..fastnn import config
+
+
+def _bf16(cache: WeightCache, weight: torch.Tensor) -> torch.Tensor:
+    return cache.get((weight,), native.prepare_weight)
+
+
+def _fused_target(x: torch.Tensor) -> bool:
+    """True when the update can be added in place by the kernel epilogue."""
+    return x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+
+
+class TriangleMultiplication(nn.Module):
+    def __init__(self, c_pair: int = 128, _outgoing: bool = True) -> None:
+        super().__init__()
+        self.c_pair = c_pair
+        self.left_norm_input = LayerNorm(c_pair)
+        self.projection = nn.Linear(c_pair, 2 * c_pair, bias=False)
+        self.gate = nn.Linear(c_pair, 2 * c_pair, bias=False)
+        self.center_norm = LayerNorm(c_pair)
+        self.output_projection = nn.Linear(c_pair, c_pair, bias=False)
+        self.gating_linear = nn.Linear(c_pair, c_pair, bias=False)
+        self.equation = "cik,cjk->cij" if _outgoing else "ckj,cki->cij"
+        self._packed = WeightCache()
+        self._out_w = WeightCache()
+
+    @property
+    def outgoing(self) -> bool:
+        return self.equation == "cik,cjk->cij"
+
+    def _run(self, pair, mask, out, accumulate):
+        config.require_cuda("triangle_multiplication_implementation")
+        packed = self._packed.get(
+            (self.projection.weight, self.gate.weight, self.gating_linear.weight),
+            native.pack_triangle_weights)
+        return native.triangle_multiplication(
+            pair, mask, self.outgoing, self.left_norm_input.weight, self.left_norm_input.bias,
+            None, None, self.center_norm.weight, self.center_norm.bias,
+            _bf16(self._out_w, self.output_projection.weight), None,
+            self.left_norm_input.eps, self.center_norm.eps, weights_packed=True, packed=packed,
+            out=out, accumulate=accumulate)
+
+    def forward(self, pair: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        return self._run(pair, mask, None, False)
+
+    def accumulate_(self, pair: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        if _fused_target(pair):
+            return self._run(pair, mask, pair, True)
+        pair += self.forward(pair, mask)
+        return pair
+
+
+class GridSelfAttention(nn.Module):
+    def __init__(self, c_pair: int = 128, num_head: int = 4, transpose: bool = False):
+        super().__init__()
+        self.c_pair = c_pair
+        self.num_head = num_head
+        self.qkv_dim = c_pair // num_head
+        self.transpose = transpose
+        self.act_norm = LayerNorm(c_pair)
+        self.pair_bias_projection = nn.Linear(c_pair, num_head, bias=False)
+        self.q_projection = nn.Linear(c_pair, c_pair, bias=False)
+        self.k_projection = nn.Linear(c_pair, c_pair, bias=False)
+        self.v_projection = nn.Linear(c_pair, c_pair, bias=False)
+        self.gating_query = nn.Linear(c_pair, c_pair, bias=False)
+        self.output_projection = nn.Linear(c_pair, c_pair, bias=False)
+        self._packed = WeightCache()
+        self._bias_w = WeightCache()
+        self._out_w = WeightCache()
+
+    def _run(self, pair, mask, out, accumulate):
+        config.require_cuda("dot_product_attention_implementation")
+        packed = self._packed.get(
+            (self.q_projection.weight, self.k_projection.weight, self.v_projection.weight,
+             self.gating_query.weight), native.pack_attention_weights)
+        return native.grid_self_attention(
+            pair, mask, self.transpose, self.act_norm.weight, self.act_norm.bias,
+            self.act_norm.eps, _bf16(self._bias_w, self.pair_bias_projection.weight), packed,
+            _bf16(self._out_w, self.output_projection.weight), self.num_head, out=out,
+            accumulate=accumulate)
+
+    def forward(self, pair: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        return self._run(pair, mask, None, False)
+
+    def accumulate_(self, pair: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        if _fused_target(pair):
+            return self._run(pair, mask, pair, True)
+        pair += self.forward(pair, mask)
+        return pair
+
+
+class Transition(nn.Module):
+    def __init__(self, c_x: int, num_intermediate_factor: int = 4) -> None:
+        super().__init__()
+        self.num_intermediate_factor = num_intermediate_factor
+        self.c_in = c_x
+        self.input_layer_norm = LayerNorm(c_x)
+        self.transition1 = nn.Linear(c_x, num_intermediate_factor * c_x * 2, bias=False)
+        self.transition2 = nn.Linear(num_intermediate_factor * c_x, c_x, bias=False)
+        self._glu_weight_cache = WeightCache()
+        self._w2 = WeightCache()
+
+    def _run(self, x, out, accumulate):
+        config.require_cuda("gated_linear_unit_implementation")
+        w1 = self._glu_weight_cache.get((self.transition1.weight,), native.pack_glu_weight)
+        return native.transition(x, self.input_layer_norm.weight, self.input_layer_norm.bias,
+                                 self.input_layer_norm.eps, w1,
+                                 _bf16(self._w2, self.transition2.weight),
+                                 self.num_intermediate_factor, out=out, accumulate=accumulate)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self._run(x, None, False)
+
+    def accumulate_(self, x: torch.Tensor) -> torch.Tensor:
+        if _fused_target(x):
+            return self._run(x, x, True)
+        x += self.forward(x)
+        return x
+
+
+class AdaptiveLayerNorm(nn.Module):
+    def __init__(self, c_x: int, c_single_cond: int, use_single_cond: bool = False) -> None:
+        super().__init__()
+        self.c_x = c_x
+        self.c_single_cond = c_single_cond
+        self.use_single_cond = use_single_cond
+        if use_single_cond:
+            self.layer_norm = LayerNorm(c_x, elementwise_affine=False, bias=False)
+            self.single_cond_layer_norm = LayerNorm(c_single_cond, bias=False)
+            self.single_cond_scale = nn.Linear(c_single_cond, c_x, bias=True)
+            self.single_cond_bias = nn.Linear(c_single_cond, c_x, bias=False)
+        else:
+            self.layer_norm = LayerNorm(c_x)
+
+    def modulation(self, single_cond: torch.Tensor):
+        """(sigmoid(scale), shift) of the conditioned path as bf16 [N, c_x], the
+        rounding of the reference under bf16 autocast (:57-62)."""
+        sc = F.layer_norm(single_cond.float(), (self.c_single_cond,),
+                          self.single_cond_layer_norm.weight, None,
+                          self.single_cond_layer_norm.eps).bfloat16()
+        scale = F.linear(sc, self.single_cond_scale.weight.bfloat16(),
+                         self.single_cond_scale.bias.bfloat16())
+        shift = F.linear(sc, self.single_cond_bias.weight.bfloat16())
+        return torch.sigmoid(scale), shift
+
+    def forward(self, x: torch.Tensor, single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
+        assert (single_cond is None) == (self.use_single_cond is False)
+        y = self.layer_norm(x)
+        if self.use_single_cond:
+            scale, shift = self.modulation(single_cond)
+            return (scale.float() * y.float() + shift.float()).bfloat16()
+        return y
+
+
+class AdaLNZero(nn.Module):
+    def __init__(self, c_in: int, c_out: int, c_single_cond: int, use_single_cond: bool = False) -> None:
+        super().__init__()
+        self.c_in = c_in
+        self.c_out = c_out
+        self.c_single_cond = c_single_cond
+        self.use_single_cond = use_single_cond
+        self.transition2 = nn.Linear(c_in, c_out, bias=False)
+        if use_single_cond:
+            self.adaptive_zero_cond = nn.Linear(c_single_cond, c_out, bias=True)
+
+    def out_gate(self, single_cond: torch.Tensor) -> torch.Tensor:
+        """sigmoid(adaptive_zero_cond(single_cond)) as bf16 (:91-94)."""
+        cond = F.linear(single_cond.bfloat16(), self.adaptive_zero_cond.weight.bfloat16(),
+                        self.adaptive_zero_cond.bias.bfloat16())
+        return torch.sigmoid(cond)
+
+    def forward(self, x: torch.Tensor, single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
+        assert (single_cond is None) == (self.use_single_cond is False)
+        out = native.linear(x, self.transition2.weight)
+        if self.use_single_cond:
+            out = (self.out_gate(single_cond) * out).bfloat16()
+        return out
+
+
+class DiffusionTransition(nn.Module):
+    def __init__(self, c_x: int, c_single_cond: int, num_intermediate_factor: int = 2,
+                 use_single_cond: bool = False) -> None:
+        super().__init__()
+        self.c_x = c_x
+        self.c_single_cond = c_single_cond
+        self.num_intermediate_factor = num_intermediate_factor
+        self.use_single_cond = use_single_cond
+        self.adaptive_layernorm = AdaptiveLayerNorm(c_x, c_single_cond, use_single_cond)
+        self.transition1 = nn.Linear(c_x, 2 * c_x * num_intermediate_factor, bias=False)
+        self._glu_weight_cache = WeightCache()
+        self.adaptive_zero_init = AdaLNZero(num_intermediate_factor * c_x, c_x, c_single_cond,
+                                            use_single_cond)
+        self._w2 = WeightCache()
+
+    def _run(self, x, single_cond, out, accumulate):
+        config.require_cuda("gated_linear_unit_implementation")
+        assert (single_cond is None) == (self.use_single_cond is False)
+        w1 = self._glu_weight_cache.get((self.transition1.weight,), native.pack_glu_weight)
+        ln = self.adaptive_layernorm.layer_norm
+        scale = shift = gate = None
+        if self.use_single_cond:
+            scale, shift = self.adaptive_layernorm.modulation(single_cond)
+            gate = self.adaptive_zero_init.out_gate(single_cond)
+        return native.transition(x, ln.weight, ln.bias, ln.eps, w1,
+                                 _bf16(self._w2, self.adaptive_zero_init.transition2.weight),
+                                 self.num_intermediate_factor, mod_scale=scale, mod_shift=shift,
+                                 out_gate=gate, out=out, accumulate=accumulate)
+
+    def forward(self, x: torch.Tensor, single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self._run(x, single_cond, None, False)
+
+    def accumulate_(self, x, single_cond=None):
+        if _fused_target(x):
+            return self._run(x, single_cond, x, True)
+        x += self.forward(x, single_cond)
+        return x
+
+
+class SelfAttention(nn.Module):
+    def __init__(self, c_x: int = 768, c_single_cond: int = 384, num_head: int = 16,
+                 use_single_cond: bool = False) -> None:
+        super().__init__()
+        self.c_x = c_x
+        self.c_single_cond = c_single_cond
+        self.num_head = num_head
+        self.qkv_dim = c_x // num_head
+        self.use_single_cond = use_single_cond
+        self.adaptive_layernorm = AdaptiveLayerNorm(c_x, c_single_cond, use_single_cond)
+        self.q_projection = nn.Linear(c_x, c_x, bias=True)
+        self.k_projection = nn.Linear(c_x, c_x, bias=False)
+        self.v_projection = nn.Linear(c_x, c_x, bias=False)
+        self.gating_query = nn.Linear(c_x, c_x, bias=False)
+        self.adaptive_zero_init = AdaLNZero(c_x, c_x, c_single_cond, use_single_cond)
+        self._packed = WeightCache()
+        self._wo = WeightCache()
+
+    def _run(self, x, mask, pair_logits, single_cond, out, accumulate):
+        config.require_cuda("dot_product_attention_implementation")
+        assert (single_cond is None) == (self.use_single_cond is False)
+        packed = self._packed.get(
+            (self.q_projection.weight, self.k_projection.weight, self.v_projection.weight,
+             self.gating_query.weight), native.pack_attention_weights)
+        ln = self.adaptive_layernorm.layer_norm
+        scale = shift = gate = None
+        if self.use_single_cond:
+            scale, shift = self.adaptive_layernorm.modulation(single_cond)
+            gate = self.adaptive_zero_init.out_gate(single_cond)
+        return native.self_attention(
+            x, mask, pair_logits, ln.weight, ln.bias, ln.eps, packed, self.q_projection.bias,
+            _bf16(self._wo, self.adaptive_zero_init.transition2.weight), self.num_head,
+            mod_scale=scale, mod_shift=shift, out_gate=gate, out=out, accumulate=accumulate)
+
+    def forward(self, x: torch.Tensor, mask: torch.Tensor, pair_logits: Optional[torch.Tensor] = None,
+                single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self._run(x, mask, pair_logits, single_cond, None, False)
+
+    def accumulate_(self, x, mask, pair_logits=None, single_cond=None):
+        if _fused_target(x):
+            return self._run(x, mask, pair_logits, single_cond, x, True)
+        x += self.forward(x, mask, pair_logits, single_cond)
+        return x
+
+
+class DiffusionTransformer(nn.Module):
+    def __init__(self, c_act: int = 768, c_single_cond: int = 384, c_pair_cond: int = 128,
+                 num_head: int = 16, num_blocks: int = 24, super_block_size: int = 4) -> None:
+        super().__init__()
+        self.c_act = c_act
+        self.c_single_cond = c_single_cond
+        self.c_pair_cond = c_pair_cond
+        self.num_head = num_head
+        self.num_blocks = num_blocks
+        self.super_block_size = super_block_size
+        self.num_super_blocks = num_blocks // super_block_size
+        self.pair_input_layer_norm = LayerNorm(c_pair_cond)
+        self.pair_logits_projection = nn.ModuleList(
+            [nn.Linear(c_pair_cond, super_block_size * num_head, bias=False)
+             for _ in range(self.num_super_blocks)])
+        self.self_attention = nn.ModuleList(
+            [SelfAttention(c_act, c_single_cond, num_head=num_head, use_single_cond=True)
+             for _ in range(num_blocks)])
+        self.transition_block = nn.ModuleList(
+            [DiffusionTransition(c_act, c_single_cond, use_single_cond=True)
+             for _ in range(num_blocks)])
+        self._logits_key = None
+        self._logits = None
+
+    def pair_logits(self, pair_cond: torch.Tensor) -> list[torch.Tensor]:
+        """[super_block][j] -> [H, N, N] bf16 logits; cached per pair_cond version
+        like the reference's InputCache (:256-265)."""
+        key = (pair_cond.data_ptr(), pair_cond._version, tuple(pair_cond.shape),
+               tuple((p.weight.data_ptr(), p.weight._version) for p in self.pair_logits_projection))
+        if key != self._logits_key:
+            ln = self.pair_input_layer_norm
+            logits = []
+            for proj in self.pair_logits_projection:
+                w = proj.weight  # [(b h), c]: block j uses rows [j*H, (j+1)*H)
+                logits.append([native.pair_logits(pair_cond, ln.weight, ln.bias, ln.eps,
+                                                  w[j * self.num_head:(j + 1) * self.num_head])
+                               for j in range(self.super_block_size)])
+            self._logits, self._logits_key = logits, key
+        return self._logits
+
+    def forward(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
+                pair_cond: torch.Tensor) -> torch.Tensor:
+        logits = self.pair_logits(pair_cond)
+        for s in range(self.num_super_blocks):
+            for j in range(self.super_block_size):
+                i = s * self.super_block_size + j
+                self.self_attention[i].accumulate_(act, mask, logits[s][j], single_cond)
+                self.transition_block[i].accumulate_(act, single_cond)
+        return act
+
+
+class PairformerBlock(nn.Module):
+    def __init__(self, n_heads: int = 16, c_pair: int = 128, c_single: int = 384,
+                 c_hidden_mul: int = 128, n_heads_pair: int = 4, num_intermediate_factor: int = 4,
+                 with_single: bool = True) -> None:
+        super().__init__()
+        self.n_heads = n_heads
+        self.with_single = with_single
+        self.num_intermediate_factor = num_intermediate_factor
+        self.triangle_multiplication_outgoing = TriangleMultiplication(c_pair=c_pair, _outgoing=True)
+        self.triangle_multiplication_incoming = TriangleMultiplication(c_pair=c_pair, _outgoing=False)
+        self.pair_attention1 = GridSelfAttention(c_pair=c_pair, num_head=n_heads_pair, transpose=False)
+        self.pair_attention2 = GridSelfAttention(c_pair=c_pair, num_head=n_heads_pair, transpose=True)
+        self.pair_transition = Transition(c_x=c_pair, num_intermediate_factor=num_intermediate_factor)
+        self.c_single = c_single
+        if with_single:
+            self.single_pair_logits_norm = LayerNorm(c_pair)
+            self.single_pair_logits_projection = nn.Linear(c_pair, n_heads, bias=False)
+            self.single_attention_ = SelfAttention(c_x=c_single, num_head=n_heads, use_single_cond=False)
+            self.single_transition = Transition(c_x=c_single)
+        self._logits_w = WeightCache()
+
+    def forward(self, pair: torch.Tensor, pair_mask: torch.Tensor,
+                single: Optional[torch.Tensor] = None, seq_mask: Optional[torch.Tensor] = None):
+        """Updates pair (and single) in place and returns them, as the reference."""
+        self.triangle_multiplication_outgoing.accumulate_(pair, pair_mask)
+        self.triangle_multiplication_incoming.accumulate_(pair, pair_mask)
+        self.pair_attention1.accumulate_(pair, pair_mask)
+        self.pair_attention2.accumulate_(pair, pair_mask)
+        self.pair_transition.accumulate_(pair)
+        if not self.with_single:
+            return pair
+        norm = self.single_pair_logits_norm
+        logits = native.pair_logits(pair, norm.weight, norm.bias, norm.eps,
+                                    _bf16(self._logits_w, self.single_pair_logits_projection.weight))
+        self.single_attention_.accumulate_(single, seq_mask, logits)
+        self.single_transition.accumulate_(single)
+        return pair, single
