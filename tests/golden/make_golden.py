@@ -1,0 +1,167 @@
+"""Generates the golden fixtures of tests/golden/*.npz by running the
+reference implementation itself (xfold, torch backend, CPU).
+
+Usage (from the repository root, with the reference checkout available):
+    PYTHONPATH=<xfold checkout> python tests/golden/make_golden.py
+
+Each fixture holds the inputs, the module's state_dict (parameter names of
+the reference modules) and the reference outputs, in float32; `bf16:` entries
+are the same forward under torch.amp.autocast('cpu', bfloat16), the precision
+mode of the reference's GPU route.  Sizes are small so the files stay small;
+the oracle tests replay them through oracle/hotpath.py.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def _init(module: torch.nn.Module, seed: int, std: float = 0.2) -> None:
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for name, p in module.named_parameters():
+            owner = module.get_submodule(name.rsplit(".", 1)[0]) if "." in name else module
+            if isinstance(owner, torch.nn.Linear):
+                p.copy_(torch.randn(p.shape, generator=g) * std)
+            elif name.endswith("weight"):
+                p.copy_(1.0 + 0.1 * torch.randn(p.shape, generator=g))
+            else:
+                p.copy_(0.1 * torch.randn(p.shape, generator=g))
+
+
+def _save(name: str, module, inputs: dict, outputs: dict) -> None:
+    arrays = {}
+    if module is not None:
+        for k, v in module.state_dict().items():
+            arrays[f"param:{k}"] = v.detach().float().numpy()
+    for k, v in inputs.items():
+        arrays[f"in:{k}"] = v.detach().float().numpy()
+    for k, v in outputs.items():
+        arrays[f"out:{k}"] = v.detach().float().numpy()
+    np.savez_compressed(OUT / f"{name}.npz", **arrays)
+    print(f"wrote {name}.npz ({sum(a.size for a in arrays.values())} values)")
+
+
+def _both(fn):
+    """Runs fn() in float32 and under CPU bf16 autocast (inference mode)."""
+    with torch.inference_mode():
+        fp32 = fn()
+        with torch.amp.autocast("cpu", dtype=torch.bfloat16):
+            bf16 = fn()
+    return fp32, bf16
+
+
+def main() -> None:
+    from xfold.fastnn import config
+    from xfold import fastnn
+    from xfold.nn.attention import GridSelfAttention
+    from xfold.nn.diffusion_transformer import DiffusionTransition, SelfAttention
+    from xfold.nn.pairformer import PairformerBlock
+    from xfold.nn.primitives import Transition
+    from xfold.nn.triangle_multiplication import TriangleMultiplication
+
+    for opt in ("layer_norm_implementation", "dot_product_attention_implementation",
+                "gated_linear_unit_implementation", "triangle_multiplication_implementation"):
+        setattr(config, opt, "torch")
+    g = torch.Generator().manual_seed(1234)
+
+    def masks(n, tail):
+        seq = torch.ones(n)
+        seq[-tail:] = 0
+        return seq, seq[:, None] * seq[None, :]
+
+    # --- TriangleMultiplication, both directions, ragged mask (reference test :104-115 pattern)
+    for outgoing in (True, False):
+        n, c = 9, 16
+        mod = TriangleMultiplication(c, _outgoing=outgoing).eval()
+        _init(mod, 10 + outgoing)
+        pair = torch.randn(n, n, c, generator=g)
+        mask = (torch.rand(n, n, generator=g) > 0.2).float()
+        fp32, bf16 = _both(lambda: mod(pair, mask))
+        _save(f"triangle_{'outgoing' if outgoing else 'incoming'}", mod,
+              {"pair": pair, "mask": mask}, {"update": fp32, "bf16:update": bf16})
+
+    # --- GridSelfAttention, starting and ending node
+    for transpose in (False, True):
+        n, c = 7, 16
+        mod = GridSelfAttention(c, num_head=4, transpose=transpose).eval()
+        _init(mod, 20 + transpose)
+        pair = torch.randn(n, n, c, generator=g)
+        _, mask = masks(n, 2)
+        fp32, bf16 = _both(lambda: mod(pair, mask))
+        _save(f"grid_attention_{'ending' if transpose else 'starting'}", mod,
+              {"pair": pair, "mask": mask}, {"update": fp32, "bf16:update": bf16})
+
+    # --- Transition (GLU)
+    mod = Transition(16, num_intermediate_factor=4).eval()
+    _init(mod, 30)
+    x = torch.randn(5, 6, 16, generator=g)
+    fp32, bf16 = _both(lambda: mod(x))
+    _save("transition", mod, {"x": x}, {"update": fp32, "bf16:update": bf16})
+
+    # --- dot_product_attention with mask ranks 1/2/4 and bias (reference test :70-89 pattern)
+    q = torch.randn(2, 3, 5, 8, generator=g)
+    k = torch.randn(2, 3, 6, 8, generator=g)
+    v = torch.randn(2, 3, 6, 8, generator=g)
+    bias = torch.randn(2, 3, 5, 6, generator=g)
+    m1 = torch.tensor([1, 1, 0, 1, 0, 1], dtype=torch.bool)
+    m2 = torch.tensor([[1, 0, 1, 1, 1, 0], [0, 0, 0, 0, 0, 0]], dtype=torch.bool)
+    m4 = m1[None, None, None, :].expand(2, 1, 1, 6)
+    outs = {}
+    with torch.inference_mode():
+        for tag, mask in (("rank1", m1), ("rank2", m2), ("rank4", m4), ("none", None)):
+            outs[tag] = fastnn.dot_product_attention(q, k, v, mask=mask, bias=bias)
+    _save("dot_product_attention", None,
+          {"q": q, "k": k, "v": v, "bias": bias, "mask_rank1": m1.float(), "mask_rank2": m2.float(),
+           "mask_rank4": m4.float()}, outs)
+
+    # --- SelfAttention, plain (single track) and conditioned (diffusion)
+    for cond in (False, True):
+        n, c, cs = 10, 32, 8
+        mod = SelfAttention(c, cs, num_head=4, use_single_cond=cond).eval()
+        _init(mod, 40 + cond)
+        x = torch.randn(n, c, generator=g)
+        seq, _ = masks(n, 3)
+        logits = torch.randn(4, n, n, generator=g)
+        sc = torch.randn(n, cs, generator=g) if cond else None
+        fp32, bf16 = _both(lambda: mod(x, seq, logits, sc))
+        inputs = {"x": x, "mask": seq, "pair_logits": logits}
+        if cond:
+            inputs["single_cond"] = sc
+        _save(f"self_attention_{'conditioned' if cond else 'plain'}", mod, inputs,
+              {"update": fp32, "bf16:update": bf16})
+
+    # --- DiffusionTransition (conditioned)
+    mod = DiffusionTransition(16, 8, use_single_cond=True).eval()
+    _init(mod, 50)
+    x = torch.randn(6, 16, generator=g)
+    sc = torch.randn(6, 8, generator=g)
+    fp32, bf16 = _both(lambda: mod(x, sc))
+    _save("diffusion_transition", mod, {"x": x, "single_cond": sc},
+          {"update": fp32, "bf16:update": bf16})
+
+    # --- PairformerBlock end to end (reference test :117-125 pattern)
+    n = 8
+    mod = PairformerBlock(n_heads=4, c_pair=16, c_single=32, n_heads_pair=4).eval()
+    _init(mod, 60, std=0.1)
+    pair = torch.randn(n, n, 16, generator=g)
+    single = torch.randn(n, 32, generator=g)
+    seq, pmask = masks(n, 2)
+
+    def block():
+        p, s = pair.clone(), single.clone()
+        return mod(p, pmask, s, seq)
+
+    (p32, s32), (p16, s16) = _both(block)
+    _save("pairformer_block", mod, {"pair": pair, "single": single, "pair_mask": pmask, "seq_mask": seq},
+          {"pair": p32, "single": s32, "bf16:pair": p16, "bf16:single": s16})
+
+
+if __name__ == "__main__":
+    sys.exit(main())

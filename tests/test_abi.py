@@ -1,0 +1,52 @@
+"""The C-ABI library loads and exports every function include/xfold_b200.h
+declares (no device work: this runs without a GPU)."""
+
+import re
+from pathlib import Path
+
+import pytest
+
+from xfold_cpu_b200 import _capi
+from xfold_cpu_b200.build import LIB_PATH
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "xfold_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"XFB_API\s+[\w\s\*]+?\b(xfb_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_operator_set():
+    names = declared_symbols()
+    for required in ("xfb_triangle_multiplication", "xfb_dot_product_attention",
+                     "xfb_gated_linear_unit", "xfb_linear", "xfb_layer_norm", "xfb_runtime_info",
+                     "xfb_gemm", "xfb_grid_self_attention", "xfb_transition", "xfb_self_attention"):
+        assert required in names
+
+
+@pytest.mark.skipif(not LIB_PATH.exists(), reason="library not built")
+def test_library_exports_every_declared_symbol():
+    lib = _capi.load()
+    missing = [name for name in declared_symbols() if not hasattr(lib, name)]
+    assert not missing, missing
+
+
+def test_binding_table_matches_header():
+    assert sorted(_capi.SIGNATURES) == declared_symbols()
+
+
+@pytest.mark.skipif(not LIB_PATH.exists(), reason="library not built")
+def test_workspace_queries_need_no_device():
+    lib = _capi.load()
+    assert lib.xfb_triangle_multiplication_workspace(1024, 128) > 4 * 1024 * 1024 * 128
+    assert lib.xfb_grid_self_attention_workspace(64, 128, 4) > 0
+    assert lib.xfb_transition_workspace(100, 128, 4) > 0
+
+
+@pytest.mark.skipif(not LIB_PATH.exists(), reason="library not built")
+def test_argument_errors_are_reported_without_a_device():
+    lib = _capi.load()
+    rc = lib.xfb_linear(None, 4, 7, None, 8, None, None, 0, 0, None)
+    assert rc == _capi.ERR_INVALID
+    assert "multiples of 8" in _capi.last_error()

@@ -1,0 +1,111 @@
+"""Pins the CPU oracle to the reference: every golden fixture (made by running
+the reference modules, tests/golden/make_golden.py) is replayed through
+oracle/hotpath.py.  float32 outputs must agree to 1e-5 (relative to the
+output's max magnitude); the reference's own bf16-autocast outputs are checked
+to sit within the 1e-2 parity tolerance of the float32 oracle."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+FP32_TOL = 1e-5
+BF16_TOL = 2e-2
+
+
+def load(name):
+    data = np.load(GOLDEN / f"{name}.npz")
+    params = {k[6:]: torch.from_numpy(data[k]) for k in data.files if k.startswith("param:")}
+    inputs = {k[3:]: torch.from_numpy(data[k]) for k in data.files if k.startswith("in:")}
+    outputs = {k[4:]: torch.from_numpy(data[k]) for k in data.files if k.startswith("out:")}
+    return params, inputs, outputs
+
+
+def check(got, ref, tol):
+    err = oracle.relative_error(got, ref)
+    assert err <= tol, f"relative error {err:.3e} > {tol}"
+
+
+@pytest.mark.parametrize("direction", ["outgoing", "incoming"])
+def test_triangle_multiplication(direction):
+    p, i, o = load(f"triangle_{direction}")
+    got = oracle.triangle_multiplication(i["pair"], i["mask"], p, direction == "outgoing")
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_triangle_direction_is_not_symmetric():
+    """Planted mistake: swapping the contraction direction must be caught."""
+    p, i, o = load("triangle_outgoing")
+    wrong = oracle.triangle_multiplication(i["pair"], i["mask"], p, False)
+    assert oracle.relative_error(wrong, o["update"]) > 1e-2
+
+
+@pytest.mark.parametrize("node", ["starting", "ending"])
+def test_grid_self_attention(node):
+    p, i, o = load(f"grid_attention_{node}")
+    got = oracle.grid_self_attention(i["pair"], i["mask"], p, node == "ending", 4)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_grid_attention_chunking_is_exact():
+    p, i, o = load("grid_attention_ending")
+    got = oracle.grid_self_attention(i["pair"], i["mask"], p, True, 4, batch_chunk=2)
+    check(got, o["update"], FP32_TOL)
+
+
+def test_transition():
+    p, i, o = load("transition")
+    got = oracle.transition(i["x"], p)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+@pytest.mark.parametrize("rank", ["rank1", "rank2", "rank4", "none"])
+def test_dot_product_attention(rank):
+    _, i, o = load("dot_product_attention")
+    mask = None
+    if rank != "none":
+        mask = i[f"mask_{rank}"].bool()
+        if rank == "rank1" or rank == "rank2":
+            mask = mask.float()
+    got = oracle.dot_product_attention(i["q"], i["k"], i["v"], mask=mask, bias=i["bias"])
+    check(got, o[rank], FP32_TOL)
+
+
+def test_fully_masked_row_is_uniform():
+    """rank2 fixture row 1 masks every key: the reference gives the plain mean of v."""
+    _, i, o = load("dot_product_attention")
+    mean_v = i["v"][1].mean(dim=1, keepdim=True).expand(-1, 5, -1)
+    check(o["rank2"][1], mean_v, 1e-5)
+
+
+@pytest.mark.parametrize("variant", ["plain", "conditioned"])
+def test_self_attention(variant):
+    p, i, o = load(f"self_attention_{variant}")
+    cond = variant == "conditioned"
+    got = oracle.self_attention(i["x"], i["mask"], i["pair_logits"], p, i.get("single_cond"), 4, cond)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_diffusion_transition():
+    p, i, o = load("diffusion_transition")
+    got = oracle.diffusion_transition(i["x"], i["single_cond"], p, True)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_pairformer_block():
+    p, i, o = load("pairformer_block")
+    pair, single = oracle.pairformer_block(i["pair"], i["pair_mask"], i["single"], i["seq_mask"], p,
+                                           n_heads=4, n_heads_pair=4)
+    check(pair, o["pair"], 1e-5)
+    check(single, o["single"], 1e-5)
+    check(o["bf16:pair"] - i["pair"], pair - i["pair"], BF16_TOL)
+    check(o["bf16:single"] - i["single"], single - i["single"], BF16_TOL)
