@@ -109,33 +109,66 @@ int get_encoder() {
   return XFB_OK;
 }
 
+// N-D tensor map (rank 2..5) over bf16 or f32 data.  dims[0] is contiguous;
+// strides[i] is the byte stride of dims[i+1].  Size-1 trailing dimensions
+// get a consistent stride.  The base must be 16-byte aligned and every stride
+// a multiple of 16 bytes (the TMA rules).
+int make_map_nd(CUtensorMap* map, bool f32, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swz) {
+  XFB_TRY(get_encoder());
+  if (!aligned16(base)) return fail(XFB_ERR_INVALID, "TMA operand base is not 16-byte aligned");
+  cuuint64_t d[5], s[4];
+  cuuint32_t bx[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    estr[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    uint64_t st = strides[i];
+    if (dims[i + 1] == 1 && i > 0) st = std::max<uint64_t>(st, s[i - 1] * dims[i]);
+    st = static_cast<uint64_t>(round_up(static_cast<int64_t>(st), 16));
+    if (strides[i] % 16 != 0 && dims[i + 1] != 1)
+      return fail(XFB_ERR_INVALID, "TMA operand stride is not a multiple of 16 bytes");
+    s[i] = st;
+  }
+  CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        rank, const_cast<void*>(base), d, s, bx, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d): rank %d dims %llu %llu %llu box %u %u",
+             static_cast<int>(r), rank, (unsigned long long)dims[0],
+             (unsigned long long)(rank > 1 ? dims[1] : 0), (unsigned long long)(rank > 2 ? dims[2] : 0),
+             box[0], rank > 1 ? box[1] : 0);
+    return fail(XFB_ERR_CUDA, buf);
+  }
+  return XFB_OK;
+}
+
 // 3-D bf16 tensor map: element (x, y, z) at base + x*2 + y*stride1 + z*stride2.
 int make_map(CUtensorMap* map, const void* base, uint64_t dx, uint64_t dy, uint64_t dz,
              uint64_t stride1, uint64_t stride2, uint32_t bx, uint32_t by,
              CUtensorMapSwizzle swz) {
-  XFB_TRY(get_encoder());
-  if (!aligned16(base)) return fail(XFB_ERR_INVALID, "TMA operand base is not 16-byte aligned");
-  if (stride1 % 16 != 0 || stride2 % 16 != 0)
-    return fail(XFB_ERR_INVALID, "TMA operand row stride is not a multiple of 16 bytes");
   if (dz == 1) stride2 = std::max<uint64_t>(stride2, stride1 * dy);
-  stride2 = round_up(static_cast<int64_t>(stride2), 16);
-  cuuint64_t dims[3] = {dx, dy, dz};
-  cuuint64_t strides[2] = {stride1, stride2};
-  cuuint32_t box[3] = {bx, by, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    char buf[256];
-    snprintf(buf, sizeof(buf),
-             "cuTensorMapEncodeTiled failed (%d): dims %llu %llu %llu strides %llu %llu box %u %u",
-             static_cast<int>(r), (unsigned long long)dx, (unsigned long long)dy,
-             (unsigned long long)dz, (unsigned long long)stride1, (unsigned long long)stride2, bx,
-             by);
-    return fail(XFB_ERR_CUDA, buf);
-  }
-  return XFB_OK;
+  const uint64_t dims[3] = {dx, dy, dz};
+  const uint64_t strides[2] = {stride1, stride2};
+  const uint32_t box[3] = {bx, by, 1};
+  return make_map_nd(map, false, 3, base, dims, strides, box, swz);
+}
+
+// Row-major [batch][rows][ld] output map with a box of 128 rows and one
+// 128-byte swizzle atom of columns (32 f32 or 64 bf16).
+int make_out_map(CUtensorMap* map, const void* base, bool f32, int64_t cols, int64_t rows,
+                 int64_t batch, int64_t ld, int64_t bstride) {
+  const int64_t es = f32 ? 4 : 2;
+  const uint64_t dims[3] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows),
+                            static_cast<uint64_t>(batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(ld * es),
+                               static_cast<uint64_t>((batch > 1 ? bstride : ld * rows) * es)};
+  const uint32_t box[3] = {f32 ? 32u : 64u, 128u, 1u};
+  return make_map_nd(map, f32, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <class Kernel>
@@ -146,14 +179,29 @@ int set_smem(Kernel kernel, int bytes) {
 
 // ------------------------------------------------------------------ GEMM launcher
 
+// Deepest operand pipeline that fits next to the epilogue's buffers.
+template <int BN, class Epi>
+constexpr int gemm_stages() {
+  constexpr int stage = (128 + BN) * 64 * 2;
+  constexpr int aux = ((Epi::kAuxBytes + 1023) / 1024) * 1024 * 2;
+  constexpr int staging = ((Epi::kStagingBytes + 1023) / 1024) * 1024 * Epi::kStagingBufs;
+  constexpr int budget = 200 * 1024 - aux - staging;
+  return budget / stage > 6 ? 6 : budget / stage;
+}
+
 // A: K-major -> element (m, k) at A[bat*a_bs + m*lda + k]; MN-major -> A[bat*a_bs + k*lda + m].
-// B: K-major -> element (n, k) at B[bat*b_bs + n*ldb + k]; MN-major -> B[bat*b_bs + k*ldb + n].
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+// B: K-major -> element (n, k) at B[bb*b_bs + n*ldb + k]; MN-major -> B[bb*b_bs + k*ldb + n],
+// with bb = 0 when b_shared (one weight for every batch index) else bb = bat.
+template <int BN, bool A_MN, bool B_MN, class Epi>
 int run_gemm(const void* A, int64_t lda, int64_t a_bs, const void* B, int64_t ldb, int64_t b_bs,
-             int64_t M, int64_t N, int64_t K, int64_t batch, const Epi& epi, cudaStream_t st) {
+             int64_t M, int64_t N, int64_t K, int64_t batch, const Epi& epi, cudaStream_t st,
+             bool b_shared = false) {
+  constexpr int STAGES = gemm_stages<BN, Epi>();
+  static_assert(STAGES >= 2, "epilogue buffers leave no room for the operand pipeline");
   if (M <= 0 || N <= 0 || batch <= 0) return XFB_OK;
   if (K <= 0) return fail(XFB_ERR_INVALID, "GEMM with empty reduction dimension");
   if (M > (1ll << 31) - 256 || N > (1 << 30)) return fail(XFB_ERR_INVALID, "GEMM too large");
+  const int64_t b_batch = b_shared ? 1 : batch;
   CUtensorMap ta, tb;
   if (A_MN) {
     XFB_TRY(make_map(&ta, A, M, K, batch, lda * 2, a_bs * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B));
@@ -161,9 +209,9 @@ int run_gemm(const void* A, int64_t lda, int64_t a_bs, const void* B, int64_t ld
     XFB_TRY(make_map(&ta, A, K, M, batch, lda * 2, a_bs * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   if (B_MN) {
-    XFB_TRY(make_map(&tb, B, N, K, batch, ldb * 2, b_bs * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B));
+    XFB_TRY(make_map(&tb, B, N, K, b_batch, ldb * 2, b_bs * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B));
   } else {
-    XFB_TRY(make_map(&tb, B, K, N, batch, ldb * 2, b_bs * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B));
+    XFB_TRY(make_map(&tb, B, K, N, b_batch, ldb * 2, b_bs * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   xfb::GemmShape sh;
   sh.M = static_cast<int>(M);
@@ -173,12 +221,13 @@ int run_gemm(const void* A, int64_t lda, int64_t a_bs, const void* B, int64_t ld
   sh.m_tiles = static_cast<int>((M + 127) / 128);
   sh.n_tiles = static_cast<int>((N + BN - 1) / BN);
   sh.k_blocks = static_cast<int>((K + 63) / 64);
+  sh.b_shared = b_shared ? 1 : 0;
   const int64_t total = static_cast<int64_t>(sh.m_tiles) * sh.n_tiles * sh.batch;
   if (total > (1ll << 31) - 1) return fail(XFB_ERR_INVALID, "GEMM has too many tiles");
   int sms;
   XFB_TRY(sm_count(&sms));
   const int grid = static_cast<int>(std::min<int64_t>(total, sms));
-  using L = xfb::GemmSmem<BN, STAGES>;
+  using L = xfb::GemmSmem<BN, STAGES, Epi>;
   auto kernel = xfb::gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   XFB_TRY(set_smem(kernel, L::kLaunchBytes));
   kernel<<<grid, xfb::kGemmThreads, L::kLaunchBytes, st>>>(ta, tb, sh, epi);
@@ -186,22 +235,56 @@ int run_gemm(const void* A, int64_t lda, int64_t a_bs, const void* B, int64_t ld
   return XFB_OK;
 }
 
-// Row-major K-major GEMM with a plain (linear) epilogue, BN = 128.
+template <class EPI>
+int linear_tma(const bf16* x, int64_t m, int64_t k, int64_t ldx, const bf16* w, int64_t n,
+               const float* bias, const bf16* gate, void* out, int accumulate, cudaStream_t st) {
+  constexpr bool kF32 = EPI::kColsPerBox == 32;
+  EPI epi;
+  XFB_TRY(make_out_map(&epi.out_map, out, kF32, n, m, 1, n, 0));
+  epi.bias = bias;
+  epi.accumulate = accumulate;
+  if constexpr (EPI::kAuxBytes > 0) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(n), static_cast<uint64_t>(m), 1};
+    const uint64_t strides[2] = {static_cast<uint64_t>(n * 2), static_cast<uint64_t>(n * m * 2)};
+    const uint32_t box[3] = {64, 128, 1};
+    XFB_TRY(make_map_nd(&epi.gate_map, false, 3, gate, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  return run_gemm<128, false, false>(x, ldx, 0, w, k, 0, m, n, k, 1, epi, st);
+}
+
+// y[m][n] (=|+=) bf16(x[m][k] w[n][k]^T + bias) [* gate], BN = 128, output via
+// TMA store / reduce-add (f32 or bf16 y with row stride n).  Needs n % 8 == 0
+// and 16-byte aligned pointers; anything else takes the direct-store epilogue.
 int linear_core(const bf16* x, int64_t m, int64_t k, int64_t ldx, const bf16* w, int64_t n,
                 const float* bias, const bf16* gate, int64_t ld_gate, void* out, int out_f32,
                 int accumulate, int64_t ld_out, cudaStream_t st) {
-  xfb::EpiLinear<128> epi;
-  epi.out = out;
-  epi.ld_out = ld_out;
-  epi.bstride_out = 0;
-  epi.out_f32 = out_f32;
-  epi.accumulate = accumulate;
-  epi.bias = bias;
-  epi.gate = gate;
-  epi.ld_gate = ld_gate;
-  epi.M = static_cast<int>(m);
-  epi.N = static_cast<int>(n);
-  return run_gemm<128, 6, false, false>(x, ldx, 0, w, k, 0, m, n, k, 1, epi, st);
+  const bool tma_ok = n % 8 == 0 && ld_out == n && aligned16(out) &&
+                      (gate == nullptr || (ld_gate == n && aligned16(gate)));
+  if (!tma_ok) {
+    xfb::EpiDirect<128> epi;
+    epi.out = out;
+    epi.ld_out = ld_out;
+    epi.bstride_out = 0;
+    epi.out_f32 = out_f32;
+    epi.accumulate = accumulate;
+    epi.bias = bias;
+    epi.gate = gate;
+    epi.ld_gate = ld_gate;
+    epi.M = static_cast<int>(m);
+    epi.N = static_cast<int>(n);
+    return run_gemm<128, false, false>(x, ldx, 0, w, k, 0, m, n, k, 1, epi, st);
+  }
+  if (gate != nullptr) {
+    return out_f32 ? linear_tma<xfb::EpiOutGated<128, true>>(x, m, k, ldx, w, n, bias, gate, out,
+                                                             accumulate, st)
+                   : linear_tma<xfb::EpiOutGated<128, false>>(x, m, k, ldx, w, n, bias, gate, out,
+                                                              accumulate, st);
+  }
+  return out_f32 ? linear_tma<xfb::EpiOut<128, true>>(x, m, k, ldx, w, n, bias, gate, out,
+                                                      accumulate, st)
+                 : linear_tma<xfb::EpiOut<128, false>>(x, m, k, ldx, w, n, bias, gate, out,
+                                                       accumulate, st);
 }
 
 // ------------------------------------------------------------------ LayerNorm launcher
@@ -566,12 +649,9 @@ XFB_API int xfb_gated_linear_unit(const void* x, int64_t m, int64_t k, const voi
     XFB_TRY(launch_pack(weight, nullptr, nullptr, nullptr, XFB_BF16, 1, n, k, 2 * n, pk, st));
     w = pk;
   }
-  xfb::EpiGLU<128> epi;
-  epi.out = static_cast<bf16*>(y);
-  epi.ld_out = n;
-  epi.M = static_cast<int>(m);
-  epi.N_out = static_cast<int>(n);
-  return run_gemm<128, 6, false, false>(x, k, 0, w, k, 0, m, 2 * n, k, 1, epi, st);
+  xfb::EpiGLU epi;
+  XFB_TRY(make_out_map(&epi.out_map, y, false, n, m, 1, n, 0));
+  return run_gemm<128, false, false>(x, k, 0, w, k, 0, m, 2 * n, k, 1, epi, st);
 }
 
 XFB_API int xfb_gemm(const void* a, const void* b, void* c, int64_t batch, int64_t m, int64_t n,
@@ -584,7 +664,7 @@ XFB_API int xfb_gemm(const void* a, const void* b, void* c, int64_t batch, int64
   XFB_REQUIRE(lda % 8 == 0 && ldb % 8 == 0, "gemm leading dimensions must be multiples of 8");
   XFB_REQUIRE(c_dtype == XFB_F32 ? n % 4 == 0 : n % 8 == 0, "gemm output rows must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  xfb::EpiLinear<256> epi;
+  xfb::EpiDirect<256> epi;
   epi.out = c;
   epi.ld_out = n;
   epi.bstride_out = m * n;
@@ -597,9 +677,9 @@ XFB_API int xfb_gemm(const void* a, const void* b, void* c, int64_t batch, int64
   epi.N = static_cast<int>(n);
   const int64_t a_bs = m * k, b_bs = n * k;
   if (!a_mn_major && !b_mn_major)
-    return run_gemm<256, 4, false, false>(a, lda, a_bs, b, ldb, b_bs, m, n, k, batch, epi, st);
+    return run_gemm<256, false, false>(a, lda, a_bs, b, ldb, b_bs, m, n, k, batch, epi, st);
   if (a_mn_major && b_mn_major)
-    return run_gemm<256, 4, true, true>(a, lda, a_bs, b, ldb, b_bs, m, n, k, batch, epi, st);
+    return run_gemm<256, true, true>(a, lda, a_bs, b, ldb, b_bs, m, n, k, batch, epi, st);
   return fail(XFB_ERR_INVALID, "gemm supports both operands K-major or both MN-major");
 }
 
@@ -673,24 +753,35 @@ XFB_API int xfb_triangle_multiplication(
   // 1. x = LN(pair)
   XFB_TRY(run_layer_norm(pair, pair_dtype, M, c, c, left_weight, left_bias, left_eps, w.x, c,
                          nullptr, nullptr, nullptr, 0, nullptr, 0, st));
-  // 2. fused projection ‖ gate ‖ output gate -> a, b (channel-major), g
+  // 2. fused projection ‖ gate ‖ output gate -> a, b (channel-major), g; batched
+  //    over pair rows i with the packed weight shared, tiles of 128 columns j
   {
     xfb::EpiTriProj epi;
-    epi.a = w.a;
-    epi.b = w.b;
-    epi.g = w.g;
+    const uint64_t ab_dims[3] = {static_cast<uint64_t>(n), static_cast<uint64_t>(n),
+                                 static_cast<uint64_t>(c)};
+    const uint64_t ab_strides[2] = {static_cast<uint64_t>(pitch * 2),
+                                    static_cast<uint64_t>(n * pitch * 2)};
+    const uint32_t ab_box[3] = {128, 1, 32};
+    XFB_TRY(make_map_nd(&epi.a_map, false, 3, w.a, ab_dims, ab_strides, ab_box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE));
+    XFB_TRY(make_map_nd(&epi.b_map, false, 3, w.b, ab_dims, ab_strides, ab_box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE));
+    const uint64_t g_dims[3] = {static_cast<uint64_t>(c), static_cast<uint64_t>(n),
+                                static_cast<uint64_t>(n)};
+    const uint64_t g_strides[2] = {static_cast<uint64_t>(c * 2), static_cast<uint64_t>(n * c * 2)};
+    const uint32_t g_box[3] = {64, 128, 1};
+    XFB_TRY(make_map_nd(&epi.g_map, false, 3, w.g, g_dims, g_strides, g_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
     epi.mask = mask;
-    epi.chan_stride = n * pitch;
     epi.n = static_cast<int>(n);
-    epi.pitch = static_cast<int>(pitch);
-    epi.c = static_cast<int>(c);
-    epi.M = static_cast<int>(M);
     epi.n_proj_tiles = static_cast<int>(2 * c / 64);
-    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, wcat, c, 0, M, 5 * c, c, 1, epi, st)));
+    epi.c = static_cast<int>(c);
+    XFB_TRY((run_gemm<128, false, false>(w.x, c, n * c, wcat, c, 0, n, 5 * c, c, n, epi, st,
+                                         true)));
   }
   // 3. per-channel contraction z[ch] = a[ch] b[ch]^T (outgoing) or b[ch]^T a[ch] (incoming)
   {
-    xfb::EpiLinear<256> epi;
+    xfb::EpiDirect<256> epi;
     epi.out = w.z;
     epi.ld_out = pitch;
     epi.bstride_out = n * pitch;
@@ -702,11 +793,11 @@ XFB_API int xfb_triangle_multiplication(
     epi.M = static_cast<int>(n);
     epi.N = static_cast<int>(n);
     if (outgoing) {
-      XFB_TRY((run_gemm<256, 4, false, false>(w.a, pitch, n * pitch, w.b, pitch, n * pitch, n, n,
-                                              n, c, epi, st)));
+      XFB_TRY((run_gemm<256, false, false>(w.a, pitch, n * pitch, w.b, pitch, n * pitch, n, n, n,
+                                           c, epi, st)));
     } else {
-      XFB_TRY((run_gemm<256, 4, true, true>(w.b, pitch, n * pitch, w.a, pitch, n * pitch, n, n,
-                                            n, c, epi, st)));
+      XFB_TRY((run_gemm<256, true, true>(w.b, pitch, n * pitch, w.a, pitch, n * pitch, n, n, n,
+                                         c, epi, st)));
     }
   }
   // 4. centre LayerNorm over channels (channel-major in, row-major out; x is reused)
@@ -887,8 +978,38 @@ XFB_API int xfb_grid_self_attention(
     XFB_CUDA(cudaMemsetAsync(w.k, 0, bytes, st));
     XFB_CUDA(cudaMemsetAsync(w.v, 0, bytes, st));
   }
-  {
-    xfb::EpiAttProj epi;
+  if (c == 128 && heads == 4) {
+    // batched over pair rows i (weight shared), TMA stores of 128-token tiles
+    xfb::EpiAttProjTma epi;
+    bf16* bufs[3] = {w.q, w.k, w.v};
+    for (int t = 0; t < 3; ++t) {
+      if (!transpose) {
+        const uint64_t dims[3] = {32, static_cast<uint64_t>(n), static_cast<uint64_t>(n * 4)};
+        const uint64_t strides[2] = {64, static_cast<uint64_t>(n * 64)};
+        const uint32_t box[3] = {32, 128, 1};
+        XFB_TRY(make_map_nd(&epi.qkv_map[t], false, 3, bufs[t], dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_64B));
+      } else {
+        const uint64_t dims[4] = {32, static_cast<uint64_t>(n), 4, static_cast<uint64_t>(n)};
+        const uint64_t strides[3] = {64, static_cast<uint64_t>(n * 64),
+                                     static_cast<uint64_t>(4 * n * 64)};
+        const uint32_t box[4] = {32, 1, 1, 128};
+        XFB_TRY(make_map_nd(&epi.qkv_map[t], false, 4, bufs[t], dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_64B));
+      }
+    }
+    const uint64_t g_dims[3] = {static_cast<uint64_t>(c), static_cast<uint64_t>(n),
+                                static_cast<uint64_t>(n)};
+    const uint64_t g_strides[2] = {static_cast<uint64_t>(c * 2), static_cast<uint64_t>(n * c * 2)};
+    const uint32_t g_box[3] = {64, 128, 1};
+    XFB_TRY(make_map_nd(&epi.g_map, false, 3, w.g, g_dims, g_strides, g_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
+    epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
+    epi.transpose = transpose;
+    XFB_TRY((run_gemm<128, false, false>(w.x, c, n * c, wcat, c, 0, n, 4 * c, c, n, epi, st,
+                                         true)));
+  } else {
+    xfb::EpiAttProjDirect epi;
     epi.q = w.q;
     epi.k = w.k;
     epi.v = w.v;
@@ -902,7 +1023,7 @@ XFB_API int xfb_grid_self_attention(
     epi.M = static_cast<int>(M);
     epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
     epi.q_bias = nullptr;
-    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, wcat, c, 0, M, 4 * c, c, 1, epi, st)));
+    XFB_TRY((run_gemm<128, false, false>(w.x, c, 0, wcat, c, 0, M, 4 * c, c, 1, epi, st)));
   }
   // 3. attention per batch row; output written back in pair order, gated (x reused)
   {
@@ -991,12 +1112,9 @@ XFB_API int xfb_transition(const void* x, int x_dtype, int64_t rows, int64_t c,
                          static_cast<const bf16*>(mod_scale), static_cast<const bf16*>(mod_shift),
                          nullptr, 0, nullptr, 0, st));
   {
-    xfb::EpiGLU<128> epi;
-    epi.out = w.h;
-    epi.ld_out = hid;
-    epi.M = static_cast<int>(rows);
-    epi.N_out = static_cast<int>(hid);
-    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, w1p, c, 0, rows, 2 * hid, c, 1, epi, st)));
+    xfb::EpiGLU epi;
+    XFB_TRY(make_out_map(&epi.out_map, w.h, false, hid, rows, 1, hid, 0));
+    XFB_TRY((run_gemm<128, false, false>(w.x, c, 0, w1p, c, 0, rows, 2 * hid, c, 1, epi, st)));
   }
   return linear_core(w.h, rows, hid, hid, static_cast<const bf16*>(w2), c, nullptr,
                      static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32,
@@ -1071,7 +1189,7 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
     XFB_CUDA(cudaMemsetAsync(w.v, 0, bytes, st));
   }
   {
-    xfb::EpiAttProj epi;
+    xfb::EpiAttProjDirect epi;
     epi.q = w.q;
     epi.k = w.k;
     epi.v = w.v;
@@ -1085,7 +1203,7 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
     epi.M = static_cast<int>(n);
     epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
     epi.q_bias = q_bias;
-    XFB_TRY((run_gemm<128, 6, false, false>(w.x, c, 0, wcat, c, 0, n, 4 * c, c, 1, epi, st)));
+    XFB_TRY((run_gemm<128, false, false>(w.x, c, 0, wcat, c, 0, n, 4 * c, c, 1, epi, st)));
   }
   {
     xfb::AttnArgs a;

@@ -1,18 +1,28 @@
 // Persistent, warp-specialised bf16 GEMM on tcgen05 for sm_100a.
 //
-//   D[bat][m][n] = sum_k A[bat](m, k) * B[bat](n, k)        (f32 accumulate in TMEM)
+//   D[bat][m][n] = sum_k A[bat](m, k) * B[bat or 0](n, k)     (f32 accumulate in TMEM)
 //
 // A and B are read by TMA into 128-byte-swizzled shared-memory stages.  Each
-// operand is either K-major (K contiguous in global memory, e.g. activations
-// [rows][K] and nn.Linear weights [out][in]) or MN-major (M/N contiguous, the
-// layout the incoming triangle contraction reads its operands in).
+// operand is K-major (K contiguous: activations [rows][K], nn.Linear weights
+// [out][in]) or MN-major (M/N contiguous: the incoming triangle contraction).
+// With `b_shared` the B operand is the same for every batch index — used to
+// run the K = c projections "batched over pair rows" so that no output tile
+// straddles two rows of the pair.
 //
-// Warp roles (192 threads, one CTA per SM):
-//   warps 0-3  epilogue: TMEM lane quarter w, one accumulator row per thread
-//   warp 4     TMA producer (one elected lane)
-//   warp 5     TMEM allocator + MMA issuer (one elected lane)
+// Warp roles (320 threads, one CTA per SM):
+//   warps 0-7  epilogue: warp w reads TMEM lane quarter w%4 and column half w/4
+//   warp 8     TMA producer (one elected lane): A/B stages + the epilogue's
+//              auxiliary input tile (e.g. the output gate), double-buffered
+//   warp 9     TMEM allocator + MMA issuer (one elected lane)
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the epilogue
-// of tile i overlaps the main loop of tile i+1.
+// of tile i overlaps the main loop of tile i+1.  Epilogues stage their output
+// tile in shared memory and one thread writes it with TMA bulk stores (or a
+// TMA reduce-add into an f32 residual stream), so global traffic is in full
+// lines regardless of the output layout.
+//
+// Epilogue protocol (all 256 epilogue threads, one call per tile):
+//   Epi::compute(ctx)  TMEM -> registers -> math -> staging buffer
+//   Epi::store(ctx)    (one thread) bulk stores from the staging buffer
 #pragma once
 
 #include "common.cuh"
@@ -21,49 +31,66 @@ namespace xfb {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiThreads = 256;
+constexpr int kGemmThreads = kGemmEpiThreads + 64;
+constexpr int kGemmProducerWarp = 8;
+constexpr int kGemmMmaWarp = 9;
 
 struct GemmShape {
   int M, N, K, batch;
   int m_tiles, n_tiles, k_blocks;
+  int b_shared;  // 1: B has no batch dimension
 };
 
-// What an epilogue functor sees for one accumulator row of one tile.
-struct EpiRow {
-  int bat;         // batch index
-  int m0, n0;      // tile origin
-  int row;         // global row index (m0 + lane row); may be >= M for tail tiles
-  uint32_t tmem;   // TMEM address of column 0 of this thread's accumulator row
+// What an epilogue sees for its share of one tile.
+struct EpiCtx {
+  int bat;            // batch index
+  int m0, n0;         // tile origin
+  int row;            // row inside the tile (0..127) = TMEM lane
+  int half;           // column half (0/1) handled by this thread
+  uint32_t tmem;      // TMEM address of tile column 0 in this thread's lane quarter
+  uint8_t* staging;   // staging buffer of this tile
+  const uint8_t* aux; // auxiliary input tile (nullptr when the epilogue has none)
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, class Epi>
 struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarrierOffset = STAGES * kStageBytes;
-  // full[S], empty[S], tfull[2], tempty[2], tmem slot, abort flag
-  static constexpr int kTotal = kBarrierOffset + (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kAuxStride = ((Epi::kAuxBytes + 1023) / 1024) * 1024;
+  static constexpr int kStagingStride = ((Epi::kStagingBytes + 1023) / 1024) * 1024;
+  static constexpr int kAuxOff = STAGES * kStageBytes;
+  static constexpr int kStagingOff = kAuxOff + 2 * kAuxStride;
+  static constexpr int kBarOff = kStagingOff + Epi::kStagingBufs * kStagingStride;
+  // full[S], empty[S], tfull[2], tempty[2], aux_full[2], aux_empty[2]
+  static constexpr int kNumBars = 2 * STAGES + 8;
+  static constexpr int kTotal = kBarOff + kNumBars * 8 + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;  // slack for 1024-byte alignment
+  static_assert(kLaunchBytes <= 232448, "GEMM shared memory exceeds 227 KB");
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, GemmShape shape, Epi epi) {
+                     const __grid_constant__ CUtensorMap tmB, GemmShape shape,
+                     const __grid_constant__ Epi epi) {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128, 192 or 256");
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, Epi>;
   constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256 : 512;
   constexpr uint32_t kIdesc = idesc_bf16(kGemmBM, BN, A_MN, B_MN);
+  constexpr bool kAux = Epi::kAuxBytes > 0;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* aux_full = tempty + 2;
+  uint64_t* aux_empty = aux_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -76,16 +103,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], kGemmEpiThreads);
+      mbar_init(&aux_full[b], 1);
+      mbar_init(&aux_empty[b], kGemmEpiThreads);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kGemmMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kGemmProducerWarp && lane == 0) {
     tma_prefetch(&tmA);
     tma_prefetch(&tmB);
   }
@@ -97,16 +126,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int tiles_per_batch = shape.m_tiles * shape.n_tiles;
   const int total_tiles = tiles_per_batch * shape.batch;
 
-  if (warp == 4) {
+  if (warp == kGemmProducerWarp) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
         const int bat = tile / tiles_per_batch;
         const int rem = tile - bat * tiles_per_batch;
         const int m0 = (rem / shape.n_tiles) * kGemmBM;
         const int n0 = (rem % shape.n_tiles) * BN;
+        const int bb = shape.b_shared ? 0 : bat;
+        if constexpr (kAux) {
+          if (!mbar_wait(&aux_empty[acc], acc_phase ^ 1, kErrWaitProducer, abort_flag)) break;
+          mbar_arrive_expect_tx(&aux_full[acc], Epi::kAuxBytes);
+          epi.load_aux(smem + L::kAuxOff + acc * L::kAuxStride, &aux_full[acc], bat, m0, n0);
+        }
         for (int kb = 0; kb < shape.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitProducer, abort_flag)) break;
           uint8_t* sA = smem + stage * L::kStageBytes;
@@ -122,18 +159,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if constexpr (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_3d(sB + c * 8192, &tmB, &full[stage], n0 + 64 * c, k0, bat);
+              tma_load_3d(sB + c * 8192, &tmB, &full[stage], n0 + 64 * c, k0, bb);
           } else {
-            tma_load_3d(sB, &tmB, &full[stage], k0, n0, bat);
+            tma_load_3d(sB, &tmB, &full[stage], k0, n0, bb);
           }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kGemmMmaWarp) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       int stage = 0;
@@ -176,45 +217,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue warps 0-3
+    // ------------------------------------------------ epilogue warps 0-7
+    const bool leader = threadIdx.x == 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+    int iter = 0;
+    EpiCtx ctx;
+    ctx.row = (warp & 3) * 32 + lane;
+    ctx.half = warp >> 2;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
       const int bat = tile / tiles_per_batch;
       const int rem = tile - bat * tiles_per_batch;
-      const int m0 = (rem / shape.n_tiles) * kGemmBM;
-      const int n0 = (rem % shape.n_tiles) * BN;
-      if (!mbar_wait(&tfull[acc], acc_phase, kErrWaitEpilogue, abort_flag)) break;
+      ctx.bat = bat;
+      ctx.m0 = (rem / shape.n_tiles) * kGemmBM;
+      ctx.n0 = (rem % shape.n_tiles) * BN;
+      // Every epilogue thread runs every tile and every barrier: a wait that gave
+      // up (the CTA is aborting) skips the work but not the named barriers.
+      bool ok = mbar_wait(&tfull[acc], acc_phase, kErrWaitEpilogue, abort_flag);
+      if constexpr (kAux) {
+        ok = mbar_wait(&aux_full[acc], acc_phase, kErrWaitEpilogue, abort_flag) && ok;
+      }
       tc_fence_after();
-      EpiRow r;
-      r.bat = bat;
-      r.m0 = m0;
-      r.n0 = n0;
-      r.row = m0 + warp * 32 + lane;
-      r.tmem = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + acc * BN;
-      epi(r);
+      ctx.tmem = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + acc * BN;
+      ctx.staging = smem + L::kStagingOff + (iter % Epi::kStagingBufs) * L::kStagingStride;
+      ctx.aux = kAux ? smem + L::kAuxOff + acc * L::kAuxStride : nullptr;
+      if constexpr (Epi::kStagingBytes > 0) {
+        // the bulk store that last read this staging buffer must be done reading
+        if (leader) bulk_wait_read<Epi::kStagingBufs - 1>();
+        named_barrier(1, kGemmEpiThreads);
+      }
+      if (ok) epi.compute(ctx);
+      fence_async_smem();
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if constexpr (kAux) mbar_arrive(&aux_empty[acc]);
+      if constexpr (Epi::kStagingBytes > 0) {
+        named_barrier(1, kGemmEpiThreads);
+        if (leader && ok && !*abort_flag) {
+          epi.store(ctx);
+          bulk_commit();
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
+    if constexpr (Epi::kStagingBytes > 0) {
+      if (leader) bulk_wait<0>();
+    }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kGemmMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
-// ====================================================================== epilogues
-//
-// Each functor is called once per accumulator row by all 128 epilogue threads.
-// TMEM loads are warp-collective, so every thread loads even when its row is
-// past M; only the global stores are guarded.
+// ====================================================================== epilogue helpers
 
 __device__ __forceinline__ void store16_bf16(__nv_bfloat16* dst, const float (&v)[16]) {
   uint4 a, b;
@@ -230,41 +292,178 @@ __device__ __forceinline__ void store16_bf16(__nv_bfloat16* dst, const float (&v
   reinterpret_cast<uint4*>(dst)[1] = b;
 }
 
-__device__ __forceinline__ void load16_bf16(const __nv_bfloat16* src, float (&v)[16]) {
-  const uint4 a = reinterpret_cast<const uint4*>(src)[0];
-  const uint4 b = reinterpret_cast<const uint4*>(src)[1];
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+__device__ __forceinline__ void unpack8_bf16(const uint4 w, float* v) {
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(ww[i] << 16);
+    v[2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u);
   }
 }
 
-// out[bat][row][col] (=|+=) bf16(acc + bias) [* gate, rounded to bf16]
-// The projection result is a bf16 tensor in the autocast reference, hence the
-// rounding before the gate product and before the f32 residual add.
+// Address of 16-byte chunk `chunk` (0..7) of row `row` in a [rows][128 B] tile
+// written / read by TMA with the 128-byte swizzle (base 1024-byte aligned).
+__device__ __forceinline__ uint8_t* sw128_chunk(uint8_t* base, int row, int chunk) {
+  return base + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+__device__ __forceinline__ const uint8_t* sw128_chunk(const uint8_t* base, int row, int chunk) {
+  return base + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
+// Same for [rows][64 B] tiles with the 64-byte swizzle (base 512-byte aligned).
+__device__ __forceinline__ uint8_t* sw64_chunk(uint8_t* base, int row, int chunk) {
+  return base + row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
+}
+
+// Stores 32 floats as bf16 into four consecutive swizzled 16-byte chunks.
+__device__ __forceinline__ void stage32_bf16_sw128(uint8_t* base, int row, int chunk0,
+                                                   const float* v) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+    w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+    w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+    w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(sw128_chunk(base, row, chunk0 + c)) = w;
+  }
+}
+
+// ====================================================================== epilogues
+
+// Plain output through TMA: out (f32 or bf16) [bat][m][n] = bf16(acc + bias),
+// stored, or added into an f32 tensor with a TMA reduce-add (the residual
+// update x += op(x)).  The output map is 3-D {N, M, batch} with a box of
+// {32 f32 | 64 bf16, 128, 1} and the 128-byte swizzle.
+template <int BN, bool OUT_F32>
+struct EpiOut {
+  static constexpr int kColsPerBox = OUT_F32 ? 32 : 64;
+  static constexpr int kStagingBytes = 128 * BN * (OUT_F32 ? 4 : 2);
+  static constexpr int kStagingBufs = 1;
+  static constexpr int kAuxBytes = 0;
+  CUtensorMap out_map;
+  const float* bias;   // [N] or null
+  int accumulate;      // TMA reduce-add instead of store (f32 only)
+
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+
+  __device__ void compute(const EpiCtx& c) const {
+    constexpr int kHalf = BN / 2;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kHalf; c0 += 16) {
+      const int col = c.half * kHalf + c0;
+      float v[16];
+      tmem_ld16(c.tmem + col, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float b = bias ? bias[c.n0 + col + i] : 0.f;
+        v[i] = bf16r(v[i] + b);
+      }
+      write(c, col, v);
+    }
+  }
+
+  __device__ __forceinline__ void write(const EpiCtx& c, int col, const float (&v)[16]) const {
+    uint8_t* box = c.staging + (col / kColsPerBox) * (128 * 128);
+    const int inbox = col % kColsPerBox;
+    if constexpr (OUT_F32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4*>(sw128_chunk(box, c.row, inbox / 4 + q)) =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+        w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+        w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+        w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+        *reinterpret_cast<uint4*>(sw128_chunk(box, c.row, inbox / 8 + q)) = w;
+      }
+    }
+  }
+
+  __device__ void store(const EpiCtx& c) const {
+#pragma unroll
+    for (int b = 0; b < BN / kColsPerBox; ++b) {
+      const uint8_t* src = c.staging + b * (128 * 128);
+      if (OUT_F32 && accumulate) {
+        tma_reduce_add_3d(&out_map, src, c.n0 + b * kColsPerBox, c.m0, c.bat);
+      } else {
+        tma_store_3d(&out_map, src, c.n0 + b * kColsPerBox, c.m0, c.bat);
+      }
+    }
+  }
+};
+
+// EpiOut with an output gate [M][N] bf16 (already squashed) read through the
+// auxiliary TMA ring: out = bf16(bf16(acc + bias) * gate).  Gate map 3-D
+// {N, M, 1}, box {64, 128, 1}, 128-byte swizzle.
+template <int BN, bool OUT_F32>
+struct EpiOutGated : EpiOut<BN, OUT_F32> {
+  static constexpr int kAuxBytes = 128 * BN * 2;
+  CUtensorMap gate_map;
+
+  __device__ void load_aux(void* dst, uint64_t* bar, int bat, int m0, int n0) const {
+#pragma unroll
+    for (int b = 0; b < BN / 64; ++b)
+      tma_load_3d(static_cast<uint8_t*>(dst) + b * 16384, &gate_map, bar, n0 + 64 * b, m0, bat);
+  }
+
+  __device__ void compute(const EpiCtx& c) const {
+    constexpr int kHalf = BN / 2;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kHalf; c0 += 16) {
+      const int col = c.half * kHalf + c0;
+      float v[16], g[16];
+      tmem_ld16(c.tmem + col, v);
+      const uint8_t* gbox = c.aux + (col / 64) * 16384;
+      unpack8_bf16(*reinterpret_cast<const uint4*>(sw128_chunk(gbox, c.row, (col % 64) / 8)), g);
+      unpack8_bf16(*reinterpret_cast<const uint4*>(sw128_chunk(gbox, c.row, (col % 64) / 8 + 1)),
+                   g + 8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float b = this->bias ? this->bias[c.n0 + col + i] : 0.f;
+        v[i] = bf16r(bf16r(v[i] + b) * g[i]);
+      }
+      this->write(c, col, v);
+    }
+  }
+};
+
+// Direct per-thread stores (no staging): out [bat][m][ld] bf16 or f32.  Used by
+// the batched contraction (whose rows are 512-byte contiguous runs) and by odd
+// shapes the TMA layouts do not cover.
 template <int BN>
-struct EpiLinear {
+struct EpiDirect {
+  static constexpr int kStagingBytes = 0;
+  static constexpr int kStagingBufs = 1;
+  static constexpr int kAuxBytes = 0;
   void* out;
   int64_t ld_out;
   int64_t bstride_out;
-  int out_f32;       // 1: f32 output, 0: bf16 output
-  int accumulate;    // 1: out (f32) += value
-  const float* bias;          // [N] or null
-  const __nv_bfloat16* gate;  // [M][ld_gate] (already squashed) or null
+  int out_f32;
+  int accumulate;
+  const float* bias;
+  const __nv_bfloat16* gate;
   int64_t ld_gate;
   int M, N;
 
-  __device__ void operator()(const EpiRow& r) const {
-    const bool row_ok = r.row < M;
-    const int64_t row_off = r.bat * bstride_out + static_cast<int64_t>(r.row) * ld_out;
-    const __nv_bfloat16* grow = gate ? gate + static_cast<int64_t>(r.row) * ld_gate : nullptr;
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+  __device__ void store(const EpiCtx&) const {}
+
+  __device__ void compute(const EpiCtx& c) const {
+    constexpr int kHalf = BN / 2;
+    const int row = c.m0 + c.row;
+    const bool row_ok = row < M;
+    const int64_t row_off = c.bat * bstride_out + static_cast<int64_t>(row) * ld_out;
+    const __nv_bfloat16* grow = gate ? gate + static_cast<int64_t>(row) * ld_gate : nullptr;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
+    for (int c0 = 0; c0 < kHalf; c0 += 16) {
       float v[16];
-      tmem_ld16(r.tmem + c0, v);
-      const int col = r.n0 + c0;
+      tmem_ld16(c.tmem + c.half * kHalf + c0, v);
+      const int col = c.n0 + c.half * kHalf + c0;
       if (!row_ok || col >= N) continue;
       const bool full = col + 16 <= N;
 #pragma unroll
@@ -274,16 +473,11 @@ struct EpiLinear {
         v[i] = bf16r(x);
       }
       if (grow != nullptr) {
-        float g[16];
-        if (full) {
-          load16_bf16(grow + col, g);
-        } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            g[i] = (col + i < N) ? __bfloat162float(grow[col + i]) : 0.f;
+        for (int i = 0; i < 16; ++i) {
+          const float g = (full || col + i < N) ? __bfloat162float(grow[col + i]) : 0.f;
+          v[i] = bf16r(v[i] * g);
         }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = bf16r(v[i] * g[i]);
       }
       if (out_f32) {
         float* orow = reinterpret_cast<float*>(out) + row_off;
@@ -320,106 +514,168 @@ struct EpiLinear {
   }
 };
 
-// Gated linear unit: the packed weight places, in every BN-wide tile, BN/2 gate
-// units followed by the BN/2 value units of the same output columns.
-//   out[row][n0/2 + j] = bf16( bf16(silu(bf16(gate_j))) * bf16(value_j) )
-template <int BN>
+// Gated linear unit.  The packed weight places, in every 128-wide tile, 64 gate
+// units followed by the 64 value units of the same output columns.
+//   h[row][n0/2 + j] = bf16( silu(gate_j) * value_j )
+// Output map 3-D {hidden, M, 1}, box {64, 128, 1}, 128-byte swizzle.
 struct EpiGLU {
-  __nv_bfloat16* out;
-  int64_t ld_out;
-  int M, N_out;  // N_out = hidden width (half the packed weight rows)
+  static constexpr int kStagingBytes = 128 * 64 * 2;
+  static constexpr int kStagingBufs = 2;
+  static constexpr int kAuxBytes = 0;
+  CUtensorMap out_map;
 
-  __device__ void operator()(const EpiRow& r) const {
-    const bool row_ok = r.row < M;
-    __nv_bfloat16* orow = out + static_cast<int64_t>(r.row) * ld_out;
-    const int ocol0 = r.n0 / 2;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-      float a[16], b[16];
-      tmem_ld16(r.tmem + c0, a);
-      tmem_ld16(r.tmem + BN / 2 + c0, b);
-      const int col = ocol0 + c0;
-      if (!row_ok || col >= N_out) continue;
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+
+  __device__ void compute(const EpiCtx& c) const {
+    float a[32], b[32];
+    tmem_ld32(c.tmem + c.half * 32, a);
+    tmem_ld32(c.tmem + 64 + c.half * 32, b);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float g = bf16r(a[i]);
-        const float act = bf16r(g * sigmoidf_stable(g));
-        a[i] = bf16r(act * bf16r(b[i]));
-      }
-      if (col + 16 <= N_out) {
-        store16_bf16(orow + col, a);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (col + i < N_out) orow[col + i] = __float2bfloat16_rn(a[i]);
-      }
-    }
+    for (int i = 0; i < 32; ++i) a[i] = a[i] * sigmoid_fast(a[i]) * b[i];
+    stage32_bf16_sw128(c.staging, c.row, c.half * 4, a);
+  }
+
+  __device__ void store(const EpiCtx& c) const {
+    tma_store_3d(&out_map, c.staging, c.n0 / 2, c.m0, c.bat);
   }
 };
 
-// Triangle-multiplication input projection.  Packed weight rows per 128-wide
-// tile t < n_proj_tiles: 64 projection channels [64t, 64t+64) then the 64 gate
-// channels with the same indices; the last tile holds the c output-gate rows.
-//   p_ch = bf16( bf16(bf16(proj_ch) * mask) * bf16(sigmoid(bf16(gate_ch))) )
-//   channel 2c -> a[c][i][j], channel 2c+1 -> b[c][i][j]   (a, b row pitch `pitch`)
-//   g[pos][c'] = bf16(sigmoid(bf16(x . w_gating[c'])))
+// Triangle-multiplication input projection, batched over pair rows i (bat) with
+// tiles of 128 columns j.  Packed weight rows per 128-wide tile t < n_proj_tiles:
+// 64 projection channels [64t, 64t+64) then the 64 gate channels of the same
+// indices; the last tile holds the c output-gate rows.
+//   p_ch = proj_ch * mask[i][j] * sigmoid(gate_ch)
+//   channel 2c' -> a[c'][i][j], channel 2c'+1 -> b[c'][i][j]   (a, b: [c][n][pitch])
+//   g[i][j][c'] = sigmoid(x . w_gating[c'])
+// a / b maps: 3-D {n (j), n (i), c}, box {128, 1, 32}, no swizzle;
+// g map: 3-D {c, n (j), n (i)}, box {64, 128, 1}, 128-byte swizzle.
 struct EpiTriProj {
-  __nv_bfloat16* a;
-  __nv_bfloat16* b;
-  __nv_bfloat16* g;
-  const float* mask;  // [n][n] or nullptr
-  int64_t chan_stride;  // elements between channels of a / b (n * pitch)
-  int n, pitch, c;      // pair side, padded row pitch of a/b, channels
-  int M;                // n * n
-  int n_proj_tiles;     // 2c / 64
+  static constexpr int kStagingBytes = 32768;
+  static constexpr int kStagingBufs = 2;
+  static constexpr int kAuxBytes = 0;
+  CUtensorMap a_map, b_map, g_map;
+  const float* mask;  // [n][n] or null
+  int n, n_proj_tiles, c;
 
-  __device__ void operator()(const EpiRow& r) const {
-    const bool row_ok = r.row < M;
-    const int tile = r.n0 / 128;
-    const int pos = row_ok ? r.row : 0;
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+
+  __device__ void compute(const EpiCtx& c) const {
+    const int tile = c.n0 / 128;
+    const int j = c.m0 + c.row;
     if (tile < n_proj_tiles) {
-      const int i = pos / n;
-      const int j = pos - i * n;
-      const float mval = (mask != nullptr && row_ok) ? mask[pos] : 1.f;
-      const int64_t poff = static_cast<int64_t>(i) * pitch + j;
-#pragma unroll 1
-      for (int c0 = 0; c0 < 64; c0 += 16) {
-        float pv[16], gv[16];
-        tmem_ld16(r.tmem + c0, pv);
-        tmem_ld16(r.tmem + 64 + c0, gv);
-        if (!row_ok) continue;
+      float mval = 1.f;
+      if (mask != nullptr && j < n) mval = mask[static_cast<int64_t>(c.bat) * n + j];
+      float pv[32], gv[32];
+      tmem_ld32(c.tmem + c.half * 32, pv);
+      tmem_ld32(c.tmem + 64 + c.half * 32, gv);
+      __nv_bfloat16* sa = reinterpret_cast<__nv_bfloat16*>(c.staging);
+      __nv_bfloat16* sb = sa + 32 * 128;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const int ch = tile * 64 + c0 + q;
-          const float p = bf16r(bf16r(pv[q]) * mval);
-          const float s = bf16r(sigmoidf_stable(bf16r(gv[q])));
-          const __nv_bfloat16 val = __float2bfloat16_rn(p * s);
-          __nv_bfloat16* dst = ((ch & 1) ? b : a) + (ch >> 1) * chan_stride + poff;
-          *dst = val;
-        }
+      for (int q = 0; q < 32; q += 2) {
+        const int ch = c.half * 16 + q / 2;  // local a / b channel
+        sa[ch * 128 + c.row] = __float2bfloat16_rn(pv[q] * mval * sigmoid_fast(gv[q]));
+        sb[ch * 128 + c.row] = __float2bfloat16_rn(pv[q + 1] * mval * sigmoid_fast(gv[q + 1]));
       }
     } else {
-      __nv_bfloat16* grow = g + static_cast<int64_t>(pos) * c;
-#pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 16) {
-        float v[16];
-        tmem_ld16(r.tmem + c0, v);
-        if (!row_ok || c0 >= c) continue;
+      float v[32];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = bf16r(sigmoidf_stable(bf16r(v[q])));
-        store16_bf16(grow + c0, v);
+      for (int h = 0; h < 2; ++h) {
+        tmem_ld32(c.tmem + c.half * 64 + h * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = sigmoid_fast(v[i]);
+        stage32_bf16_sw128(c.staging + c.half * 16384, c.row, h * 4, v);
+      }
+    }
+  }
+
+  __device__ void store(const EpiCtx& c) const {
+    const int tile = c.n0 / 128;
+    if (tile < n_proj_tiles) {
+      tma_store_3d(&a_map, c.staging, c.m0, c.bat, tile * 32);
+      tma_store_3d(&b_map, c.staging + 8192, c.m0, c.bat, tile * 32);
+    } else {
+      tma_store_3d(&g_map, c.staging, 0, c.m0, c.bat);
+      if (this->c > 64) tma_store_3d(&g_map, c.staging + 16384, 64, c.m0, c.bat);
+    }
+  }
+};
+
+// Triangle-attention input projection for c = 128, 4 heads of 32, batched over
+// pair rows i with tiles of 128 columns j.  Packed weight rows: q, k, v, gate
+// (128 each).  Position (i, j) is batch row r = i, token t = j (starting node)
+// or r = j, t = i (ending node).
+//   q/k/v[r][h][t][0..31]  (q = bf16(acc) * q_scale before its own rounding)
+//   g[i][j][col] = sigmoid(x . w_gate[col])
+// q/k/v maps: starting 3-D {32, n (t), n*4 (r*4+h)}, box {32, 128, 1};
+// ending 4-D {32, n (t), 4 (h), n (r)}, box {32, 1, 1, 128}; 64-byte swizzle.
+struct EpiAttProjTma {
+  static constexpr int kStagingBytes = 32768;
+  static constexpr int kStagingBufs = 2;
+  static constexpr int kAuxBytes = 0;
+  CUtensorMap qkv_map[3];
+  CUtensorMap g_map;
+  float q_scale;
+  int transpose;
+
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+
+  __device__ void compute(const EpiCtx& c) const {
+    const int which = c.n0 / 128;  // 0 q, 1 k, 2 v, 3 gate
+    float v[32];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      tmem_ld32(c.tmem + c.half * 64 + h2 * 32, v);
+      if (which == 3) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = sigmoid_fast(v[i]);
+        stage32_bf16_sw128(c.staging + c.half * 16384, c.row, h2 * 4, v);
+      } else {
+        if (which == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = bf16r(v[i]) * q_scale;
+        }
+        uint8_t* head = c.staging + (c.half * 2 + h2) * 8192;  // [128 t][64 B]
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+          w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+          w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+          w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+          *reinterpret_cast<uint4*>(sw64_chunk(head, c.row, q)) = w;
+        }
+      }
+    }
+  }
+
+  __device__ void store(const EpiCtx& c) const {
+    const int which = c.n0 / 128;
+    if (which == 3) {
+      tma_store_3d(&g_map, c.staging, 0, c.m0, c.bat);
+      tma_store_3d(&g_map, c.staging + 16384, 64, c.m0, c.bat);
+      return;
+    }
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint8_t* src = c.staging + h * 8192;
+      if (!transpose) {
+        tma_store_3d(&qkv_map[which], src, 0, c.m0, c.bat * 4 + h);
+      } else {
+        tma_store_4d(&qkv_map[which], src, 0, c.bat, h, c.m0);
       }
     }
   }
 };
 
-// Triangle-attention input projection.  Packed weight rows: q (c), k (c), v (c),
-// gate (c), in 128-wide tiles.  Position pos = i*n + j belongs to batch row
-// b = i, token t = j (starting node) or b = j, t = i (ending node).
-//   q/k/v[b][h][t][dd] (head pitch dp >= d, padding left untouched)
-//   q is scaled by d^-0.5 after rounding, as the reference scales the bf16 q.
-//   g[pos][col] = bf16(sigmoid(bf16(x . w_gate[col])))
-struct EpiAttProj {
+// Attention input projection with direct stores, any c / head layout: the
+// single-track and diffusion SelfAttention (one batch row) and the c = 64
+// triangle attention.  Flat rows: position pos = i*n + j with batch row
+// i (starting) or j (ending); q/k/v[r][h][t][dd] with head pitch dp >= d
+// (padding left as is), q = bf16(bf16(acc + q_bias) * q_scale).
+struct EpiAttProjDirect {
+  static constexpr int kStagingBytes = 0;
+  static constexpr int kStagingBufs = 1;
+  static constexpr int kAuxBytes = 0;
   __nv_bfloat16* q;
   __nv_bfloat16* k;
   __nv_bfloat16* v;
@@ -428,26 +684,30 @@ struct EpiAttProj {
   int transpose;
   int M;
   float q_scale;
-  const float* q_bias;  // [c] or null: bias of the q projection (SelfAttention)
+  const float* q_bias;
 
-  __device__ void operator()(const EpiRow& r) const {
-    const bool row_ok = r.row < M;
-    const int pos = row_ok ? r.row : 0;
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+  __device__ void store(const EpiCtx&) const {}
+
+  __device__ void compute(const EpiCtx& cx) const {
+    const int row = cx.m0 + cx.row;
+    const bool row_ok = row < M;
+    const int pos = row_ok ? row : 0;
     const int i = pos / n;
     const int j = pos - i * n;
     const int bidx = transpose ? j : i;
     const int tok = transpose ? i : j;
 #pragma unroll 1
-    for (int c0 = 0; c0 < 128; c0 += 16) {
+    for (int c0 = 0; c0 < 64; c0 += 16) {
       float x[16];
-      tmem_ld16(r.tmem + c0, x);
-      const int colg = r.n0 + c0;  // column of the packed [q|k|v|gate] output
-      const int which = colg / c;  // 0 q, 1 k, 2 v, 3 gate
+      tmem_ld16(cx.tmem + cx.half * 64 + c0, x);
+      const int colg = cx.n0 + cx.half * 64 + c0;
+      const int which = colg / c;
       const int cc = colg - which * c;
       if (!row_ok || which > 3) continue;
       if (which == 3) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) x[e] = bf16r(sigmoidf_stable(bf16r(x[e])));
+        for (int e = 0; e < 16; ++e) x[e] = sigmoid_fast(x[e]);
         store16_bf16(g + static_cast<int64_t>(pos) * c + cc, x);
         continue;
       }
@@ -456,26 +716,16 @@ struct EpiAttProj {
       for (int e = 0; e < 16; ++e) {
         if (which == 0) {
           const float qb = q_bias ? q_bias[cc + e] : 0.f;
-          x[e] = bf16r(bf16r(x[e] + qb) * q_scale);
-        } else {
-          x[e] = bf16r(x[e]);
+          x[e] = bf16r(x[e] + qb) * q_scale;
         }
       }
-      if (d % 16 == 0) {
-        const int h = cc / d;
-        const int dd = cc - h * d;
-        __nv_bfloat16* dst =
-            base + ((static_cast<int64_t>(bidx) * heads + h) * n + tok) * dp + dd;
-        store16_bf16(dst, x);
-      } else {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int col = cc + e;
-          const int h = col / d;
-          const int dd = col - h * d;
-          base[((static_cast<int64_t>(bidx) * heads + h) * n + tok) * dp + dd] =
-              __float2bfloat16_rn(x[e]);
-        }
+      for (int e = 0; e < 16; ++e) {
+        const int col = cc + e;
+        const int h = col / d;
+        const int dd = col - h * d;
+        base[((static_cast<int64_t>(bidx) * heads + h) * n + tok) * dp + dd] =
+            __float2bfloat16_rn(x[e]);
       }
     }
   }

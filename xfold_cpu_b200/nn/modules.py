@@ -317,9 +317,13 @@ class DiffusionTransformer(nn.Module):
     def pair_logits(self, pair_cond: torch.Tensor) -> list[torch.Tensor]:
         """[super_block][j] -> [H, N, N] bf16 logits; cached per pair_cond version
         like the reference's InputCache (:256-265)."""
-        key = (pair_cond.data_ptr(), pair_cond._version, tuple(pair_cond.shape),
-               tuple((p.weight.data_ptr(), p.weight._version) for p in self.pair_logits_projection))
-        if key != self._logits_key:
+        try:
+            key = (pair_cond.data_ptr(), pair_cond._version, tuple(pair_cond.shape),
+                   tuple((p.weight.data_ptr(), p.weight._version)
+                         for p in self.pair_logits_projection))
+        except RuntimeError:  # inference tensors carry no version counter: no reuse
+            key = None
+        if key is None or key != self._logits_key:
             ln = self.pair_input_layer_norm
             logits = []
             for proj in self.pair_logits_projection:
