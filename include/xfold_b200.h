@@ -93,6 +93,24 @@ XFB_API int xfb_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t col
 XFB_API int xfb_linear(const void* x, int64_t m, int64_t k, const void* weight, int64_t n,
                        const float* bias, void* y, int y_dtype, int accumulate, void* stream);
 
+/* Allocation-free variant of xfb_gated_linear_unit for callers that cannot
+ * hand this library device memory: code that runs where cudaMalloc is not
+ * allowed or not wanted (a host runtime that owns every device allocation
+ * through its own pool and budget, or a service that must keep its footprint
+ * fixed after start-up).  It has no counterpart in the reference.
+ * `weight` is the unpacked transition1.weight [2n][k] (bf16); the packed copy
+ * goes to a fixed scratch array built into the library (8 MiB per device,
+ * held from load until exit), so 2*n*k must not exceed
+ * XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS (larger weights are rejected with
+ * XFB_ERR_INVALID).  No cudaMalloc / cudaFree happens.  The first call on a
+ * device looks up the scratch's device address; make that first call before
+ * any stream capture.  All calls share the one scratch array, so calls that
+ * overlap on the GPU (other streams, other threads) race; each call rewrites
+ * every scratch element it reads. */
+#define XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS (4ll * 1024 * 1024)
+XFB_API int xfb_gated_linear_unit_noalloc(const void* x, int64_t m, int64_t k, const void* weight,
+                                          int64_t n, void* y, void* stream);
+
 /* Batched GEMM, bf16 in, f32 accumulate: c[b][i][j] = sum_k A_b(i, k) B_b(j, k).
  * K-major operands: a [batch][m][k], b [batch][n][k]; MN-major (a_mn_major =
  * b_mn_major = 1): a [batch][k][m], b [batch][k][n].  c [batch][m][n], f32 or bf16.

@@ -38,6 +38,7 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_pack_glu_weight": (_i, [_p, _i, _i64, _i64, _p, _p]),
     "xfb_gated_linear_unit_workspace": (_i64, [_i64, _i64, _i64]),
     "xfb_gated_linear_unit": (_i, [_p, _i64, _i64, _p, _i64, _i, _p, _p, _i64, _p]),
+    "xfb_gated_linear_unit_noalloc": (_i, [_p, _i64, _i64, _p, _i64, _p, _p]),
     "xfb_pack_triangle_weights_bytes": (_i64, [_i64]),
     "xfb_pack_triangle_weights": (_i, [_p, _p, _p, _i, _i64, _p, _p]),
     "xfb_triangle_multiplication_workspace": (_i64, [_i64, _i64]),

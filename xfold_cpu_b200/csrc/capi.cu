@@ -654,6 +654,68 @@ XFB_API int xfb_gated_linear_unit(const void* x, int64_t m, int64_t k, const voi
   return run_gemm<128, false, false>(x, k, 0, w, k, 0, m, 2 * n, k, 1, epi, st);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Scratch of xfb_gated_linear_unit_noalloc: the packed weight is written here
+// instead of into a caller-provided workspace.  It is part of the module, so
+// every device that loads the library holds these 8 MiB until the process exits.
+static __device__ __align__(256) bf16 g_glu_noalloc_scratch[XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS];
+
+bf16* g_glu_noalloc_ptr[kMaxDevices];
+cudaError_t g_glu_noalloc_status[kMaxDevices];
+std::once_flag g_glu_noalloc_once[kMaxDevices];
+
+// Device address of the scratch on the current device.  The host symbol is
+// only a stand-in for the device array, so the address is asked for once per
+// device (on the first call made with that device current) and kept.
+int glu_noalloc_scratch(bf16** out) {
+  int dev;
+  XFB_TRY(current_device(&dev));
+  std::call_once(g_glu_noalloc_once[dev], [dev]() {
+    void* p = nullptr;
+    g_glu_noalloc_status[dev] = cudaGetSymbolAddress(&p, g_glu_noalloc_scratch);
+    g_glu_noalloc_ptr[dev] = static_cast<bf16*>(p);
+  });
+  if (g_glu_noalloc_status[dev] != cudaSuccess || g_glu_noalloc_ptr[dev] == nullptr) {
+    return fail(XFB_ERR_CUDA, std::string("cudaGetSymbolAddress(GLU scratch): ") +
+                                  cudaGetErrorString(g_glu_noalloc_status[dev]));
+  }
+  *out = g_glu_noalloc_ptr[dev];
+  return XFB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+XFB_API int xfb_gated_linear_unit_noalloc(const void* x, int64_t m, int64_t k, const void* weight,
+                                          int64_t n, void* y, void* stream) {
+  XFB_REQUIRE(m >= 0 && k > 0, "GLU expects m >= 0 and k > 0");
+  XFB_REQUIRE(n > 0 && n % 64 == 0, "GLU hidden width must be a positive multiple of 64");
+  XFB_REQUIRE(k % 8 == 0, "GLU input width must be a multiple of 8");
+  XFB_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(y),
+              "GLU pointers must be 16-byte aligned");
+  if (2 * n * k > XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "xfb_gated_linear_unit_noalloc: weight of 2n*k = %lld elements exceeds the fixed "
+             "scratch of %lld elements; use xfb_gated_linear_unit with a workspace",
+             (long long)(2 * n * k), (long long)XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS);
+    return fail(XFB_ERR_INVALID, buf);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bf16* packed = nullptr;
+  XFB_TRY(glu_noalloc_scratch(&packed));
+  // Every row of the packed weight the GEMM reads is rewritten here, so nothing
+  // left from an earlier call is used.
+  XFB_TRY(launch_pack(weight, nullptr, nullptr, nullptr, XFB_BF16, 1, n, k, 2 * n, packed, st));
+  xfb::EpiGLU epi;
+  XFB_TRY(make_out_map(&epi.out_map, y, false, n, m, 1, n, 0));
+  return run_gemm<128, false, false>(x, k, 0, packed, k, 0, m, 2 * n, k, 1, epi, st);
+}
+
 XFB_API int xfb_gemm(const void* a, const void* b, void* c, int64_t batch, int64_t m, int64_t n,
                      int64_t k, int a_mn_major, int b_mn_major, int c_dtype, void* stream) {
   XFB_REQUIRE(batch >= 0 && m >= 0 && n >= 0 && k > 0, "gemm expects batch, m, n >= 0, k > 0");
