@@ -292,7 +292,7 @@ int linear_core(const bf16* x, int64_t m, int64_t k, int64_t ldx, const bf16* w,
 int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t ldx,
                    const float* w, const float* b, double eps, bf16* y, int64_t ldy,
                    const bf16* mod_scale, const bf16* mod_shift, const bf16* wh, int heads,
-                   bf16* head_out, int64_t head_ld, cudaStream_t st) {
+                   bf16* head_out, int64_t head_ld, cudaStream_t st, float head_scale = 1.f) {
   if (rows <= 0) return XFB_OK;
   XFB_REQUIRE(x_dtype == XFB_F32 || x_dtype == XFB_BF16, "LayerNorm input must be f32 or bf16");
   XFB_REQUIRE(heads >= 0 && heads <= 16, "head projection supports at most 16 heads");
@@ -312,6 +312,7 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
   a.heads = heads;
   a.head_out = head_out;
   a.head_ld = head_ld;
+  a.head_scale = head_scale;
   int sms;
   XFB_TRY(sm_count(&sms));
   const int64_t warps = (rows + 0);
@@ -448,26 +449,32 @@ int check_workspace(const Carver& cv, const void* ws, int64_t ws_bytes) {
 
 // ------------------------------------------------------------------ attention launcher
 
-template <int DP, int BMODE>
-int launch_flash(const bf16* q, const bf16* k, const bf16* v, const xfb::AttnArgs& args,
+template <int DP, int BMODE, bool PRE>
+int launch_flash(const bf16* q, const bf16* k, const bf16* v, xfb::AttnArgs args,
                  cudaStream_t st) {
   CUtensorMap tq, tk, tv, tb;
   const CUtensorMapSwizzle swz = DP == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   const int64_t bh = static_cast<int64_t>(args.B) * args.H;
   XFB_TRY(make_map(&tq, q, DP, args.nq, bh, DP * 2, int64_t(args.nq) * DP * 2, DP, 128, swz));
-  XFB_TRY(make_map(&tk, k, DP, args.nk, bh, DP * 2, int64_t(args.nk) * DP * 2, DP, 128, swz));
-  XFB_TRY(make_map(&tv, v, DP, args.nk, bh, DP * 2, int64_t(args.nk) * DP * 2, DP, 128, swz));
+  XFB_TRY(make_map(&tk, k, DP, args.nk, bh, DP * 2, int64_t(args.nk) * DP * 2, DP,
+                   xfb::kAttnBK, swz));
+  XFB_TRY(make_map(&tv, v, DP, args.nk, bh, DP * 2, int64_t(args.nk) * DP * 2, DP,
+                   xfb::kAttnBK, swz));
   if (BMODE == xfb::kBiasTma) {
     const int64_t z = args.bias_batched ? bh : args.H;
-    XFB_TRY(make_map(&tb, args.bias, args.nk, args.nq, z, args.bias_sq * 2, args.bias_sh * 2, 64,
-                     128, CU_TENSOR_MAP_SWIZZLE_128B));
+    XFB_TRY(make_map(&tb, args.bias, args.nk, args.nq, z, args.bias_sq * 2, args.bias_sh * 2,
+                     xfb::kAttnBK, 128, CU_TENSOR_MAP_SWIZZLE_128B));
   } else {
     memset(&tb, 0, sizeof(tb));
   }
+  args.q_tiles = (args.nq + 127) / 128;
   using L = xfb::AttnSmem<DP>;
-  auto kernel = xfb::flash_attn_kernel<DP, BMODE>;
+  auto kernel = xfb::flash_attn_kernel<DP, BMODE, PRE>;
   XFB_TRY(set_smem(kernel, L::kLaunchBytes));
-  dim3 grid(static_cast<unsigned>((args.nq + 127) / 128), static_cast<unsigned>(bh));
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int64_t items = bh * args.q_tiles;
+  const int grid = static_cast<int>(std::min<int64_t>(items, int64_t(sms) * L::kCtasPerSm));
   kernel<<<grid, xfb::kAttnThreads, L::kLaunchBytes, st>>>(tq, tk, tv, tb, args);
   XFB_LAUNCHED();
   return XFB_OK;
@@ -475,11 +482,12 @@ int launch_flash(const bf16* q, const bf16* k, const bf16* v, const xfb::AttnArg
 
 // Picks the bias path: TMA-streamed bf16 tiles when the layout allows it
 // (row stride nk with nk % 8 == 0, contiguous heads, 16-byte aligned), else
-// per-thread global loads.
-int run_flash(int dp, int bias_dtype, const bf16* q, const bf16* k, const bf16* v,
+// per-thread global loads.  `pre`: q and the bias already carry log2(e)
+// (only the TMA bias path takes pre-scaled inputs).
+int run_flash(int dp, int bias_dtype, bool pre, const bf16* q, const bf16* k, const bf16* v,
               const xfb::AttnArgs& args, cudaStream_t st) {
-  XFB_REQUIRE(args.nk <= xfb::AttnSmem<32>::kMaxKeys, "attention supports at most 8192 keys");
-  XFB_REQUIRE(static_cast<int64_t>(args.B) * args.H <= 65535, "attention batch*heads too large");
+  XFB_REQUIRE(static_cast<int64_t>(args.B) * args.H * ((args.nq + 127) / 128) < (1ll << 31),
+              "attention has too many work items");
   int mode = xfb::kBiasGlobalBf16;
   if (args.bias != nullptr) {
     if (bias_dtype == XFB_F32) {
@@ -490,15 +498,35 @@ int run_flash(int dp, int bias_dtype, const bf16* q, const bf16* k, const bf16* 
       mode = xfb::kBiasTma;
     }
   }
-  if (dp == 32) {
-    if (mode == xfb::kBiasTma) return launch_flash<32, xfb::kBiasTma>(q, k, v, args, st);
-    if (mode == xfb::kBiasGlobalF32) return launch_flash<32, xfb::kBiasGlobalF32>(q, k, v, args, st);
-    return launch_flash<32, xfb::kBiasGlobalBf16>(q, k, v, args, st);
+  if (pre) {
+    XFB_REQUIRE(mode == xfb::kBiasTma && dp == 32, "pre-scaled attention needs the TMA bias path");
+    return launch_flash<32, xfb::kBiasTma, true>(q, k, v, args, st);
   }
-  if (mode == xfb::kBiasTma) return launch_flash<64, xfb::kBiasTma>(q, k, v, args, st);
-  if (mode == xfb::kBiasGlobalF32) return launch_flash<64, xfb::kBiasGlobalF32>(q, k, v, args, st);
-  return launch_flash<64, xfb::kBiasGlobalBf16>(q, k, v, args, st);
+  if (dp == 32) {
+    if (mode == xfb::kBiasTma) return launch_flash<32, xfb::kBiasTma, false>(q, k, v, args, st);
+    if (mode == xfb::kBiasGlobalF32)
+      return launch_flash<32, xfb::kBiasGlobalF32, false>(q, k, v, args, st);
+    return launch_flash<32, xfb::kBiasGlobalBf16, false>(q, k, v, args, st);
+  }
+  if (mode == xfb::kBiasTma) return launch_flash<64, xfb::kBiasTma, false>(q, k, v, args, st);
+  if (mode == xfb::kBiasGlobalF32)
+    return launch_flash<64, xfb::kBiasGlobalF32, false>(q, k, v, args, st);
+  return launch_flash<64, xfb::kBiasGlobalBf16, false>(q, k, v, args, st);
 }
+
+// Key mask -> bits, one 32-bit word per 32 keys per row.
+int launch_mask_bits(const void* mask, bool is_float, int64_t rows, int64_t nk, int64_t stride,
+                     uint32_t* out, cudaStream_t st) {
+  const int words = static_cast<int>((nk + 31) / 32);
+  const int64_t total = rows * words;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  xfb::pack_mask_bits_kernel<<<blocks, 256, 0, st>>>(mask, is_float ? 1 : 0, rows,
+                                                     static_cast<int>(nk), stride, out, words);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+int64_t mask_words(int64_t nk) { return (nk + 31) / 32; }
 
 int head_pitch(int64_t d) { return d <= 32 ? 32 : 64; }
 
@@ -547,7 +575,7 @@ XFB_API int xfb_check_device(void) {
     return fail(XFB_ERR_DEVICE, buf);
   }
   cudaFuncAttributes attr;
-  XFB_CUDA(cudaFuncGetAttributes(&attr, xfb::flash_attn_kernel<32, xfb::kBiasTma>));
+  XFB_CUDA(cudaFuncGetAttributes(&attr, xfb::flash_attn_kernel<32, xfb::kBiasTma, true>));
   XFB_TRY(get_encoder());
   return XFB_OK;
 }
@@ -890,6 +918,7 @@ XFB_API int64_t xfb_dot_product_attention_workspace(int64_t B, int64_t H, int64_
                                                     int64_t d) {
   const int64_t dp = head_pitch(d);
   Carver cv{nullptr, 0, 0};
+  cv.take<uint32_t>(B * mask_words(nk));
   cv.take<bf16>(B * H * nq * dp);
   cv.take<bf16>(B * H * nk * dp);
   cv.take<bf16>(B * H * nk * dp);
@@ -921,8 +950,12 @@ XFB_API int xfb_dot_product_attention(const void* q, const void* k, const void* 
   const bf16* kk = static_cast<const bf16*>(k);
   const bf16* vv = static_cast<const bf16*>(v);
   const bool direct = (d == dp) && q_pre_scaled && aligned16(q) && aligned16(k) && aligned16(v);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  const int64_t mask_rows = mask_batched ? B : 1;
+  uint32_t* bits = mask ? cv.take<uint32_t>(mask_rows * mask_words(nk)) : nullptr;
+  if (direct) XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  if (mask) XFB_TRY(launch_mask_bits(mask, mask_dtype == XFB_F32, mask_rows, nk, nk, bits, st));
   if (!direct) {
-    Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
     bf16* q2 = cv.take<bf16>(B * H * nq * dp);
     bf16* k2 = cv.take<bf16>(B * H * nk * dp);
     bf16* v2 = cv.take<bf16>(B * H * nk * dp);
@@ -946,9 +979,8 @@ XFB_API int xfb_dot_product_attention(const void* q, const void* k, const void* 
   a.nq = static_cast<int>(nq);
   a.nk = static_cast<int>(nk);
   a.d = static_cast<int>(d);
-  a.mask = mask;
-  a.mask_is_float = mask_dtype == XFB_F32;
-  a.mask_sb = mask_batched ? nk : 0;
+  a.mask_bits = bits;
+  a.mask_sb = mask_batched ? mask_words(nk) : 0;
   a.bias = bias;
   a.bias_sb = bias_batched ? H * nq * nk : 0;
   a.bias_sh = nq * nk;
@@ -960,7 +992,7 @@ XFB_API int xfb_dot_product_attention(const void* q, const void* k, const void* 
   a.gate = nullptr;
   a.gate_sb = a.gate_sh = a.gate_sq = 0;
   a.bias_batched = bias_batched;
-  return run_flash(dp, bias_dtype, qq, kk, vv, a, st);
+  return run_flash(dp, bias_dtype, false, qq, kk, vv, a, st);
 }
 
 XFB_API int64_t xfb_pack_attention_weights_bytes(int64_t c) { return 4 * c * c * 2; }
@@ -976,6 +1008,7 @@ XFB_API int xfb_pack_attention_weights(const void* q_w, const void* k_w, const v
 namespace {
 struct GsaWs {
   bf16 *x, *bias, *q, *k, *v, *g, *packed;
+  uint32_t* bits;
 };
 void gsa_layout(Carver& cv, int64_t n, int64_t c, int64_t heads, bool need_pack, GsaWs* w) {
   const int64_t dp = head_pitch(c / heads);
@@ -986,6 +1019,7 @@ void gsa_layout(Carver& cv, int64_t n, int64_t c, int64_t heads, bool need_pack,
   w->v = cv.take<bf16>(n * heads * n * dp);
   w->g = cv.take<bf16>(n * n * c);
   w->packed = need_pack ? cv.take<bf16>(4 * c * c) : nullptr;
+  w->bits = cv.take<uint32_t>(n * mask_words(n));
 }
 }  // namespace
 
@@ -1029,10 +1063,14 @@ XFB_API int xfb_grid_self_attention(
     XFB_TRY(launch_pack(q_w, k_w, v_w, gate_w, XFB_BF16, 2, c, c, 4 * c, w.packed, st));
     wcat = w.packed;
   }
+  // Scores in log2 units from the producers (q and bias carry log2(e)) when the
+  // bias can stream through TMA; otherwise the attention kernel scales them.
+  const bool pre = dp == 32 && n % 8 == 0;
+  const float log2e = 1.4426950408889634f;
   // 1. x = LN(pair) and the pair bias (projected before any transpose)
   XFB_TRY(run_layer_norm(pair, pair_dtype, M, c, c, norm_weight, norm_bias, eps, w.x, c, nullptr,
                          nullptr, static_cast<const bf16*>(bias_weight),
-                         static_cast<int>(heads), w.bias, M, st));
+                         static_cast<int>(heads), w.bias, M, st, pre ? log2e : 1.f));
   // 2. q, k, v (head-major per batch row) and the squashed gate
   if (d != dp) {
     const int64_t bytes = n * heads * n * dp * 2;
@@ -1066,7 +1104,7 @@ XFB_API int xfb_grid_self_attention(
     const uint32_t g_box[3] = {64, 128, 1};
     XFB_TRY(make_map_nd(&epi.g_map, false, 3, w.g, g_dims, g_strides, g_box,
                         CU_TENSOR_MAP_SWIZZLE_128B));
-    epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
+    epi.q_scale = (pre ? log2e : 1.f) / std::sqrt(static_cast<float>(d));
     epi.transpose = transpose;
     XFB_TRY((run_gemm<128, false, false>(w.x, c, n * c, wcat, c, 0, n, 4 * c, c, n, epi, st,
                                          true)));
@@ -1083,7 +1121,7 @@ XFB_API int xfb_grid_self_attention(
     epi.dp = dp;
     epi.transpose = transpose;
     epi.M = static_cast<int>(M);
-    epi.q_scale = 1.f / std::sqrt(static_cast<float>(d));
+    epi.q_scale = (pre ? log2e : 1.f) / std::sqrt(static_cast<float>(d));
     epi.q_bias = nullptr;
     XFB_TRY((run_gemm<128, false, false>(w.x, c, 0, wcat, c, 0, M, 4 * c, c, 1, epi, st)));
   }
@@ -1095,9 +1133,9 @@ XFB_API int xfb_grid_self_attention(
     a.nq = static_cast<int>(n);
     a.nk = static_cast<int>(n);
     a.d = static_cast<int>(d);
-    a.mask = mask;
-    a.mask_is_float = 1;
-    a.mask_sb = n;
+    if (mask != nullptr) XFB_TRY(launch_mask_bits(mask, true, n, n, n, w.bits, st));
+    a.mask_bits = mask ? w.bits : nullptr;
+    a.mask_sb = mask_words(n);
     a.bias = w.bias;
     a.bias_sb = 0;
     a.bias_sh = M;
@@ -1116,7 +1154,7 @@ XFB_API int xfb_grid_self_attention(
     a.gate_sb = a.out_sb;
     a.gate_sh = a.out_sh;
     a.gate_sq = a.out_sq;
-    XFB_TRY(run_flash(dp, XFB_BF16, w.q, w.k, w.v, a, st));
+    XFB_TRY(run_flash(dp, XFB_BF16, pre, w.q, w.k, w.v, a, st));
   }
   // 4. output projection (+ residual)
   XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
@@ -1188,6 +1226,7 @@ XFB_API int xfb_transition(const void* x, int x_dtype, int64_t rows, int64_t c,
 namespace {
 struct SaWs {
   bf16 *x, *q, *k, *v, *g, *packed;
+  uint32_t* bits;
 };
 void sa_layout(Carver& cv, int64_t n, int64_t c, int64_t heads, bool need_pack, SaWs* w) {
   const int64_t dp = head_pitch(c / heads);
@@ -1197,6 +1236,7 @@ void sa_layout(Carver& cv, int64_t n, int64_t c, int64_t heads, bool need_pack, 
   w->v = cv.take<bf16>(heads * n * dp);
   w->g = cv.take<bf16>(n * c);
   w->packed = need_pack ? cv.take<bf16>(4 * c * c) : nullptr;
+  w->bits = cv.take<uint32_t>(mask_words(n));
 }
 }  // namespace
 
@@ -1274,8 +1314,8 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
     a.nq = static_cast<int>(n);
     a.nk = static_cast<int>(n);
     a.d = static_cast<int>(d);
-    a.mask = mask;
-    a.mask_is_float = 1;
+    if (mask != nullptr) XFB_TRY(launch_mask_bits(mask, true, 1, n, n, w.bits, st));
+    a.mask_bits = mask ? w.bits : nullptr;
     a.mask_sb = 0;
     a.bias = pair_logits;
     a.bias_sb = 0;
@@ -1290,7 +1330,7 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
     a.gate_sb = 0;
     a.gate_sh = d;
     a.gate_sq = c;
-    XFB_TRY(run_flash(dp, XFB_BF16, w.q, w.k, w.v, a, st));
+    XFB_TRY(run_flash(dp, XFB_BF16, false, w.q, w.k, w.v, a, st));
   }
   return linear_core(w.x, n, c, c, static_cast<const bf16*>(wo), c, nullptr,
                      static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32,

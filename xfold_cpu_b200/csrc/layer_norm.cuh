@@ -58,6 +58,7 @@ struct LnArgs {
   int heads;
   __nv_bfloat16* head_out;         // [H][head_ld]
   int64_t head_ld;
+  float head_scale;                // multiplies the head projection before rounding
 };
 
 // C = 32 * 4 * R channels: each lane holds R groups of 4 consecutive channels.
@@ -191,7 +192,8 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
       const int shift = 5 - __ffs(HP) + 1;  // number of low bits summed away
       if ((lane & ((1 << shift) - 1)) == 0) {
         const int hidx = lane >> shift;
-        if (hidx < a.heads) a.head_out[hidx * a.head_ld + row] = __float2bfloat16_rn(tot);
+        if (hidx < a.heads)
+          a.head_out[hidx * a.head_ld + row] = __float2bfloat16_rn(tot * a.head_scale);
       }
     }
   }
