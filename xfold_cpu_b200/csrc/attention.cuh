@@ -9,11 +9,14 @@
 //                           the bias tile arrives by TMA with K_t / V_t; P is
 //                           written as bf16 into a 128B-swizzled SMEM tile
 //   O   += P_t V_t          tcgen05.mma accumulating in TMEM (V read MN-major)
-// Scores are in log2 units: with PRE, q carries d^-0.5 * log2(e) and the bias
-// log2(e) from their producers; otherwise the kernel multiplies by log2(e).
-// The running reference max m_ref only moves when a tile's max exceeds it by
-// more than 8 (a factor 256), so O in TMEM is rescaled (tcgen05.ld / st)
-// rarely; l and P stay relative to m_ref.
+//   l   += P_t 1            a second MMA against a tile of ones: the row sums of
+//                           the bf16 probabilities, next to O in TMEM
+// With PRE, q carries d^-0.5 * log2(e) and the bias log2(e) from their
+// producers, so scores are in log2 units; otherwise the exponent's FMA scales
+// them by log2(e).  The running reference max m_ref only moves when a tile's
+// max exceeds it by more than 8 (a factor 256), so O and l in TMEM are rescaled
+// (tcgen05.ld / st) rarely.  A fixed share of the exponentials runs as a
+// polynomial on the FMA pipe instead of the MUFU unit (exp2_poly2).
 //
 // Mask semantics follow the reference: a masked key gets the logit -1e9 (so a
 // fully masked row is a uniform average), keys past the sequence end get
@@ -25,9 +28,16 @@
 namespace xfb {
 
 constexpr int kAttnThreads = 192;
-constexpr int kAttnKvStages = 2;
+constexpr int kAttnKvStages = 3;    // K / V ring, freed by the PV MMA
+constexpr int kAttnBiasStages = 2;  // bias ring, freed by the softmax warps once read
 constexpr int kAttnBK = 64;  // keys per tile
 constexpr float kLog2e = 1.4426950408889634f;
+// Of every 8 pairs of probabilities in a row tile, this many are computed by
+// exp2_poly2 (FMA pipe) and the rest by ex2.approx (MUFU).
+#ifndef XFB_FLASH_POLY_PAIRS
+#define XFB_FLASH_POLY_PAIRS 0
+#endif
+constexpr int kAttnPolyPairs = XFB_FLASH_POLY_PAIRS;
 
 // Bias source: streamed bf16 tiles through TMA, or per-thread global loads.
 enum AttnBiasMode : int { kBiasTma = 0, kBiasGlobalBf16 = 1, kBiasGlobalF32 = 2 };
@@ -56,11 +66,14 @@ struct AttnSmem {
   static constexpr int kKOff = kQOff + 2 * kQBytes;
   static constexpr int kVOff = kKOff + kAttnKvStages * kKVBytes;
   static constexpr int kBiasOff = kVOff + kAttnKvStages * kKVBytes;
-  static constexpr int kPOff = kBiasOff + kAttnKvStages * kBiasBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  // q_full[2], q_empty[2], kv_full[S], kv_empty[S], s_full[2], s_free[2],
+  static constexpr int kPOff = kBiasOff + kAttnBiasStages * kBiasBytes;
+  static constexpr int kOnesOff = kPOff + 2 * kPBytes;  // 16 x 64 bf16 ones (row-sum MMA)
+  static constexpr int kOnesBytes = 16 * kAttnBK * 2;
+  static constexpr int kBarOff = kOnesOff + kOnesBytes;
+  // q_full[2], q_empty[2], kv_full[S], kv_empty[S], b_full[SB], b_empty[SB],
+  // s_full[2], s_free[2],
   // p_full[2], o_done[2], o_free
-  static constexpr int kNumBars = 4 + 2 * kAttnKvStages + 9;
+  static constexpr int kNumBars = 4 + 2 * kAttnKvStages + 2 * kAttnBiasStages + 9;
   static constexpr int kTotal = kBarOff + kNumBars * 8 + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;
   static constexpr int kCtasPerSm = kLaunchBytes * 2 <= 220 * 1024 ? 2 : 1;
@@ -141,6 +154,72 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Stores 16 consecutive TMEM columns of this thread's lane from src[0..15].
+__device__ __forceinline__ void tmem_st16_from(uint32_t taddr, const float* src) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(src[0])), "r"(__float_as_uint(src[1])), "r"(__float_as_uint(src[2])),
+      "r"(__float_as_uint(src[3])), "r"(__float_as_uint(src[4])), "r"(__float_as_uint(src[5])),
+      "r"(__float_as_uint(src[6])), "r"(__float_as_uint(src[7])), "r"(__float_as_uint(src[8])),
+      "r"(__float_as_uint(src[9])), "r"(__float_as_uint(src[10])), "r"(__float_as_uint(src[11])),
+      "r"(__float_as_uint(src[12])), "r"(__float_as_uint(src[13])), "r"(__float_as_uint(src[14])),
+      "r"(__float_as_uint(src[15]))
+      : "memory");
+}
+
+// max with NaN propagation (a NaN logit must poison its row, as in the
+// reference); the three-operand form is native on sm_100.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Maximum of 64 scores: 32 three-operand maxima in a tree of depth 4.
+__device__ __forceinline__ float tile_max64(const float* s) {
+  float a[22];
+#pragma unroll
+  for (int i = 0; i < 21; ++i) a[i] = max3_nan(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
+  a[21] = s[63];
+  float b[8];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) b[i] = max3_nan(a[3 * i], a[3 * i + 1], a[3 * i + 2]);
+  b[7] = a[21];
+  return max3_nan(max3_nan(b[0], b[1], b[2]), max3_nan(b[3], b[4], b[5]), max_nan(b[6], b[7]));
+}
+
+// 2^x for a pair of values on the FMA pipe (Cody-Waite range reduction plus a
+// minimax polynomial).  x = j + f with j = rint(x) from the 1.5 * 2^23
+// rounding constant and f in [-0.5, 0.5]; 2^f is the degree-3 polynomial
+// below, fitted here to minimise the relative error on that interval (max
+// 7.5e-5, well under the 2^-9 of the bf16 probabilities it feeds); 2^j is
+// added to the exponent field as an integer.  Inputs are clamped at -125 so the
+// exponent cannot underflow: 2^-125 stands for anything smaller, which is
+// below f32 resolution next to the row max's 2^0.  A NaN input gives a finite
+// value here; the MUFU share of the same row carries the NaN.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992805719375610f, c1 = 0.69326096773147583f,
+                  c2 = 0.24261112511157990f, c3 = 0.05517166852951050f;
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 r = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = fma2(r, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(make_float2(c3, c3), f, make_float2(c2, c2));
+  p = fma2(p, f, make_float2(c1, c1));
+  p = fma2(p, f, make_float2(c0, c0));
+  return make_float2(__uint_as_float(__float_as_uint(t.x) * 8388608u + __float_as_uint(p.x)),
+                     __uint_as_float(__float_as_uint(t.y) * 8388608u + __float_as_uint(p.y)));
+}
+
 // Work item w -> (b, h, q-tile), query tiles fastest so concurrent CTAs share K / V.
 __device__ __forceinline__ void attn_item(const AttnArgs& a, int w, int& b, int& h, int& qt) {
   qt = w % a.q_tiles;
@@ -159,8 +238,10 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   using L = AttnSmem<DP>;
   constexpr uint32_t kIdescS = idesc_bf16(128, kAttnBK, false, false);
   constexpr uint32_t kIdescO = idesc_bf16(128, DP, false, true);
-  constexpr uint32_t kTmemCols = 256;  // S: 2 x 64 columns, O: DP columns at 128
+  constexpr uint32_t kIdescL = idesc_bf16(128, 16, false, false);
+  constexpr uint32_t kTmemCols = 256;  // S: 2 x 64 columns, O: DP columns at 128, l: 16 after O
   constexpr uint32_t kOCol = 128;
+  constexpr uint32_t kLCol = kOCol + DP;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -170,12 +251,15 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   uint8_t* sV = smem + L::kVOff;
   uint8_t* sBias = smem + L::kBiasOff;
   uint8_t* sP = smem + L::kPOff;
+  uint8_t* sOnes = smem + L::kOnesOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 2;
   uint64_t* kv_full = q_empty + 2;
   uint64_t* kv_empty = kv_full + kAttnKvStages;
-  uint64_t* s_full = kv_empty + kAttnKvStages;
+  uint64_t* b_full = kv_empty + kAttnKvStages;
+  uint64_t* b_empty = b_full + kAttnBiasStages;
+  uint64_t* s_full = b_empty + kAttnBiasStages;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* o_done = p_full + 2;
@@ -202,6 +286,10 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int s = 0; s < kAttnBiasStages; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 128);
+    }
     mbar_init(o_free, 128);
     *abort_flag = 0;
     fence_mbar_init();
@@ -209,6 +297,13 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   if (warp == 5) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
+  }
+  if (warp < 4) {
+    // the ones tile of the row-sum MMA (every element 1.0, so no swizzle matters)
+    for (int i = threadIdx.x; i < L::kOnesBytes / 16; i += 128)
+      reinterpret_cast<uint4*>(sOnes)[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u,
+                                                     0x3F803F80u);
+    fence_async_smem();
   }
   if (warp == 4 && lane == 0) {
     tma_prefetch(&tmQ);
@@ -225,7 +320,6 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       const bool tma_bias = BMODE == kBiasTma && has_bias;
-      const uint32_t stage_bytes = 2 * L::kKVBytes + (tma_bias ? L::kBiasBytes : 0);
       int g = 0;   // global key-tile counter (ring index)
       int it = 0;  // item counter of this CTA
       bool ok = true;
@@ -245,12 +339,20 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&kv_full[st], stage_bytes);
+          mbar_arrive_expect_tx(&kv_full[st], 2 * L::kKVBytes);
           tma_load_3d(sK + st * L::kKVBytes, &tmK, &kv_full[st], 0, t * kAttnBK, bh);
           tma_load_3d(sV + st * L::kKVBytes, &tmV, &kv_full[st], 0, t * kAttnBK, bh);
-          if (tma_bias)
-            tma_load_3d(sBias + st * L::kBiasBytes, &tmBias, &kv_full[st], t * kAttnBK,
-                        qt * 128, bz);
+          if (tma_bias) {
+            const int sb = g % kAttnBiasStages;
+            if (!mbar_wait(&b_empty[sb], ((g / kAttnBiasStages) & 1) ^ 1, kErrWaitProducer,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&b_full[sb], L::kBiasBytes);
+            tma_load_3d(sBias + sb * L::kBiasBytes, &tmBias, &b_full[sb], t * kAttnBK, qt * 128,
+                        bz);
+          }
         }
       }
     }
@@ -261,6 +363,7 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
       int it = 0;
       bool ok = true;
       const uint32_t p_addr0 = smem_u32(sP);
+      const uint32_t ones_addr = smem_u32(sOnes);
       for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
         const int qb = it & 1;
         if (!mbar_wait(&q_full[qb], (it >> 1) & 1, kErrWaitMma, abort_flag)) break;
@@ -304,8 +407,12 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
             for (int j = 0; j < kAttnBK / 16; ++j)
               umma_bf16(tmem_base + kOCol, p_desc(p_addr, j), v_desc<DP>(v_addr, j), kIdescO,
                         (t > 1 || j > 0) ? 1u : 0u);
+#pragma unroll
+            for (int j = 0; j < kAttnBK / 16; ++j)
+              umma_bf16(tmem_base + kLCol, p_desc(p_addr, j), sw128_desc(ones_addr + j * 32, 16, 1024),
+                        kIdescL, (t > 1 || j > 0) ? 1u : 0u);
             umma_commit(&o_done[pb]);
-            umma_commit(&kv_empty[st]);  // K, V and bias of that tile are no longer read
+            umma_commit(&kv_empty[st]);  // K and V of that tile are no longer read
           }
         }
         g += n_tiles;
@@ -316,7 +423,11 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
     const int row = warp * 32 + lane;
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
     const int words = (args.nk + 31) / 32;
-    constexpr float kMasked = -1e9f * kLog2e;
+    // Scores stay in the units the MMA produced (log2 with PRE, natural
+    // otherwise); kScale converts inside the exponent's FMA.
+    constexpr float kScale = PRE ? 1.f : kLog2e;
+    constexpr float kMasked = PRE ? -1e9f * kLog2e : -1e9f;
+    const float2 scale2 = make_float2(kScale, kScale);
     int g = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
@@ -333,11 +444,17 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
                    ? static_cast<const void*>(reinterpret_cast<const float*>(args.bias) + off)
                    : static_cast<const void*>(reinterpret_cast<const __nv_bfloat16*>(args.bias) + off);
       }
-      float m_ref = -INFINITY, l_run = 0.f;
+      float m_ref = -INFINITY;  // reference max, log2 units
       for (int t = 0; t < n_tiles; ++t) {
         const int gt = g + t;
         const int sb = gt & 1;
         const int key0 = t * kAttnBK;
+        // mask words of this tile, loaded ahead of the waits
+        uint32_t w0 = 0xFFFFFFFFu, w1 = 0xFFFFFFFFu;
+        if (mrow != nullptr) {
+          w0 = mrow[2 * t];
+          w1 = (2 * t + 1 < words) ? mrow[2 * t + 1] : 0u;
+        }
         // ---- S_t from TMEM
         ok = mbar_wait(&s_full[sb], (gt >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
         tc_fence_after();
@@ -347,30 +464,23 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&s_free[sb]);
-        // ---- bias (log2 units)
+        float2* s2 = reinterpret_cast<float2*>(s);
+        // ---- bias
         if (BMODE == kBiasTma && has_bias) {
-          const int st = gt % kAttnKvStages;
-          // the tile landed with K / V (the S MMA waited for it); observe the
-          // phase here too for the visibility of the TMA writes
-          ok = mbar_wait(&kv_full[st], (gt / kAttnKvStages) & 1, kErrWaitSoftmax, abort_flag) && ok;
-          const uint8_t* bt = sBias + st * L::kBiasBytes + row * 128;
+          const int sbias = gt % kAttnBiasStages;
+          ok = mbar_wait(&b_full[sbias], (gt / kAttnBiasStages) & 1, kErrWaitSoftmax, abort_flag) &&
+               ok;
+          const uint8_t* bt = sBias + sbias * L::kBiasBytes + row * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint4 wv = *reinterpret_cast<const uint4*>(bt + ((c ^ (row & 7)) << 4));
             const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float b0 = __uint_as_float(ww[e] << 16);
-              const float b1 = __uint_as_float(ww[e] & 0xFFFF0000u);
-              if constexpr (PRE) {
-                s[c * 8 + 2 * e] += b0;
-                s[c * 8 + 2 * e + 1] += b1;
-              } else {
-                s[c * 8 + 2 * e] = (s[c * 8 + 2 * e] + b0) * kLog2e;
-                s[c * 8 + 2 * e + 1] = (s[c * 8 + 2 * e + 1] + b1) * kLog2e;
-              }
-            }
+            for (int e = 0; e < 4; ++e)
+              s2[c * 4 + e] = add2(s2[c * 4 + e], make_float2(__uint_as_float(ww[e] << 16),
+                                                              __uint_as_float(ww[e] & 0xFFFF0000u)));
           }
+          mbar_arrive(&b_empty[sbias]);  // the values are in registers: the slot may refill
         } else if (brow != nullptr) {
 #pragma unroll
           for (int j = 0; j < kAttnBK; ++j) {
@@ -380,18 +490,10 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
                        ? reinterpret_cast<const float*>(brow)[key0 + j]
                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(brow)[key0 + j]);
             }
-            s[j] = PRE ? s[j] + bj : (s[j] + bj) * kLog2e;
+            s[j] += bj;
           }
-        } else if (!PRE) {
-#pragma unroll
-          for (int j = 0; j < kAttnBK; ++j) s[j] *= kLog2e;
         }
-        // ---- key mask: masked -> -1e9 (log2 units), past the end -> -inf
-        uint32_t w0 = 0xFFFFFFFFu, w1 = 0xFFFFFFFFu;
-        if (mrow != nullptr) {
-          w0 = mrow[2 * t];
-          w1 = (2 * t + 1 < words) ? mrow[2 * t + 1] : 0u;
-        }
+        // ---- key mask: masked -> -1e9, past the end -> -inf
         if (key0 + kAttnBK > args.nk || (w0 & w1) != 0xFFFFFFFFu) {
 #pragma unroll
           for (int j = 0; j < kAttnBK; ++j) {
@@ -403,40 +505,48 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
             }
           }
         }
-        // ---- tile max and lazy reference update
-        float mt = s[0];
-#pragma unroll
-        for (int j = 1; j < kAttnBK; ++j) mt = fmaxf(mt, s[j]);
-        const bool grow = mt > m_ref + 8.f;
+        // ---- tile max and lazy reference update (a NaN max always "grows")
+        const float mt = tile_max64(s) * kScale;
+        const bool grow = !(mt <= m_ref + 8.f);
         float factor = 1.f;
         if (grow) {
           factor = ex2_approx(m_ref - mt);  // 0 when m_ref = -inf
-          l_run *= factor;
           m_ref = mt;
         }
-        // O already holds earlier tiles of this item: rescale it in TMEM (rare).
+        // O and l already hold earlier tiles of this item: rescale them in TMEM (rare).
         if (t > 0 && __any_sync(0xffffffffu, grow)) {
           const int gp = gt - 1;
           ok = mbar_wait(&o_done[gp & 1], (gp >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
           tc_fence_after();
           float o[DP];
+          float lv[16];
 #pragma unroll
           for (int c = 0; c < DP / 32; ++c) tmem_ld32_to(t_row + kOCol + c * 32, o + c * 32);
-          tmem_wait_ld();
+          tmem_ld16(t_row + kLCol, lv);
 #pragma unroll
           for (int i = 0; i < DP; ++i) o[i] *= factor;
 #pragma unroll
+          for (int i = 0; i < 16; ++i) lv[i] *= factor;
+#pragma unroll
           for (int c = 0; c < DP / 32; ++c) tmem_st32_from(t_row + kOCol + c * 32, o + c * 32);
+          tmem_st16_from(t_row + kLCol, lv);
           tmem_wait_st();
         }
-        // ---- probabilities
-        float rs = 0.f;
+        // ---- probabilities: 2^(s * kScale - m_ref), split between MUFU and FMA pipes
+        {
+          const float2 neg = make_float2(-m_ref, -m_ref);
 #pragma unroll
-        for (int j = 0; j < kAttnBK; ++j) {
-          s[j] = ex2_approx(s[j] - m_ref);
-          rs += s[j];
+          for (int j = 0; j < kAttnBK / 2; ++j) {
+            float2 x = fma2(s2[j], scale2, neg);
+            if ((j & 7) < kAttnPolyPairs) {
+              x = exp2_poly2(x);
+            } else {
+              x.x = ex2_approx(x.x);
+              x.y = ex2_approx(x.y);
+            }
+            s2[j] = x;
+          }
         }
-        l_run += rs;
         // ---- P into the swizzled SMEM tile of this parity; the PV MMA that read
         //      it last (tile g-2) must have completed.
         const int pb = gt & 1;
@@ -462,13 +572,14 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
       ok = mbar_wait(&o_done[gl & 1], (gl >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
       tc_fence_after();
       float o[DP];
+      float lv[16];
 #pragma unroll
       for (int c = 0; c < DP / 32; ++c) tmem_ld32_to(t_row + kOCol + c * 32, o + c * 32);
-      tmem_wait_ld();
+      tmem_ld16(t_row + kLCol, lv);
       tc_fence_before();
       mbar_arrive(o_free);
       if (q_ok && ok) {
-        const float inv_l = 1.f / l_run;
+        const float inv_l = 1.f / lv[0];
         __nv_bfloat16* orow =
             args.out + b * args.out_sb + h * args.out_sh + static_cast<int64_t>(q) * args.out_sq;
         const __nv_bfloat16* grow_p =
