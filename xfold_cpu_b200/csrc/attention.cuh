@@ -3,12 +3,13 @@
 //
 // Persistent CTAs (two per SM for head dim <= 32) walk work items (batch row b,
 // head h, 128-query tile).  Per 64-key tile t of an item:
-//   S_t  = Q K_t^T          tcgen05.mma from TMA-loaded swizzled SMEM into TMEM
-//                           (double-buffered S)
-//   P_t  = 2^(S_t + bias_t - m_ref)   softmax warps, one query row per thread;
-//                           the bias tile arrives by TMA with K_t / V_t; P is
-//                           written as bf16 into a 128B-swizzled SMEM tile
-//   O   += P_t V_t          tcgen05.mma accumulating in TMEM (V read MN-major)
+//   S_t  = bias_t + Q K_t^T tcgen05.mma from TMA-loaded swizzled SMEM into TMEM
+//                           (double-buffered S); the bf16 bias tile enters the
+//                           accumulator exactly through MMAs against a 16 x 16
+//                           identity, so the softmax never touches it
+//   P_t  = 2^(S_t - m_ref)  softmax warps, one query row per thread; P goes
+//                           back to TMEM as bf16 (tcgen05.st)
+//   O   += P_t V_t          tcgen05.mma with A = P from TMEM, V read MN-major
 //   l   += P_t 1            a second MMA against a tile of ones: the row sums of
 //                           the bf16 probabilities, next to O in TMEM
 // With PRE, q carries d^-0.5 * log2(e) and the bias log2(e) from their
@@ -29,7 +30,7 @@ namespace xfb {
 
 constexpr int kAttnThreads = 192;
 constexpr int kAttnKvStages = 3;    // K / V ring, freed by the PV MMA
-constexpr int kAttnBiasStages = 2;  // bias ring, freed by the softmax warps once read
+constexpr int kAttnBiasStages = 3;  // bias ring, freed by the S MMA
 constexpr int kAttnBK = 64;  // keys per tile
 constexpr float kLog2e = 1.4426950408889634f;
 // Of every 8 pairs of probabilities in a row tile, this many are computed by
@@ -61,15 +62,15 @@ struct AttnSmem {
   static constexpr int kQBytes = 128 * DP * 2;
   static constexpr int kKVBytes = kAttnBK * DP * 2;
   static constexpr int kBiasBytes = 128 * kAttnBK * 2;  // one 64-key swizzle atom per row
-  static constexpr int kPBytes = 128 * kAttnBK * 2;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + 2 * kQBytes;
   static constexpr int kVOff = kKOff + kAttnKvStages * kKVBytes;
   static constexpr int kBiasOff = kVOff + kAttnKvStages * kKVBytes;
-  static constexpr int kPOff = kBiasOff + kAttnBiasStages * kBiasBytes;
-  static constexpr int kOnesOff = kPOff + 2 * kPBytes;  // 16 x 64 bf16 ones (row-sum MMA)
-  static constexpr int kOnesBytes = 16 * kAttnBK * 2;
-  static constexpr int kBarOff = kOnesOff + kOnesBytes;
+  static constexpr int kOnesOff = kBiasOff + kAttnBiasStages * kBiasBytes;
+  static constexpr int kOnesBytes = 16 * kAttnBK * 2;  // 16 x 64 bf16 ones (row-sum MMA)
+  static constexpr int kIdentOff = kOnesOff + kOnesBytes;
+  static constexpr int kIdentBytes = 16 * 128;  // 16 x 16 identity in 128-byte swizzled rows
+  static constexpr int kBarOff = kIdentOff + kIdentBytes;
   // q_full[2], q_empty[2], kv_full[S], kv_empty[S], b_full[SB], b_empty[SB],
   // s_full[2], s_free[2],
   // p_full[2], o_done[2], o_free
@@ -99,7 +100,8 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t addr, int kstep) {
   }
 }
 
-// P tile (128 queries x 64 keys, K-major, one 128-byte swizzle atom per row).
+// Bias tile (128 queries x 64 keys, K-major, one 128-byte swizzle atom per row)
+// as the A operand of the identity MMAs; kstep selects 16 keys.
 __device__ __forceinline__ uint64_t p_desc(uint32_t addr, int kstep) {
   return sw128_desc(addr + kstep * 32, 16, 1024);
 }
@@ -152,6 +154,20 @@ __device__ __forceinline__ void tmem_wait_ld() {
 __device__ __forceinline__ void tmem_wait_st() {
   __syncwarp();
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Stores 32 consecutive TMEM columns of this thread's lane from raw words.
+__device__ __forceinline__ void tmem_st32_u(uint32_t taddr, const uint32_t* v) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+      "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 // Stores 16 consecutive TMEM columns of this thread's lane from src[0..15].
@@ -238,10 +254,12 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   using L = AttnSmem<DP>;
   constexpr uint32_t kIdescS = idesc_bf16(128, kAttnBK, false, false);
   constexpr uint32_t kIdescO = idesc_bf16(128, DP, false, true);
-  constexpr uint32_t kIdescL = idesc_bf16(128, 16, false, false);
-  constexpr uint32_t kTmemCols = 256;  // S: 2 x 64 columns, O: DP columns at 128, l: 16 after O
+  constexpr uint32_t kIdescL = idesc_bf16(128, 16, false, false);  // also the bias MMAs
+  // TMEM columns: S 2 x 64 at 0, O at 128, l (16) after O, P 2 x 32 (bf16 pairs)
   constexpr uint32_t kOCol = 128;
   constexpr uint32_t kLCol = kOCol + DP;
+  constexpr uint32_t kPCol = DP == 32 ? 192 : 224;
+  constexpr uint32_t kTmemCols = kPCol + 64 <= 256 ? 256 : 512;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -250,8 +268,8 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
   uint8_t* sBias = smem + L::kBiasOff;
-  uint8_t* sP = smem + L::kPOff;
   uint8_t* sOnes = smem + L::kOnesOff;
+  uint8_t* sIdent = smem + L::kIdentOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 2;
@@ -288,7 +306,7 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
     }
     for (int s = 0; s < kAttnBiasStages; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 128);
+      mbar_init(&b_empty[s], 1);
     }
     mbar_init(o_free, 128);
     *abort_flag = 0;
@@ -303,6 +321,17 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
     for (int i = threadIdx.x; i < L::kOnesBytes / 16; i += 128)
       reinterpret_cast<uint4*>(sOnes)[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u,
                                                      0x3F803F80u);
+    // identity: row n holds 1.0 at k = n, in the 128-byte swizzle (16-byte
+    // chunk c of row n stored at chunk position c ^ (n % 8))
+    for (int i = threadIdx.x; i < L::kIdentBytes / 16; i += 128) {
+      const int n = i >> 3;
+      const int c = (i & 7) ^ (n & 7);
+      const uint32_t one = (n & 1) ? 0x3F800000u : 0x00003F80u;
+      const int word = c == (n >> 3) ? (n & 7) >> 1 : -1;
+      reinterpret_cast<uint4*>(sIdent)[i] =
+          make_uint4(word == 0 ? one : 0u, word == 1 ? one : 0u, word == 2 ? one : 0u,
+                     word == 3 ? one : 0u);
+    }
     fence_async_smem();
   }
   if (warp == 4 && lane == 0) {
@@ -362,8 +391,9 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
       int g = 0;
       int it = 0;
       bool ok = true;
-      const uint32_t p_addr0 = smem_u32(sP);
+      const bool tma_bias = BMODE == kBiasTma && has_bias;
       const uint32_t ones_addr = smem_u32(sOnes);
+      const uint64_t ident_desc = sw128_desc(smem_u32(sIdent), 16, 1024);
       for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
         const int qb = it & 1;
         if (!mbar_wait(&q_full[qb], (it >> 1) & 1, kErrWaitMma, abort_flag)) break;
@@ -378,13 +408,28 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
               ok = false;
               break;
             }
+            const int sbias = gt % kAttnBiasStages;
+            if (tma_bias &&
+                !mbar_wait(&b_full[sbias], (gt / kAttnBiasStages) & 1, kErrWaitMma, abort_flag)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
             const uint32_t k_addr = smem_u32(sK + st * L::kKVBytes);
+            if (tma_bias) {
+              // S[:, 16j + n] = sum_k bias[:, 16j + k] * I[k][n]: exact in the f32 accumulator
+              const uint32_t b_addr = smem_u32(sBias + sbias * L::kBiasBytes);
+#pragma unroll
+              for (int j = 0; j < kAttnBK / 16; ++j)
+                umma_bf16(tmem_base + sb * kAttnBK + 16 * j, p_desc(b_addr, j), ident_desc, kIdescL,
+                          0u);
+            }
 #pragma unroll
             for (int k = 0; k < DP / 16; ++k)
               umma_bf16(tmem_base + sb * kAttnBK, qk_desc<DP>(q_addr, k), qk_desc<DP>(k_addr, k),
-                        kIdescS, k > 0 ? 1u : 0u);
+                        kIdescS, (tma_bias || k > 0) ? 1u : 0u);
             umma_commit(&s_full[sb]);
+            if (tma_bias) umma_commit(&b_empty[sbias]);
             if (t == n_tiles - 1) umma_commit(&q_empty[qb]);
           }
           if (t >= 1) {
@@ -402,15 +447,16 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
             }
             tc_fence_after();
             const uint32_t v_addr = smem_u32(sV + st * L::kKVBytes);
-            const uint32_t p_addr = p_addr0 + pb * L::kPBytes;
+            const uint32_t p_tmem = tmem_base + kPCol + pb * (kAttnBK / 2);  // 8 columns per 16 keys
 #pragma unroll
             for (int j = 0; j < kAttnBK / 16; ++j)
-              umma_bf16(tmem_base + kOCol, p_desc(p_addr, j), v_desc<DP>(v_addr, j), kIdescO,
-                        (t > 1 || j > 0) ? 1u : 0u);
+              umma_bf16_ts(tmem_base + kOCol, p_tmem + 8 * j, v_desc<DP>(v_addr, j), kIdescO,
+                           (t > 1 || j > 0) ? 1u : 0u);
 #pragma unroll
             for (int j = 0; j < kAttnBK / 16; ++j)
-              umma_bf16(tmem_base + kLCol, p_desc(p_addr, j), sw128_desc(ones_addr + j * 32, 16, 1024),
-                        kIdescL, (t > 1 || j > 0) ? 1u : 0u);
+              umma_bf16_ts(tmem_base + kLCol, p_tmem + 8 * j,
+                           sw128_desc(ones_addr + j * 32, 16, 1024), kIdescL,
+                           (t > 1 || j > 0) ? 1u : 0u);
             umma_commit(&o_done[pb]);
             umma_commit(&kv_empty[st]);  // K and V of that tile are no longer read
           }
@@ -465,23 +511,8 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
         tc_fence_before();
         mbar_arrive(&s_free[sb]);
         float2* s2 = reinterpret_cast<float2*>(s);
-        // ---- bias
-        if (BMODE == kBiasTma && has_bias) {
-          const int sbias = gt % kAttnBiasStages;
-          ok = mbar_wait(&b_full[sbias], (gt / kAttnBiasStages) & 1, kErrWaitSoftmax, abort_flag) &&
-               ok;
-          const uint8_t* bt = sBias + sbias * L::kBiasBytes + row * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(bt + ((c ^ (row & 7)) << 4));
-            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              s2[c * 4 + e] = add2(s2[c * 4 + e], make_float2(__uint_as_float(ww[e] << 16),
-                                                              __uint_as_float(ww[e] & 0xFFFF0000u)));
-          }
-          mbar_arrive(&b_empty[sbias]);  // the values are in registers: the slot may refill
-        } else if (brow != nullptr) {
+        // ---- bias (the TMA bias entered S in the MMA)
+        if (brow != nullptr) {
 #pragma unroll
           for (int j = 0; j < kAttnBK; ++j) {
             float bj = 0.f;
@@ -547,23 +578,17 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
             s2[j] = x;
           }
         }
-        // ---- P into the swizzled SMEM tile of this parity; the PV MMA that read
-        //      it last (tile g-2) must have completed.
+        // ---- P (bf16 pairs) into the TMEM columns of this parity; the PV MMA
+        //      that read them last (tile g-2) must have completed.
         const int pb = gt & 1;
         if (gt >= 2) {
           ok = mbar_wait(&o_done[pb], ((gt - 2) >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
         }
-        uint8_t* prow = sP + pb * L::kPBytes + row * 128;
+        uint32_t pk[kAttnBK / 2];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 wv;
-          wv.x = pack_bf16x2(s[c * 8 + 0], s[c * 8 + 1]);
-          wv.y = pack_bf16x2(s[c * 8 + 2], s[c * 8 + 3]);
-          wv.z = pack_bf16x2(s[c * 8 + 4], s[c * 8 + 5]);
-          wv.w = pack_bf16x2(s[c * 8 + 6], s[c * 8 + 7]);
-          *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = wv;
-        }
-        fence_async_smem();
+        for (int j = 0; j < kAttnBK / 2; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
+        tmem_st32_u(t_row + kPCol + pb * (kAttnBK / 2), pk);
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[pb]);
       }
