@@ -39,6 +39,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 #define XFB_FLASH_POLY_PAIRS 0
 #endif
 constexpr int kAttnPolyPairs = XFB_FLASH_POLY_PAIRS;
+// 1: the TMA bias tile enters S through identity MMAs; 0: the softmax warps add
+// it from shared memory.
+#ifndef XFB_FLASH_BIAS_MMA
+#define XFB_FLASH_BIAS_MMA 1
+#endif
+constexpr bool kAttnBiasMma = XFB_FLASH_BIAS_MMA != 0;
 
 // Bias source: streamed bf16 tiles through TMA, or per-thread global loads.
 enum AttnBiasMode : int { kBiasTma = 0, kBiasGlobalBf16 = 1, kBiasGlobalF32 = 2 };
@@ -67,7 +73,9 @@ struct AttnSmem {
   static constexpr int kVOff = kKOff + kAttnKvStages * kKVBytes;
   static constexpr int kBiasOff = kVOff + kAttnKvStages * kKVBytes;
   static constexpr int kOnesOff = kBiasOff + kAttnBiasStages * kBiasBytes;
-  static constexpr int kOnesBytes = 16 * kAttnBK * 2;  // 16 x 64 bf16 ones (row-sum MMA)
+  // ones as one extra N chunk of the V operand (one swizzle atom wide, all keys):
+  // the PV MMA then also writes the row sums next to O
+  static constexpr int kOnesBytes = kAttnBK * (DP == 32 ? 64 : 128);
   static constexpr int kIdentOff = kOnesOff + kOnesBytes;
   static constexpr int kIdentBytes = 16 * 128;  // 16 x 16 identity in 128-byte swizzled rows
   static constexpr int kBarOff = kIdentOff + kIdentBytes;
@@ -90,13 +98,15 @@ __device__ __forceinline__ uint64_t qk_desc(uint32_t addr, int k) {
   }
 }
 
-// V tile as the MN-major B operand of O = P V (N = head dim, K = keys).
+// [V | ones] as the MN-major B operand of [O | l] = P [V | 1] (N = head dim + 16,
+// K = keys): the first swizzle-atom-wide N chunk is the V tile, the next one
+// (at byte offset `lbo`) the ones block.
 template <int DP>
-__device__ __forceinline__ uint64_t v_desc(uint32_t addr, int kstep) {
+__device__ __forceinline__ uint64_t v_desc(uint32_t addr, int kstep, uint32_t lbo) {
   if constexpr (DP == 32) {
-    return sw64_desc(addr + kstep * 16 * 64, 8192, 512);
+    return sw64_desc(addr + kstep * 16 * 64, lbo, 512);
   } else {
-    return sw128_desc(addr + kstep * 16 * 128, 8192, 1024);
+    return sw128_desc(addr + kstep * 16 * 128, lbo, 1024);
   }
 }
 
@@ -253,7 +263,7 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   static_assert(DP == 32 || DP == 64, "padded head dim must be 32 or 64");
   using L = AttnSmem<DP>;
   constexpr uint32_t kIdescS = idesc_bf16(128, kAttnBK, false, false);
-  constexpr uint32_t kIdescO = idesc_bf16(128, DP, false, true);
+  constexpr uint32_t kIdescO = idesc_bf16(128, DP + 16, false, true);  // O and l
   constexpr uint32_t kIdescL = idesc_bf16(128, 16, false, false);  // also the bias MMAs
   // TMEM columns: S 2 x 64 at 0, O at 128, l (16) after O, P 2 x 32 (bf16 pairs)
   constexpr uint32_t kOCol = 128;
@@ -306,7 +316,7 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
     }
     for (int s = 0; s < kAttnBiasStages; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
+      mbar_init(&b_empty[s], kAttnBiasMma ? 1 : 128);
     }
     mbar_init(o_free, 128);
     *abort_flag = 0;
@@ -391,7 +401,7 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
       int g = 0;
       int it = 0;
       bool ok = true;
-      const bool tma_bias = BMODE == kBiasTma && has_bias;
+      const bool tma_bias = kAttnBiasMma && BMODE == kBiasTma && has_bias;
       const uint32_t ones_addr = smem_u32(sOnes);
       const uint64_t ident_desc = sw128_desc(smem_u32(sIdent), 16, 1024);
       for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
@@ -450,13 +460,8 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
             const uint32_t p_tmem = tmem_base + kPCol + pb * (kAttnBK / 2);  // 8 columns per 16 keys
 #pragma unroll
             for (int j = 0; j < kAttnBK / 16; ++j)
-              umma_bf16_ts(tmem_base + kOCol, p_tmem + 8 * j, v_desc<DP>(v_addr, j), kIdescO,
-                           (t > 1 || j > 0) ? 1u : 0u);
-#pragma unroll
-            for (int j = 0; j < kAttnBK / 16; ++j)
-              umma_bf16_ts(tmem_base + kLCol, p_tmem + 8 * j,
-                           sw128_desc(ones_addr + j * 32, 16, 1024), kIdescL,
-                           (t > 1 || j > 0) ? 1u : 0u);
+              umma_bf16_ts(tmem_base + kOCol, p_tmem + 8 * j, v_desc<DP>(v_addr, j, ones_addr - v_addr),
+                           kIdescO, (t > 1 || j > 0) ? 1u : 0u);
             umma_commit(&o_done[pb]);
             umma_commit(&kv_empty[st]);  // K and V of that tile are no longer read
           }
@@ -511,8 +516,23 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
         tc_fence_before();
         mbar_arrive(&s_free[sb]);
         float2* s2 = reinterpret_cast<float2*>(s);
-        // ---- bias (the TMA bias entered S in the MMA)
-        if (brow != nullptr) {
+        // ---- bias (with kAttnBiasMma the TMA bias entered S in the MMA)
+        if (!kAttnBiasMma && BMODE == kBiasTma && has_bias) {
+          const int sbias = gt % kAttnBiasStages;
+          ok = mbar_wait(&b_full[sbias], (gt / kAttnBiasStages) & 1, kErrWaitSoftmax, abort_flag) &&
+               ok;
+          const uint8_t* bt = sBias + sbias * L::kBiasBytes + row * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(bt + ((c ^ (row & 7)) << 4));
+            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              s2[c * 4 + e] = add2(s2[c * 4 + e], make_float2(__uint_as_float(ww[e] << 16),
+                                                              __uint_as_float(ww[e] & 0xFFFF0000u)));
+          }
+          mbar_arrive(&b_empty[sbias]);  // the values are in registers: the slot may refill
+        } else if (brow != nullptr) {
 #pragma unroll
           for (int j = 0; j < kAttnBK; ++j) {
             float bj = 0.f;
