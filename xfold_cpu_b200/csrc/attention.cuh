@@ -28,7 +28,14 @@
 
 namespace xfb {
 
-constexpr int kAttnThreads = 192;
+// warpgroup 0: softmax warps 0-3; warpgroup 1: TMA producer (4), S-MMA issuer
+// (5, owns TMEM), PV-MMA issuer (6), idle (7).  With two CTAs per SM the
+// kernel launches at 128 registers per thread and moves registers from
+// warpgroup 1 (down to 64) to the softmax (up to 192): 128*64 + 128*192 is
+// exactly the 256*128 the CTA was launched with.
+constexpr int kAttnThreads = 256;
+constexpr int kAttnRegsLaunch = 128, kAttnRegsSoftmax = 192, kAttnRegsOther = 64;
+static_assert(kAttnRegsSoftmax + kAttnRegsOther == 2 * kAttnRegsLaunch, "register split");
 constexpr int kAttnKvStages = 3;    // K / V ring, freed by the PV MMA
 constexpr int kAttnBiasStages = 3;  // bias ring, freed by the S MMA
 constexpr int kAttnBK = 64;  // keys per tile
@@ -299,6 +306,11 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   const int lane = threadIdx.x & 31;
   const int n_tiles = (args.nk + kAttnBK - 1) / kAttnBK;
   const int n_items = args.B * args.H * args.q_tiles;
+  // this CTA's items are blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int my_items = static_cast<int>(blockIdx.x) < n_items
+                           ? (n_items - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                           : 0;
+  const int total = my_items * n_tiles;
   const bool has_bias = args.bias != nullptr;
 
   if (threadIdx.x == 0) {
@@ -355,6 +367,9 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (warp >= 4) {
+  if constexpr (AttnSmem<DP>::kCtasPerSm == 2)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnRegsOther));
   if (warp == 4) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -396,80 +411,77 @@ __global__ void __launch_bounds__(kAttnThreads, AttnSmem<DP>::kCtasPerSm)
       }
     }
   } else if (warp == 5) {
-    // ------------------------------------------------ MMA issuer
+    // ------------------------------------------------ S-MMA issuer
+    // The CTA's key tiles form one sequence g = item * n_tiles + t.  S(g) is
+    // issued as soon as its K / bias tiles have landed and the softmax has loaded
+    // S(g - 2) from the same TMEM buffer; PV runs on its own issuer (warp 6), so
+    // neither waits for the other's inputs.
     if (lane == 0) {
-      int g = 0;
-      int it = 0;
-      bool ok = true;
       const bool tma_bias = kAttnBiasMma && BMODE == kBiasTma && has_bias;
-      const uint32_t ones_addr = smem_u32(sOnes);
       const uint64_t ident_desc = sw128_desc(smem_u32(sIdent), 16, 1024);
-      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+      for (int gs = 0; gs < total; ++gs) {
+        const int it = gs / n_tiles;
+        const int t = gs - it * n_tiles;
         const int qb = it & 1;
-        if (!mbar_wait(&q_full[qb], (it >> 1) & 1, kErrWaitMma, abort_flag)) break;
+        const int st = gs % kAttnKvStages;
+        const int sb = gs & 1;
+        const int sbias = gs % kAttnBiasStages;
+        if (t == 0 && !mbar_wait(&q_full[qb], (it >> 1) & 1, kErrWaitMma, abort_flag)) break;
+        if (!mbar_wait(&kv_full[st], (gs / kAttnKvStages) & 1, kErrWaitMma, abort_flag) ||
+            !mbar_wait(&s_free[sb], ((gs >> 1) & 1) ^ 1, kErrWaitMma, abort_flag))
+          break;
+        if (tma_bias &&
+            !mbar_wait(&b_full[sbias], (gs / kAttnBiasStages) & 1, kErrWaitMma, abort_flag))
+          break;
+        tc_fence_after();
         const uint32_t q_addr = smem_u32(sQ + qb * L::kQBytes);
-        for (int t = 0; t <= n_tiles; ++t) {
-          if (t < n_tiles) {
-            const int gt = g + t;
-            const int st = gt % kAttnKvStages;
-            const int sb = gt & 1;
-            if (!mbar_wait(&kv_full[st], (gt / kAttnKvStages) & 1, kErrWaitMma, abort_flag) ||
-                !mbar_wait(&s_free[sb], ((gt >> 1) & 1) ^ 1, kErrWaitMma, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const int sbias = gt % kAttnBiasStages;
-            if (tma_bias &&
-                !mbar_wait(&b_full[sbias], (gt / kAttnBiasStages) & 1, kErrWaitMma, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t k_addr = smem_u32(sK + st * L::kKVBytes);
-            if (tma_bias) {
-              // S[:, 16j + n] = sum_k bias[:, 16j + k] * I[k][n]: exact in the f32 accumulator
-              const uint32_t b_addr = smem_u32(sBias + sbias * L::kBiasBytes);
+        const uint32_t k_addr = smem_u32(sK + st * L::kKVBytes);
+        if (tma_bias) {
+          // S[:, 16j + n] = sum_k bias[:, 16j + k] * I[k][n]: exact in the f32 accumulator
+          const uint32_t b_addr = smem_u32(sBias + sbias * L::kBiasBytes);
 #pragma unroll
-              for (int j = 0; j < kAttnBK / 16; ++j)
-                umma_bf16(tmem_base + sb * kAttnBK + 16 * j, p_desc(b_addr, j), ident_desc, kIdescL,
-                          0u);
-            }
-#pragma unroll
-            for (int k = 0; k < DP / 16; ++k)
-              umma_bf16(tmem_base + sb * kAttnBK, qk_desc<DP>(q_addr, k), qk_desc<DP>(k_addr, k),
-                        kIdescS, (tma_bias || k > 0) ? 1u : 0u);
-            umma_commit(&s_full[sb]);
-            if (tma_bias) umma_commit(&b_empty[sbias]);
-            if (t == n_tiles - 1) umma_commit(&q_empty[qb]);
-          }
-          if (t >= 1) {
-            const int gu = g + t - 1;
-            const int st = gu % kAttnKvStages;
-            const int pb = gu & 1;
-            // the previous item's O must have been read before the first PV overwrites it
-            if (t == 1 && it > 0 && !mbar_wait(o_free, (it - 1) & 1, kErrWaitMma, abort_flag)) {
-              ok = false;
-              break;
-            }
-            if (!mbar_wait(&p_full[pb], (gu >> 1) & 1, kErrWaitMma, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t v_addr = smem_u32(sV + st * L::kKVBytes);
-            const uint32_t p_tmem = tmem_base + kPCol + pb * (kAttnBK / 2);  // 8 columns per 16 keys
-#pragma unroll
-            for (int j = 0; j < kAttnBK / 16; ++j)
-              umma_bf16_ts(tmem_base + kOCol, p_tmem + 8 * j, v_desc<DP>(v_addr, j, ones_addr - v_addr),
-                           kIdescO, (t > 1 || j > 0) ? 1u : 0u);
-            umma_commit(&o_done[pb]);
-            umma_commit(&kv_empty[st]);  // K and V of that tile are no longer read
-          }
+          for (int j = 0; j < kAttnBK / 16; ++j)
+            umma_bf16(tmem_base + sb * kAttnBK + 16 * j, p_desc(b_addr, j), ident_desc, kIdescL, 0u);
         }
-        g += n_tiles;
+#pragma unroll
+        for (int k = 0; k < DP / 16; ++k)
+          umma_bf16(tmem_base + sb * kAttnBK, qk_desc<DP>(q_addr, k), qk_desc<DP>(k_addr, k),
+                    kIdescS, (tma_bias || k > 0) ? 1u : 0u);
+        umma_commit(&s_full[sb]);
+        if (tma_bias) umma_commit(&b_empty[sbias]);
+        if (t == n_tiles - 1) umma_commit(&q_empty[qb]);
       }
     }
+  } else if (warp == 6) {
+    // ------------------------------------------------ PV-MMA issuer
+    // [O | l] += P(g) [V(g) | 1] once the softmax stored P(g) in TMEM.  S(g) read
+    // K(g) before the softmax could produce P(g), so this commit frees the K / V
+    // stage for both.
+    if (lane == 0) {
+      const uint32_t ones_addr = smem_u32(sOnes);
+      for (int gp = 0; gp < total; ++gp) {
+        const int it = gp / n_tiles;
+        const int t = gp - it * n_tiles;
+        const int st = gp % kAttnKvStages;
+        const int pb = gp & 1;
+        // the previous item's O must have been read before the first PV overwrites it
+        if (t == 0 && it > 0 && !mbar_wait(o_free, (it - 1) & 1, kErrWaitMma, abort_flag)) break;
+        if (!mbar_wait(&p_full[pb], (gp >> 1) & 1, kErrWaitMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + st * L::kKVBytes);
+        const uint32_t p_tmem = tmem_base + kPCol + pb * (kAttnBK / 2);  // 8 columns per 16 keys
+#pragma unroll
+        for (int j = 0; j < kAttnBK / 16; ++j)
+          umma_bf16_ts(tmem_base + kOCol, p_tmem + 8 * j, v_desc<DP>(v_addr, j, ones_addr - v_addr),
+                       kIdescO, (t > 0 || j > 0) ? 1u : 0u);
+        umma_commit(&o_done[pb]);
+        umma_commit(&kv_empty[st]);  // K and V of that tile are no longer read
+      }
+    }
+  }
   } else {
+    if constexpr (AttnSmem<DP>::kCtasPerSm == 2)
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttnRegsSoftmax));
     // ------------------------------------------------ softmax warps 0-3
     const int row = warp * 32 + lane;
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
