@@ -209,6 +209,13 @@ def run_reference(args) -> None:
 
 # ----------------------------------------------------------------------------- GPU arm
 
+# DRAM bytes (read + write) per launch from one ncu capture of the same kernel,
+# scaled to the bench shapes by the units processed (profiles/flash_attn_n512_full.md:
+# 323.5 MB at N = 512, every tensor of the launch scales with N^2).  None where no
+# capture was taken.
+TRAFFIC_BYTES = {"flash_attn": 1.294e9, "triangle_contraction": None}
+
+
 def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
     """Times the triangle-attention flash kernel and the triangle contraction
     GEMM on the block's shapes with CUDA events on the launching stream."""
@@ -252,7 +259,8 @@ def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
         achieved = flops / t / 1e12
         results[name] = {"bound": "tensor", "achieved": round(achieved, 1),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
+                         "frac": round(achieved / peaks["bf16_tflops"], 4),
+                         "traffic": TRAFFIC_BYTES[name],
                          "ms_per_launch": round(t * 1e3, 4),
                          "flops_per_launch": flops}
     del q, k, v, bias, a, b
