@@ -251,6 +251,64 @@ XFB_API int xfb_pair_logits(const void* pair, int pair_dtype, int64_t n, int64_t
                             int64_t heads, const float* norm_weight, const float* norm_bias,
                             double eps, const void* w, void* logits, void* stream);
 
+/* ---- Row-block stages.  No counterpart in the reference, which runs every
+ * operator on the whole pair inside one process.  These run the operators above
+ * on a block of pair rows [rows][n][c] (n % 8 == 0) and stop exactly where a
+ * row-sharded pair must exchange data between GPUs; xfold_cpu_b200/sharded.py
+ * chains them with NCCL all-to-all / all-gather steps. */
+
+/* TriMul stage 1 (xfold/nn/triangle_multiplication.py:71-95 on a row block):
+ * x = LN(pair rows); a, b = channel-major [c][rows][n] bf16 (a = projection
+ * channel 2k, b = 2k+1, masked and multiplied by the sigmoid gate); g = [rows][n][c]
+ * bf16 output gate.  mask = [rows][n] f32 rows of the pair mask, or null; packed =
+ * xfb_pack_triangle_weights.  Between stages 1 and 3 the contraction of a channel
+ * shard is xfb_gemm: outgoing (a, b, both K-major), incoming (b, a, both MN-major). */
+XFB_API int64_t xfb_triangle_projection_workspace(int64_t rows, int64_t n, int64_t c);
+XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                    int64_t c, const float* mask, const float* left_weight,
+                                    const float* left_bias, double left_eps, const void* packed,
+                                    void* a, void* b, void* g, void* workspace,
+                                    int64_t workspace_bytes, void* stream);
+
+/* TriMul stage 3 (triangle_multiplication.py:96-105 on a row block): z = the
+ * contraction for these rows, channel-major [c][rows][n] bf16; update =
+ * (LN_c(z) W_o^T) * g -> out [rows][n][c] (accumulate: out f32 += update). */
+XFB_API int64_t xfb_triangle_output_workspace(int64_t rows, int64_t n, int64_t c);
+XFB_API int xfb_triangle_output(const void* z, int64_t rows, int64_t n, int64_t c, const void* g,
+                                const float* center_weight, const float* center_bias,
+                                double center_eps, const void* output_weight, void* out,
+                                int out_dtype, int accumulate, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* Grid attention stage 1 (xfold/nn/attention.py:86-98 on a row block):
+ * x = LN(pair rows) bf16 [rows][n][c]; bias rows [heads][rows][n] bf16, multiplied
+ * by log2(e) when c / heads == 32 and n % 8 == 0 (the units stage 2 expects). */
+XFB_API int xfb_grid_attention_prepare(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                       int64_t c, int64_t heads, const float* norm_weight,
+                                       const float* norm_bias, double eps, const void* bias_weight,
+                                       void* x, void* bias, void* stream);
+
+/* Grid attention stage 2 (attention.py:61-78 and 99-105 on a row block): q, k, v
+ * and the gate from x rows; each row attends over its n tokens with bias
+ * [heads][n][n] (stage 1 of every row block, assembled) and key mask [rows][n] f32
+ * (or null); gated output projection -> out [rows][n][c].  packed =
+ * xfb_pack_attention_weights.  For the ending node the caller passes the
+ * transposed rows (columns of the pair) and the mask rows of those columns. */
+XFB_API int64_t xfb_grid_attention_rows_workspace(int64_t rows, int64_t n, int64_t c,
+                                                  int64_t heads);
+XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int64_t c,
+                                    int64_t heads, const float* mask, const void* bias,
+                                    const void* packed, const void* output_w, void* out,
+                                    int out_dtype, int accumulate, void* workspace,
+                                    int64_t workspace_bytes, void* stream);
+
+/* Pair-logit projection (pairformer.py:103-106) of a row block:
+ * logits [heads][rows][n] bf16. */
+XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                 int64_t c, int64_t heads, const float* norm_weight,
+                                 const float* norm_bias, double eps, const void* w, void* logits,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

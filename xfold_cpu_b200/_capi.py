@@ -74,6 +74,19 @@ SIGNATURES: dict[str, tuple] = {
          _p, _p, _i, _i, _p, _i64, _p],
     ),
     "xfb_pair_logits": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _d, _p, _p, _p]),
+    # row-block stages of the row-sharded pair
+    "xfb_triangle_projection_workspace": (_i64, [_i64, _i64, _i64]),
+    "xfb_triangle_projection": (
+        _i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _d, _p, _p, _p, _p, _p, _i64, _p]),
+    "xfb_triangle_output_workspace": (_i64, [_i64, _i64, _i64]),
+    "xfb_triangle_output": (
+        _i, [_p, _i64, _i64, _i64, _p, _p, _p, _d, _p, _p, _i, _i, _p, _i64, _p]),
+    "xfb_grid_attention_prepare": (
+        _i, [_p, _i, _i64, _i64, _i64, _i64, _p, _p, _d, _p, _p, _p, _p]),
+    "xfb_grid_attention_rows_workspace": (_i64, [_i64, _i64, _i64, _i64]),
+    "xfb_grid_attention_rows": (
+        _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _i64, _p]),
+    "xfb_pair_logits_rows": (_i, [_p, _i, _i64, _i64, _i64, _i64, _p, _p, _d, _p, _p, _p]),
 }
 
 _lock = threading.Lock()

@@ -897,11 +897,11 @@ XFB_API int xfb_triangle_multiplication(
     const int blocks = static_cast<int>(std::min<int64_t>((M + 127) / 128, int64_t(sms) * 8));
     if (c == 128) {
       xfb::ln_channel_major_kernel<128><<<blocks, 128, 0, st>>>(
-          w.z, static_cast<int>(n), static_cast<int>(pitch), n * pitch, center_weight,
+          w.z, static_cast<int>(n), static_cast<int>(n), static_cast<int>(pitch), n * pitch, center_weight,
           center_bias, static_cast<float>(center_eps), w.x);
     } else {
       xfb::ln_channel_major_kernel<64><<<blocks, 128, 0, st>>>(
-          w.z, static_cast<int>(n), static_cast<int>(pitch), n * pitch, center_weight,
+          w.z, static_cast<int>(n), static_cast<int>(n), static_cast<int>(pitch), n * pitch, center_weight,
           center_bias, static_cast<float>(center_eps), w.x);
     }
     XFB_LAUNCHED();
@@ -1346,6 +1346,264 @@ XFB_API int xfb_pair_logits(const void* pair, int pair_dtype, int64_t n, int64_t
   return run_layer_norm(pair, pair_dtype, n * n, c, c, norm_weight, norm_bias, eps, nullptr, 0,
                         nullptr, nullptr, static_cast<const bf16*>(w), static_cast<int>(heads),
                         static_cast<bf16*>(logits), n * n, static_cast<cudaStream_t>(stream));
+}
+
+
+// ---------------------------------------------------------------- row-block stages
+// The operators above take the whole N x N pair.  The entry points below run the
+// same arithmetic on a block of pair rows and stop where a row-sharded pair needs
+// an exchange between GPUs: TriMul projection | rows -> channels | contraction
+// (xfb_gemm) | channels -> rows | TriMul output; grid-attention prepare (LN and
+// the bias rows) | bias all-gather (and, for the ending node, a row <-> column
+// transpose of the LN'd pair) | grid attention on rows.  Every tensor here has
+// n % 8 == 0 columns so rows can be exchanged without padding.
+
+namespace {
+// Scores in log2 units (q and bias pre-multiplied by log2(e)) exactly when the
+// attention kernel streams the bias by TMA with 32-wide heads.
+bool grid_pre_scaled(int64_t c, int64_t heads, int64_t n) {
+  return head_pitch(static_cast<int>(c / heads)) == 32 && n % 8 == 0;
+}
+
+struct RowAttWs {
+  bf16 *q, *k, *v, *g, *o;
+  uint32_t* bits;
+};
+void row_att_layout(Carver& cv, int64_t rows, int64_t n, int64_t c, int64_t heads, RowAttWs* w) {
+  const int64_t dp = head_pitch(static_cast<int>(c / heads));
+  w->q = cv.take<bf16>(rows * heads * n * dp);
+  w->k = cv.take<bf16>(rows * heads * n * dp);
+  w->v = cv.take<bf16>(rows * heads * n * dp);
+  w->g = cv.take<bf16>(rows * n * c);
+  w->o = cv.take<bf16>(rows * n * c);
+  w->bits = cv.take<uint32_t>(rows * mask_words(n));
+}
+}  // namespace
+
+XFB_API int64_t xfb_triangle_projection_workspace(int64_t rows, int64_t n, int64_t c) {
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(rows * n * c);
+  return cv.used;
+}
+
+XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                    int64_t c, const float* mask, const float* left_weight,
+                                    const float* left_bias, double left_eps, const void* packed,
+                                    void* a, void* b, void* g, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
+  XFB_REQUIRE(c == 64 || c == 128, "triangle multiplication supports c in {64, 128}");
+  XFB_REQUIRE(packed != nullptr, "packed triangle weights are required");
+  XFB_REQUIRE(std::isfinite(left_eps) && left_eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(aligned16(a) && aligned16(b) && aligned16(g), "a, b, g must be 16-byte aligned");
+  if (rows == 0 || n == 0) return XFB_OK;
+  XFB_REQUIRE(rows * n <= (1ll << 31) - 256, "row block too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  bf16* x = cv.take<bf16>(rows * n * c);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  XFB_TRY(run_layer_norm(pair, pair_dtype, rows * n, c, c, left_weight, left_bias, left_eps, x, c,
+                         nullptr, nullptr, nullptr, 0, nullptr, 0, st));
+  xfb::EpiTriProj epi;
+  const uint64_t ab_dims[3] = {static_cast<uint64_t>(n), static_cast<uint64_t>(rows),
+                               static_cast<uint64_t>(c)};
+  const uint64_t ab_strides[2] = {static_cast<uint64_t>(n * 2), static_cast<uint64_t>(rows * n * 2)};
+  const uint32_t ab_box[3] = {128, 1, 32};
+  XFB_TRY(make_map_nd(&epi.a_map, false, 3, a, ab_dims, ab_strides, ab_box,
+                      CU_TENSOR_MAP_SWIZZLE_NONE));
+  XFB_TRY(make_map_nd(&epi.b_map, false, 3, b, ab_dims, ab_strides, ab_box,
+                      CU_TENSOR_MAP_SWIZZLE_NONE));
+  const uint64_t g_dims[3] = {static_cast<uint64_t>(c), static_cast<uint64_t>(n),
+                              static_cast<uint64_t>(rows)};
+  const uint64_t g_strides[2] = {static_cast<uint64_t>(c * 2), static_cast<uint64_t>(n * c * 2)};
+  const uint32_t g_box[3] = {64, 128, 1};
+  XFB_TRY(make_map_nd(&epi.g_map, false, 3, g, g_dims, g_strides, g_box,
+                      CU_TENSOR_MAP_SWIZZLE_128B));
+  epi.mask = mask;
+  epi.n = static_cast<int>(n);
+  epi.n_proj_tiles = static_cast<int>(2 * c / 64);
+  epi.c = static_cast<int>(c);
+  return run_gemm<128, false, false>(x, c, n * c, packed, c, 0, n, 5 * c, c, rows, epi, st, true);
+}
+
+XFB_API int64_t xfb_triangle_output_workspace(int64_t rows, int64_t n, int64_t c) {
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(rows * n * c);
+  return cv.used;
+}
+
+XFB_API int xfb_triangle_output(const void* z, int64_t rows, int64_t n, int64_t c, const void* g,
+                                const float* center_weight, const float* center_bias,
+                                double center_eps, const void* output_weight, void* out,
+                                int out_dtype, int accumulate, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
+  XFB_REQUIRE(c == 64 || c == 128, "triangle multiplication supports c in {64, 128}");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(std::isfinite(center_eps) && center_eps >= 0,
+              "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(output_weight != nullptr && g != nullptr, "output weight and gate are required");
+  if (rows == 0 || n == 0) return XFB_OK;
+  XFB_REQUIRE(rows * n <= (1ll << 31) - 256, "row block too large");
+  XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  bf16* x = cv.take<bf16>(rows * n * c);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int blocks = static_cast<int>(std::min<int64_t>((rows * n + 127) / 128, int64_t(sms) * 8));
+  const bf16* zz = static_cast<const bf16*>(z);
+  if (c == 128) {
+    xfb::ln_channel_major_kernel<128><<<blocks, 128, 0, st>>>(
+        zz, static_cast<int>(rows), static_cast<int>(n), static_cast<int>(n), rows * n,
+        center_weight, center_bias, static_cast<float>(center_eps), x);
+  } else {
+    xfb::ln_channel_major_kernel<64><<<blocks, 128, 0, st>>>(
+        zz, static_cast<int>(rows), static_cast<int>(n), static_cast<int>(n), rows * n,
+        center_weight, center_bias, static_cast<float>(center_eps), x);
+  }
+  XFB_LAUNCHED();
+  return linear_core(x, rows * n, c, c, static_cast<const bf16*>(output_weight), c, nullptr,
+                     static_cast<const bf16*>(g), c, out, out_dtype == XFB_F32, accumulate, c, st);
+}
+
+XFB_API int xfb_grid_attention_prepare(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                       int64_t c, int64_t heads, const float* norm_weight,
+                                       const float* norm_bias, double eps, const void* bias_weight,
+                                       void* x, void* bias, void* stream) {
+  XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
+  XFB_REQUIRE(c == 64 || c == 128, "grid self-attention supports c in {64, 128}");
+  XFB_REQUIRE(heads > 0 && heads <= 16 && c % heads == 0, "heads must divide c (<= 16)");
+  XFB_REQUIRE(bias_weight != nullptr && x != nullptr && bias != nullptr,
+              "bias weight and outputs are required");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  if (rows == 0 || n == 0) return XFB_OK;
+  const float scale = grid_pre_scaled(c, heads, n) ? 1.4426950408889634f : 1.f;
+  return run_layer_norm(pair, pair_dtype, rows * n, c, c, norm_weight, norm_bias, eps,
+                        static_cast<bf16*>(x), c, nullptr, nullptr,
+                        static_cast<const bf16*>(bias_weight), static_cast<int>(heads),
+                        static_cast<bf16*>(bias), rows * n, static_cast<cudaStream_t>(stream),
+                        scale);
+}
+
+XFB_API int64_t xfb_grid_attention_rows_workspace(int64_t rows, int64_t n, int64_t c,
+                                                  int64_t heads) {
+  if (heads <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  RowAttWs w;
+  row_att_layout(cv, rows, n, c, heads, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int64_t c,
+                                    int64_t heads, const float* mask, const void* bias,
+                                    const void* packed, const void* output_w, void* out,
+                                    int out_dtype, int accumulate, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
+  XFB_REQUIRE(c == 64 || c == 128, "grid self-attention supports c in {64, 128}");
+  XFB_REQUIRE(heads > 0 && heads <= 16 && c % heads == 0, "heads must divide c (<= 16)");
+  const int64_t d = c / heads;
+  XFB_REQUIRE(d == 16 || d == 32, "grid self-attention head dim must be 16 or 32");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(packed != nullptr && output_w != nullptr && bias != nullptr,
+              "packed weights, output weight and bias are required");
+  if (rows == 0 || n == 0) return XFB_OK;
+  XFB_REQUIRE(n <= 16384 && rows * n <= (1ll << 31) - 256, "row block too large");
+  XFB_REQUIRE(aligned16(out) && aligned16(bias), "output and bias must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  RowAttWs w;
+  row_att_layout(cv, rows, n, c, heads, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int dp = head_pitch(static_cast<int>(d));
+  const bool pre = grid_pre_scaled(c, heads, n);
+  const float log2e = 1.4426950408889634f;
+  const bf16* xx = static_cast<const bf16*>(x);
+  const bf16* wcat = static_cast<const bf16*>(packed);
+  if (d != dp) {
+    const int64_t bytes = rows * heads * n * dp * 2;
+    XFB_CUDA(cudaMemsetAsync(w.q, 0, bytes, st));
+    XFB_CUDA(cudaMemsetAsync(w.k, 0, bytes, st));
+    XFB_CUDA(cudaMemsetAsync(w.v, 0, bytes, st));
+  }
+  if (c == 128 && heads == 4) {
+    xfb::EpiAttProjTma epi;
+    bf16* bufs[3] = {w.q, w.k, w.v};
+    for (int t = 0; t < 3; ++t) {
+      const uint64_t dims[3] = {32, static_cast<uint64_t>(n), static_cast<uint64_t>(rows * 4)};
+      const uint64_t strides[2] = {64, static_cast<uint64_t>(n * 64)};
+      const uint32_t box[3] = {32, 128, 1};
+      XFB_TRY(make_map_nd(&epi.qkv_map[t], false, 3, bufs[t], dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_64B));
+    }
+    const uint64_t g_dims[3] = {static_cast<uint64_t>(c), static_cast<uint64_t>(n),
+                                static_cast<uint64_t>(rows)};
+    const uint64_t g_strides[2] = {static_cast<uint64_t>(c * 2), static_cast<uint64_t>(n * c * 2)};
+    const uint32_t g_box[3] = {64, 128, 1};
+    XFB_TRY(make_map_nd(&epi.g_map, false, 3, w.g, g_dims, g_strides, g_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
+    epi.q_scale = (pre ? log2e : 1.f) / std::sqrt(static_cast<float>(d));
+    epi.transpose = 0;
+    XFB_TRY((run_gemm<128, false, false>(xx, c, n * c, wcat, c, 0, n, 4 * c, c, rows, epi, st,
+                                         true)));
+  } else {
+    xfb::EpiAttProjDirect epi;
+    epi.q = w.q;
+    epi.k = w.k;
+    epi.v = w.v;
+    epi.g = w.g;
+    epi.n = static_cast<int>(n);
+    epi.c = static_cast<int>(c);
+    epi.heads = static_cast<int>(heads);
+    epi.d = static_cast<int>(d);
+    epi.dp = dp;
+    epi.transpose = 0;
+    epi.M = static_cast<int>(rows * n);
+    epi.q_scale = (pre ? log2e : 1.f) / std::sqrt(static_cast<float>(d));
+    epi.q_bias = nullptr;
+    XFB_TRY((run_gemm<128, false, false>(xx, c, 0, wcat, c, 0, rows * n, 4 * c, c, 1, epi, st)));
+  }
+  xfb::AttnArgs a;
+  a.B = static_cast<int>(rows);
+  a.H = static_cast<int>(heads);
+  a.nq = static_cast<int>(n);
+  a.nk = static_cast<int>(n);
+  a.d = static_cast<int>(d);
+  if (mask != nullptr) XFB_TRY(launch_mask_bits(mask, true, rows, n, n, w.bits, st));
+  a.mask_bits = mask ? w.bits : nullptr;
+  a.mask_sb = mask_words(n);
+  a.bias = bias;
+  a.bias_sb = 0;
+  a.bias_sh = n * n;
+  a.bias_sq = n;
+  a.bias_batched = 0;
+  a.out = w.o;
+  a.out_sb = n * c;
+  a.out_sh = d;
+  a.out_sq = c;
+  a.gate = w.g;
+  a.gate_sb = a.out_sb;
+  a.gate_sh = a.out_sh;
+  a.gate_sq = a.out_sq;
+  XFB_TRY(run_flash(dp, XFB_BF16, pre, w.q, w.k, w.v, a, st));
+  return linear_core(w.o, rows * n, c, c, static_cast<const bf16*>(output_w), c, nullptr, nullptr,
+                     0, out, out_dtype == XFB_F32, accumulate, c, st);
+}
+
+XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                 int64_t c, int64_t heads, const float* norm_weight,
+                                 const float* norm_bias, double eps, const void* w, void* logits,
+                                 void* stream) {
+  XFB_REQUIRE(rows >= 0 && n >= 0 && heads > 0 && heads <= 16, "pair logits expect 1..16 heads");
+  XFB_REQUIRE(c == 64 || c == 128, "pair width must be 64 or 128");
+  if (rows == 0 || n == 0) return XFB_OK;
+  return run_layer_norm(pair, pair_dtype, rows * n, c, c, norm_weight, norm_bias, eps, nullptr, 0,
+                        nullptr, nullptr, static_cast<const bf16*>(w), static_cast<int>(heads),
+                        static_cast<bf16*>(logits), rows * n, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

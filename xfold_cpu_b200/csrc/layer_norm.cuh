@@ -8,8 +8,9 @@
 //   projections, H <= 16) reduced with a transposing butterfly.
 //
 // ln_channel_major_kernel: one thread per position of a channel-major
-//   [C][n][pitch] bf16 tensor (the triangle contraction output); writes the
-//   normalised row-major [n*n][C] bf16 tensor the output projection reads.
+//   [C][rows][pitch] bf16 tensor (the triangle contraction output, n valid
+//   columns); writes the normalised row-major [rows*n][C] bf16 tensor the output
+//   projection reads.
 #pragma once
 
 #include "common.cuh"
@@ -202,9 +203,9 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
 // Channel-major LayerNorm: x(ch, i, j) = in[ch*chan_stride + i*pitch + j].
 template <int C>
 __global__ void __launch_bounds__(128) ln_channel_major_kernel(
-    const __nv_bfloat16* in, int n, int pitch, int64_t chan_stride, const float* w,
+    const __nv_bfloat16* in, int rows, int n, int pitch, int64_t chan_stride, const float* w,
     const float* b, float eps, __nv_bfloat16* y) {
-  const int64_t total = static_cast<int64_t>(n) * n;
+  const int64_t total = static_cast<int64_t>(rows) * n;
   for (int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; pos < total;
        pos += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int i = static_cast<int>(pos / n);

@@ -395,3 +395,134 @@ def pair_logits(pair: torch.Tensor, norm_weight: torch.Tensor | None,
     _capi.call("xfb_pair_logits", _ptr(pair), _code(pair), n, c, heads, _ptr(nw), _ptr(nb),
                float(eps), _ptr(w), _ptr(logits), _stream(device))
     return logits
+
+
+# ----------------------------------------------------------------------------- row-block stages
+# The operators above take the whole pair.  These run them on a block of pair
+# rows and stop where a row-sharded pair exchanges data between GPUs
+# (xfold_cpu_b200/sharded.py).  Every block has n % 8 == 0 columns.
+
+def _rows_of(t: torch.Tensor, name: str) -> tuple[int, int, int]:
+    if t.dim() != 3:
+        raise ValueError(f"{name} must be a [rows, n, c] row block")
+    rows, n, c = t.shape
+    if n % 8:
+        raise ValueError(f"{name}: row blocks need n % 8 == 0 columns")
+    return rows, n, c
+
+
+def triangle_projection(pair: torch.Tensor, mask: torch.Tensor | None,
+                        left_weight: torch.Tensor, left_bias: torch.Tensor | None,
+                        left_eps: float, packed: torch.Tensor):
+    """TriMul stage 1 on pair rows [rows, n, c]: returns a, b channel-major
+    [c, rows, n] bf16 (projection channels 2k / 2k+1, masked and gated) and the
+    output gate g [rows, n, c] (triangle_multiplication.py:71-95)."""
+    device = _check_cuda(pair, mask, left_weight, packed)
+    rows, n, c = _rows_of(pair, "pair")
+    pair = _contig(pair)
+    if mask is not None:
+        mask = _contig(mask.expand(rows, n), torch.float32)
+    a = torch.empty((c, rows, n), dtype=torch.bfloat16, device=device)
+    b = torch.empty_like(a)
+    g = torch.empty((rows, n, c), dtype=torch.bfloat16, device=device)
+    lw, lb = _contig(left_weight, torch.float32), _contig(left_bias, torch.float32)
+    ws = _workspace(_capi.load().xfb_triangle_projection_workspace(rows, n, c), device)
+    _capi.call("xfb_triangle_projection", _ptr(pair), _code(pair), rows, n, c, _ptr(mask),
+               _ptr(lw), _ptr(lb), float(left_eps), _ptr(packed), _ptr(a), _ptr(b), _ptr(g),
+               _ptr(ws), ws.numel(), _stream(device))
+    return a, b, g
+
+
+def triangle_contraction(a: torch.Tensor, b: torch.Tensor, outgoing: bool) -> torch.Tensor:
+    """TriMul contraction of a channel shard, a and b [cs, n, n] channel-major:
+    outgoing z[c,i,j] = sum_k a[c,i,k] b[c,j,k]; incoming sum_k a[c,k,j] b[c,k,i]
+    (triangle_multiplication.py:34-36).  bf16 out, f32 accumulation."""
+    if outgoing:
+        return gemm(a, b, mn_major=False, out_dtype=torch.bfloat16)
+    return gemm(b, a, mn_major=True, out_dtype=torch.bfloat16)
+
+
+def triangle_output(z: torch.Tensor, g: torch.Tensor, center_weight: torch.Tensor,
+                    center_bias: torch.Tensor | None, center_eps: float,
+                    output_weight: torch.Tensor, out: torch.Tensor | None = None,
+                    accumulate: bool = False, out_dtype: torch.dtype = torch.bfloat16):
+    """TriMul stage 3 on a row block: z channel-major [c, rows, n] (the
+    contraction for these rows), g from stage 1; returns (LN_c(z) W_o^T) * g, or
+    adds it into f32 `out` [rows, n, c] (triangle_multiplication.py:96-105)."""
+    device = _check_cuda(z, g, center_weight, output_weight)
+    c, rows, n = z.shape
+    z, g = _contig(z, torch.bfloat16), _contig(g, torch.bfloat16)
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate=True needs an output tensor")
+        out = torch.empty((rows, n, c), dtype=out_dtype, device=device)
+    cw, cb = _contig(center_weight, torch.float32), _contig(center_bias, torch.float32)
+    ow = prepare_weight(output_weight)
+    ws = _workspace(_capi.load().xfb_triangle_output_workspace(rows, n, c), device)
+    _capi.call("xfb_triangle_output", _ptr(z), rows, n, c, _ptr(g), _ptr(cw), _ptr(cb),
+               float(center_eps), _ptr(ow), _ptr(out), _code(out), 1 if accumulate else 0,
+               _ptr(ws), ws.numel(), _stream(device))
+    return out
+
+
+def grid_attention_prepare(pair: torch.Tensor, norm_weight: torch.Tensor | None,
+                           norm_bias: torch.Tensor | None, eps: float,
+                           bias_weight: torch.Tensor, num_head: int):
+    """Grid attention stage 1 on pair rows: x = LN(rows) bf16 [rows, n, c] and the
+    bias rows [heads, rows, n] bf16 (attention.py:86-98), in the units
+    grid_attention_rows expects."""
+    device = _check_cuda(pair, bias_weight)
+    rows, n, c = _rows_of(pair, "pair")
+    pair = _contig(pair)
+    x = torch.empty((rows, n, c), dtype=torch.bfloat16, device=device)
+    bias = torch.empty((num_head, rows, n), dtype=torch.bfloat16, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    bw = prepare_weight(bias_weight)
+    _capi.call("xfb_grid_attention_prepare", _ptr(pair), _code(pair), rows, n, c, num_head,
+               _ptr(nw), _ptr(nb), float(eps), _ptr(bw), _ptr(x), _ptr(bias), _stream(device))
+    return x, bias
+
+
+def grid_attention_rows(x: torch.Tensor, mask: torch.Tensor | None, bias: torch.Tensor,
+                        packed: torch.Tensor, output_weight: torch.Tensor, num_head: int,
+                        out: torch.Tensor | None = None, accumulate: bool = False,
+                        out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Grid attention stage 2: x = LN'd rows [rows, n, c] (pair rows, or pair
+    columns for the ending node), mask [rows, n] key mask of those rows, bias
+    [heads, n, n] assembled from stage 1 of every row block (attention.py:61-78,
+    99-105)."""
+    device = _check_cuda(x, mask, bias, packed, output_weight)
+    rows, n, c = _rows_of(x, "x")
+    x = _contig(x, torch.bfloat16)
+    if mask is not None:
+        mask = _contig(mask.expand(rows, n), torch.float32)
+    bias = _contig(bias, torch.bfloat16)
+    if bias.shape != (num_head, n, n):
+        raise ValueError("bias must be [heads, n, n]")
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate=True needs an output tensor")
+        out = torch.empty((rows, n, c), dtype=out_dtype, device=device)
+    ow = prepare_weight(output_weight)
+    ws = _workspace(_capi.load().xfb_grid_attention_rows_workspace(rows, n, c, num_head), device)
+    _capi.call("xfb_grid_attention_rows", _ptr(x), rows, n, c, num_head, _ptr(mask), _ptr(bias),
+               _ptr(packed), _ptr(ow), _ptr(out), _code(out), 1 if accumulate else 0, _ptr(ws),
+               ws.numel(), _stream(device))
+    return out
+
+
+def pair_logits_rows(pair: torch.Tensor, norm_weight: torch.Tensor | None,
+                     norm_bias: torch.Tensor | None, eps: float,
+                     weight: torch.Tensor) -> torch.Tensor:
+    """Pair-logit projection of a row block: [heads, rows, n] bf16
+    (pairformer.py:103-106)."""
+    device = _check_cuda(pair, weight)
+    rows, n, c = pair.shape
+    heads = weight.shape[0]
+    pair = _contig(pair)
+    logits = torch.empty((heads, rows, n), dtype=torch.bfloat16, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    w = prepare_weight(weight)
+    _capi.call("xfb_pair_logits_rows", _ptr(pair), _code(pair), rows, n, c, heads, _ptr(nw),
+               _ptr(nb), float(eps), _ptr(w), _ptr(logits), _stream(device))
+    return logits
