@@ -285,6 +285,16 @@ def run_cuda(args) -> None:
         init_params_(blk, seed=SEED * 1000 + i)
         blocks.append(blk.to(dev))
     pair_h, pair_mask_h, single_h, seq_mask_h = _inputs(n_tok, SEED)
+    if world > 1:
+        # row-sharded pair: this rank holds rows R_rank of the one N x N trunk
+        from xfold_cpu_b200 import sharded
+
+        sharded.check_sharding(n_tok, C_PAIR, world)
+        pair_h = pair_h[sharded.shard_rows(n_tok, world, rank)].contiguous()
+        # peer stores over NVLink by default; XFB_EXCHANGE=collective uses NCCL all-to-all
+        exchange = (sharded.ProcessGroupExchange()
+                    if os.environ.get("XFB_EXCHANGE", "peer") == "collective"
+                    else sharded.PeerExchange())
     pair_h, pair_mask_h = pair_h.pin_memory(), pair_mask_h.pin_memory()
     single_h, seq_mask_h = single_h.pin_memory(), seq_mask_h.pin_memory()
     pair = pair_h.to(dev)
@@ -295,7 +305,10 @@ def run_cuda(args) -> None:
 
     def trunk(p, s, pm, sm):
         for blk in blocks:
-            blk(p, pm, s, sm)
+            if world > 1:
+                sharded.pairformer_block(blk, [p], pm, s, sm, exchange)
+            else:
+                blk(p, pm, s, sm)
         return p, s
 
     with torch.inference_mode():
@@ -362,15 +375,23 @@ def run_cuda(args) -> None:
     line = {
         "metric": METRIC, "value": round(step_ms / n_blocks, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": False, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) pair/single, random-init N(0,0.02) weights)",
         "config": {"workload": "48-block Pairformer trunk, N_token=1024 (BASELINE config C4)",
                    "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR, "c_single": C_SINGLE,
                    "heads_pair": 4, "heads_single": 16, "seed": SEED, "mask": "64-token padded tail",
                    "l2": "inputs larger than L2 (pair f32 = 512 MiB)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                   "parallelism": (f"row-sharded pair over {world} GPUs ("
+                                   + ("NCCL all-to-all / all-gather"
+                                      if os.environ.get("XFB_EXCHANGE", "peer") == "collective"
+                                      else "peer-store exchange kernel over NVLink + NCCL barrier")
+                                   + ")") if world > 1 else "single GPU"},
         "e2e": {"value": round(e2e_ms / n_blocks, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "note": "step = one 48-block trunk pass; host pinned in/out"},
+                "d2h_bytes_per_step": d2h,
+                "note": "step = one 48-block trunk pass; host pinned in/out"
+                        + ("; bytes per rank (its pair rows, the masks, the single copy)"
+                           if world > 1 else "")},
         "gpu_launches": int(launches),
         "roofline": ({**{k: v for k, v in dominant.items()},
                       "kernel": [k for k, v in roof.items() if v is dominant][0],

@@ -309,6 +309,34 @@ XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows,
                                  const float* norm_bias, double eps, const void* w, void* logits,
                                  void* stream);
 
+/* One block of an exchange between GPUs of a row-sharded pair: copy
+ * [d0][d1][d2_bytes] from src to dst with byte strides (runs of d2_bytes are
+ * contiguous on both sides).  dst may be another GPU's receive buffer mapped
+ * into this process by CUDA IPC; the copy uses plain 16-byte loads and stores
+ * (every size, stride and pointer a multiple of 16 bytes). */
+typedef struct {
+  const void* src;
+  void* dst;
+  int64_t d0, d1, d2_bytes;
+  int64_t src_stride0, src_stride1;
+  int64_t dst_stride0, dst_stride1;
+} xfb_copy_box;
+
+/* Copies up to 16 boxes in one launch, ending with a system-scope fence so a
+ * peer that synchronises with this stream afterwards (the caller's barrier)
+ * sees every store.  No counterpart in the reference (it has no multi-GPU pair). */
+XFB_API int xfb_exchange_copy(const xfb_copy_box* boxes, int count, void* stream);
+
+/* CUDA IPC for the exchange receive buffers (no counterpart in the reference).
+ * xfb_ipc_handle: the IPC handle (xfb_ipc_handle_bytes() bytes) of the device
+ * allocation holding ptr, and ptr's byte offset in it.  xfb_ipc_open: maps a
+ * peer process's allocation on the current device with lazy peer access and
+ * returns the address of the peer's ptr; xfb_ipc_close unmaps it. */
+XFB_API int64_t xfb_ipc_handle_bytes(void);
+XFB_API int xfb_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+XFB_API int xfb_ipc_open(const void* handle, int64_t offset, void** peer_ptr);
+XFB_API int xfb_ipc_close(void* peer_ptr, int64_t offset);
+
 #ifdef __cplusplus
 }
 #endif

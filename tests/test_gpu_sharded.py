@@ -198,3 +198,75 @@ def test_sharded_block_over_nccl():
         assert p.exitcode == 0
     assert results["err0"] == 0 and results["err1"] == 0
     assert results["pair"] < TOL and results["single"] < TOL
+
+
+def _peer_worker(rank, world, port, n, results):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "NCCL_NVLS_ENABLE": "0"})
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        peer, coll = sharded.PeerExchange(), sharded.ProcessGroupExchange()
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        rows = n // world
+        cases = {
+            "rows_to_channels": torch.randn(128, rows, n, device=dev, generator=g).bfloat16(),
+            "channels_to_rows": torch.randn(128 // world, n, n, device=dev, generator=g).bfloat16(),
+            "gather_rows": torch.randn(4, rows, n, device=dev, generator=g).bfloat16(),
+            "transpose": torch.randn(rows, n, 128, device=dev, generator=g).bfloat16(),
+        }
+        same = {}
+        for name, t in cases.items():
+            for _ in range(3):  # both receive copies and a reuse of the first
+                got = getattr(peer, name)([t])[0].clone()
+                want = getattr(coll, name)([t])[0]
+                same[name] = bool(torch.equal(got, want))
+                if not same[name]:
+                    break
+        results[f"same{rank}"] = same
+        block, pair, single, seq, pmask = _problem(n)
+        params = {k: v.detach().clone() for k, v in block.state_dict().items()}
+        block = block.to(dev)
+        mine = [pair[sharded.shard_rows(n, world, rank)].to(dev).contiguous()]
+        s = single.to(dev)
+        with torch.inference_mode():
+            for _ in range(2):  # two blocks: the exchanges reuse their receive buffers
+                sharded.pairformer_block(block, mine, pmask.to(dev), s, seq.to(dev), peer)
+            gathered = [torch.empty_like(mine[0]) for _ in range(world)]
+            dist.all_gather(gathered, mine[0])
+        torch.cuda.synchronize(dev)
+        results[f"err{rank}"] = int(_capi.device_error(clear=True))
+        if rank == 0:
+            ref_p, ref_s = oracle.pairformer_block(pair, pmask, single, seq, params)
+            ref_p, ref_s = oracle.pairformer_block(ref_p, pmask, ref_s, seq, params)
+            got = torch.cat([t.cpu() for t in gathered])
+            results["pair"] = oracle.relative_error(got - pair, ref_p - pair)
+            results["single"] = oracle.relative_error(s.cpu() - single, ref_s - single)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_over_nvlink():
+    world, n = 2, 128
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, n, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert all(results[f"same{r}"].values()), results[f"same{r}"]
+        assert results[f"err{r}"] == 0
+    assert results["pair"] < TOL and results["single"] < TOL

@@ -87,7 +87,21 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_grid_attention_rows": (
         _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _i64, _p]),
     "xfb_pair_logits_rows": (_i, [_p, _i, _i64, _i64, _i64, _i64, _p, _p, _d, _p, _p, _p]),
+    "xfb_exchange_copy": (_i, [_p, _i, _p]),
+    "xfb_ipc_handle_bytes": (_i64, []),
+    "xfb_ipc_handle": (_i, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),
+    "xfb_ipc_open": (_i, [_p, _i64, ctypes.POINTER(ctypes.c_void_p)]),
+    "xfb_ipc_close": (_i, [_p, _i64]),
 }
+
+
+class CopyBox(ctypes.Structure):
+    """xfb_copy_box (include/xfold_b200.h)."""
+
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("d0", ctypes.c_int64),
+                ("d1", ctypes.c_int64), ("d2_bytes", ctypes.c_int64),
+                ("src_stride0", ctypes.c_int64), ("src_stride1", ctypes.c_int64),
+                ("dst_stride0", ctypes.c_int64), ("dst_stride1", ctypes.c_int64)]
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

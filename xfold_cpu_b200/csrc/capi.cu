@@ -14,6 +14,7 @@
 
 #include "../../include/xfold_b200.h"
 #include "attention.cuh"
+#include "exchange.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
 #include "layer_norm.cuh"
@@ -1604,6 +1605,95 @@ XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows,
   return run_layer_norm(pair, pair_dtype, rows * n, c, c, norm_weight, norm_bias, eps, nullptr, 0,
                         nullptr, nullptr, static_cast<const bf16*>(w), static_cast<int>(heads),
                         static_cast<bf16*>(logits), rows * n, static_cast<cudaStream_t>(stream));
+}
+
+
+XFB_API int xfb_exchange_copy(const xfb_copy_box* boxes, int count, void* stream) {
+  XFB_REQUIRE(count >= 0 && count <= xfb::kMaxCopyBoxes, "exchange copy takes at most 16 boxes");
+  XFB_REQUIRE(count == 0 || boxes != nullptr, "exchange copy boxes missing");
+  xfb::CopyBoxes kb;
+  memset(&kb, 0, sizeof(kb));
+  kb.count = count;
+  uint64_t largest = 0;
+  for (int i = 0; i < count; ++i) {
+    const xfb_copy_box& b = boxes[i];
+    XFB_REQUIRE(b.d0 >= 0 && b.d1 >= 0 && b.d2_bytes >= 0, "exchange copy extents must be >= 0");
+    XFB_REQUIRE(b.d2_bytes % 16 == 0 && b.src_stride0 % 16 == 0 && b.src_stride1 % 16 == 0 &&
+                    b.dst_stride0 % 16 == 0 && b.dst_stride1 % 16 == 0,
+                "exchange copy runs and strides must be multiples of 16 bytes");
+    XFB_REQUIRE(b.src_stride0 >= 0 && b.src_stride1 >= 0 && b.dst_stride0 >= 0 && b.dst_stride1 >= 0,
+                "exchange copy strides must be non-negative");
+    const uint64_t vecs = static_cast<uint64_t>(b.d0) * b.d1 * (b.d2_bytes / 16);
+    XFB_REQUIRE(vecs == 0 || (aligned16(b.src) && aligned16(b.dst)),
+                "exchange copy pointers must be 16-byte aligned");
+    XFB_REQUIRE(b.d0 < (1ll << 32) && b.d1 < (1ll << 32) && b.d2_bytes / 16 < (1ll << 32),
+                "exchange copy extent too large");
+    xfb::CopyBox& k = kb.box[i];
+    k.src = static_cast<const uint4*>(b.src);
+    k.dst = static_cast<uint4*>(b.dst);
+    k.d0 = static_cast<uint32_t>(b.d0);
+    k.d1 = static_cast<uint32_t>(b.d1);
+    k.d2 = static_cast<uint32_t>(b.d2_bytes / 16);
+    k.s0 = b.src_stride0 / 16;
+    k.s1 = b.src_stride1 / 16;
+    k.t0 = b.dst_stride0 / 16;
+    k.t1 = b.dst_stride1 / 16;
+    largest = std::max(largest, vecs);
+  }
+  if (largest == 0) return XFB_OK;
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const uint64_t want = (largest + 255) / 256;
+  const uint64_t cap = std::max<uint64_t>(1, static_cast<uint64_t>(sms) * 8 / count);
+  dim3 grid(static_cast<unsigned>(std::min(want, cap)), count);
+  xfb::exchange_copy_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(kb);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+
+// ---------------------------------------------------------------- CUDA IPC for exchanges
+
+XFB_API int64_t xfb_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+XFB_API int xfb_ipc_handle(const void* ptr, void* handle, int64_t* offset) {
+  XFB_REQUIRE(ptr != nullptr && handle != nullptr && offset != nullptr, "ipc handle arguments missing");
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  XFB_REQUIRE(range_fn != nullptr, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(XFB_ERR_CUDA, "cuMemGetAddressRange failed for the exchange buffer");
+  cudaIpcMemHandle_t h;
+  XFB_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return XFB_OK;
+}
+
+XFB_API int xfb_ipc_open(const void* handle, int64_t offset, void** peer_ptr) {
+  XFB_REQUIRE(handle != nullptr && peer_ptr != nullptr && offset >= 0, "ipc open arguments missing");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  XFB_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  *peer_ptr = static_cast<uint8_t*>(base) + offset;
+  return XFB_OK;
+}
+
+XFB_API int xfb_ipc_close(void* peer_ptr, int64_t offset) {
+  XFB_REQUIRE(peer_ptr != nullptr && offset >= 0, "ipc close arguments missing");
+  XFB_CUDA(cudaIpcCloseMemHandle(static_cast<uint8_t*>(peer_ptr) - offset));
+  return XFB_OK;
 }
 
 }  // extern "C"

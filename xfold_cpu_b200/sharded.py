@@ -21,19 +21,20 @@ the arithmetic crosses rows:
 * Single track: the pair-logit rows are all-gathered; the single representation
   (N x 384) is replicated and every process updates its own copy identically.
 
-Exchanges go through an `Exchange`: `ProcessGroupExchange` (one shard per
-process over torch.distributed -- NCCL over NVLink on GPUs, gloo on CPU) or
+Exchanges go through one of three classes with the same four patterns:
+`PeerExchange` (one shard per GPU: the library's copy kernel stores each chunk
+straight into the peers' receive buffers over NVLink, then a one-element NCCL
+all-reduce is the barrier), `ProcessGroupExchange` (one shard per process over
+torch.distributed all-to-all / all-gather -- NCCL on GPUs, gloo on CPU) and
 `LocalExchange` (all shards in one process, for checking the sharded arithmetic
-on one device).  Exchanges copy whole tensors into this GPU's memory; no kernel
-reads another GPU's memory.
+on one device).  No kernel reads another GPU's memory: peer traffic is stores
+only, and no TMA or multicast is involved.
 
 The compute of each stage comes from a `stages` object; `NativeStages` (the
 CUDA kernels) is the default and the only one this package provides.
 """
 
 from __future__ import annotations
-
-from typing import Protocol
 
 import torch
 
@@ -42,21 +43,56 @@ from .nn.modules import (GridSelfAttention, PairformerBlock, TriangleMultiplicat
 
 
 # ----------------------------------------------------------------------------- exchanges
+# An exchange moves row-sharded data between the G ranks.  The driver needs four
+# patterns; each takes one tensor per local shard (in `ranks` order) and returns
+# one per local shard:
+#   rows_to_channels   [c, rows, n]  -> [c/G, n, n]   (rows of every rank, my channels)
+#   channels_to_rows   [c/G, n, n]   -> [c, rows, n]  (channels of every rank, my rows)
+#   gather_rows        [h, rows, n]  -> [h, n, n]     (every rank's rows)
+#   transpose          [rows, n, c]  -> [rows, n, c]  (x[i, j] -> y[j, i]: my columns, all rows)
 
-class Exchange(Protocol):
+
+class CollectiveExchange:
+    """The four patterns from all-to-all / all-gather primitives plus tensor
+    permutes.  Subclasses provide `world`, `ranks`, `all_to_all` (bufs[l] is
+    [G, ...], chunk s for rank s; returns [G, ...], chunk t from rank t) and
+    `all_gather` (returns [G, ...], rank t's tensor at t)."""
+
     world: int
-    ranks: list[int]  # global rank of each local shard
+    ranks: list[int]
 
-    def all_to_all(self, bufs: list[torch.Tensor]) -> list[torch.Tensor]:
-        """bufs[l] is [G, ...] (chunk s goes to rank s); returns [G, ...] per
-        local shard (chunk t came from rank t)."""
+    def rows_to_channels(self, blocks):
+        g = self.world
+        c, rows, n = blocks[0].shape
+        recv = self.all_to_all([t.view(g, c // g, rows, n) for t in blocks])
+        return [t.transpose(0, 1).reshape(c // g, g * rows, n) for t in recv]
 
-    def all_gather(self, bufs: list[torch.Tensor]) -> list[torch.Tensor]:
-        """bufs[l] is [...]; returns [G, ...] per local shard (rank t's tensor at t)."""
+    def channels_to_rows(self, blocks):
+        g = self.world
+        cs, n, _ = blocks[0].shape
+        rows = n // g
+        sends = [t.view(cs, g, rows, n).transpose(0, 1).contiguous() for t in blocks]
+        return [t.view(g * cs, rows, n) for t in self.all_to_all(sends)]
+
+    def gather_rows(self, blocks):
+        gathered = self.all_gather(blocks)
+        return [t.transpose(0, 1).reshape(t.shape[1], -1, t.shape[-1]) for t in gathered]
+
+    def transpose(self, blocks):
+        g = self.world
+        sends = []
+        for x in blocks:
+            rows = x.shape[0]
+            sends.append(x.view(rows, g, rows, *x.shape[2:]).transpose(0, 1).contiguous())
+        out = []
+        for t in self.all_to_all(sends):  # [t, rows of t (i), my columns (j), ...]
+            g_, rows, cols = t.shape[:3]
+            out.append(t.permute(2, 0, 1, *range(3, t.dim())).reshape(cols, g_ * rows, *t.shape[3:]))
+        return out
 
 
-class ProcessGroupExchange:
-    """One shard per process over torch.distributed (NCCL or gloo)."""
+class ProcessGroupExchange(CollectiveExchange):
+    """One shard per process over torch.distributed collectives (NCCL or gloo)."""
 
     def __init__(self, group=None) -> None:
         import torch.distributed as dist
@@ -81,7 +117,7 @@ class ProcessGroupExchange:
         return [out.view(self.world, *buf.shape)]
 
 
-class LocalExchange:
+class LocalExchange(CollectiveExchange):
     """All G shards in this process (tensor copies stand in for the transfers)."""
 
     def __init__(self, world: int) -> None:
@@ -95,6 +131,153 @@ class LocalExchange:
     def all_gather(self, bufs):
         stacked = torch.stack(list(bufs))
         return [stacked.clone() for _ in range(self.world)]
+
+
+class PeerExchange:
+    """One shard per GPU; each pattern is one launch of the library's exchange
+    copy kernel that stores straight into the peers' receive buffers over NVLink
+    (mapped into this process by CUDA IPC), each chunk at its final position, so
+    no permute copies are needed on either side.  A one-element NCCL all-reduce
+    after the copy is the barrier: when it completes on a rank, every rank's
+    stores into that rank's buffer have landed.  Receive buffers alternate
+    between two copies per pattern, so the barrier after an exchange also
+    guarantees that nobody still reads the copy the next exchange overwrites
+    (every consumer of a buffer is enqueued before its rank's next barrier).
+    The returned tensors are views of those buffers: valid until the same
+    pattern with the same shape has run twice more."""
+
+    def __init__(self, group=None) -> None:
+        import torch.distributed as dist
+
+        self._dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.ranks = [self.rank]
+        self._bufs: dict = {}
+        self._flag = None
+
+    # -- receive buffers, shared once per (pattern, shape, dtype)
+    def _recv(self, kind, shape, dtype, device):
+        key = (kind, tuple(shape), dtype)
+        entry = self._bufs.get(key)
+        if entry is None:
+            copies = []
+            for _ in range(2):
+                local = torch.empty(shape, dtype=dtype, device=device)
+                metas = [None] * self.world
+                self._dist.all_gather_object(metas, _ipc_handle(local), group=self.group)
+                peers = [local.data_ptr() if r == self.rank else _ipc_open(*meta)
+                         for r, meta in enumerate(metas)]
+                copies.append((local, peers))
+            entry = {"copies": copies, "next": 0}
+            self._bufs[key] = entry
+        local, peers = entry["copies"][entry["next"]]
+        entry["next"] ^= 1
+        return local, peers
+
+    def _copy_and_sync(self, boxes, device):
+        from . import _capi
+
+        arr = (_capi.CopyBox * len(boxes))(*boxes)
+        _capi.call("xfb_exchange_copy", ctypes_addressof(arr), len(boxes),
+                   torch.cuda.current_stream(device).cuda_stream)
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self._dist.all_reduce(self._flag, group=self.group)
+
+    def _box(self, src_ptr, dst_ptr, d0, d1, d2_bytes, s0, s1, t0, t1):
+        from . import _capi
+
+        return _capi.CopyBox(src_ptr, dst_ptr, d0, d1, d2_bytes, s0, s1, t0, t1)
+
+    def rows_to_channels(self, blocks):
+        (a,) = blocks
+        g, r = self.world, self.rank
+        a = a.contiguous()
+        c, rows, n = a.shape
+        cs, e = c // g, a.element_size()
+        local, peers = self._recv("r2c", (cs, n, n), a.dtype, a.device)
+        boxes = [self._box(a.data_ptr() + s * cs * rows * n * e, peers[s] + r * rows * n * e,
+                           cs, rows, n * e, rows * n * e, n * e, n * n * e, n * e)
+                 for s in range(g)]
+        self._copy_and_sync(boxes, a.device)
+        return [local]
+
+    def channels_to_rows(self, blocks):
+        (z,) = blocks
+        g, r = self.world, self.rank
+        z = z.contiguous()
+        cs, n, _ = z.shape
+        rows, e = n // g, z.element_size()
+        local, peers = self._recv("c2r", (g * cs, rows, n), z.dtype, z.device)
+        boxes = [self._box(z.data_ptr() + s * rows * n * e, peers[s] + r * cs * rows * n * e,
+                           cs, rows, n * e, n * n * e, n * e, rows * n * e, n * e)
+                 for s in range(g)]
+        self._copy_and_sync(boxes, z.device)
+        return [local]
+
+    def gather_rows(self, blocks):
+        (t,) = blocks
+        g, r = self.world, self.rank
+        t = t.contiguous()
+        h, rows, n = t.shape
+        e = t.element_size()
+        local, peers = self._recv("gather", (h, g * rows, n), t.dtype, t.device)
+        boxes = [self._box(t.data_ptr(), peers[s] + r * rows * n * e,
+                           h, rows, n * e, rows * n * e, n * e, g * rows * n * e, n * e)
+                 for s in range(g)]
+        self._copy_and_sync(boxes, t.device)
+        return [local]
+
+    def transpose(self, blocks):
+        (x,) = blocks
+        g, r = self.world, self.rank
+        x = x.contiguous()
+        rows, n, c = x.shape
+        e = x.element_size()
+        local, peers = self._recv("transpose", (rows, n, c), x.dtype, x.device)
+        # x[ii, s*rows + jj, :] -> rank s's y[jj, r*rows + ii, :]
+        boxes = [self._box(x.data_ptr() + s * rows * c * e, peers[s] + r * rows * c * e,
+                           rows, rows, c * e, n * c * e, c * e, c * e, n * c * e)
+                 for s in range(g)]
+        self._copy_and_sync(boxes, x.device)
+        return [local]
+
+
+# PeerExchange, ProcessGroupExchange and LocalExchange share the four patterns
+# above (plus `world` and `ranks`), which is all pairformer_block uses.
+
+
+def _ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """IPC handle of the allocation holding t, and t's byte offset in it."""
+    import ctypes
+
+    from . import _capi
+
+    lib = _capi.load()
+    buf = ctypes.create_string_buffer(int(lib.xfb_ipc_handle_bytes()))
+    off = ctypes.c_int64(0)
+    _capi.call("xfb_ipc_handle", t.data_ptr(), buf, ctypes.byref(off))
+    return buf.raw, off.value
+
+
+def _ipc_open(handle: bytes, offset: int) -> int:
+    """Maps a peer's allocation on the current device; the address of its tensor."""
+    import ctypes
+
+    from . import _capi
+
+    ptr = ctypes.c_void_p(0)
+    _capi.call("xfb_ipc_open", ctypes.create_string_buffer(handle, len(handle)), offset,
+               ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def ctypes_addressof(arr) -> int:
+    import ctypes
+
+    return ctypes.addressof(arr)
 
 
 # ----------------------------------------------------------------------------- stages
@@ -166,70 +349,38 @@ def check_sharding(n: int, c: int, world: int) -> None:
 def _triangle(mod, pairs, pair_mask, exchange, stages):
     g = exchange.world
     rows, n, c = pairs[0].shape
-    cs = c // g
-    a_list, b_list, g_list = [], [], []
-    for pair, r in zip(pairs, exchange.ranks):
-        a, b, gate = stages.trimul_project(mod, pair, pair_mask[shard_rows(n, g, r)])
-        a_list.append(a.view(g, cs, rows, n))  # chunk s = channels of rank s
-        b_list.append(b.view(g, cs, rows, n))
-        g_list.append(gate)
-    a_recv = exchange.all_to_all(a_list)  # [t, cs, rows of t, n]
-    b_recv = exchange.all_to_all(b_list)
-    del a_list, b_list
-    z_send = []
-    for ar, br in zip(a_recv, b_recv):
-        a_full = ar.transpose(0, 1).reshape(cs, n, n)
-        b_full = br.transpose(0, 1).reshape(cs, n, n)
-        z = stages.trimul_contract(mod, a_full, b_full)  # [cs, n, n], my channels, all rows
-        z_send.append(z.view(cs, g, rows, n).transpose(0, 1).contiguous())  # chunk s = rows of s
-    del a_recv, b_recv
-    z_recv = exchange.all_to_all(z_send)  # [t, cs (channels of t), my rows, n]
-    for pair, zr, gate in zip(pairs, z_recv, g_list):
-        stages.trimul_output(mod, zr.view(c, rows, n), gate, pair)
-
-
-def _bias_full(bias_rows, exchange):
-    gathered = exchange.all_gather(bias_rows)  # [G, heads, rows, n]
-    return [t.transpose(0, 1).reshape(t.shape[1], -1, t.shape[-1]) for t in gathered]
-
-
-def _transpose_blocks(blocks, exchange):
-    """Row blocks [rows, n, ...] -> the matching column blocks [rows (columns of
-    this rank), n (all rows), ...] through one all-to-all."""
-    g = exchange.world
-    sends = []
-    for x in blocks:
-        rows, n = x.shape[:2]
-        sends.append(x.view(rows, g, rows, *x.shape[2:]).transpose(0, 1).contiguous())
-    recv = exchange.all_to_all(sends)  # [t, rows of t (i), my columns (j), ...]
-    out = []
-    for t in recv:
-        g_, rows, cols = t.shape[:3]
-        out.append(t.permute(2, 0, 1, *range(3, t.dim())).reshape(cols, g_ * rows, *t.shape[3:]))
-    return out
+    projected = [stages.trimul_project(mod, pair, pair_mask[shard_rows(n, g, r)])
+                 for pair, r in zip(pairs, exchange.ranks)]
+    a_full = exchange.rows_to_channels([a for a, _, _ in projected])  # [c/G, n, n]
+    b_full = exchange.rows_to_channels([b for _, b, _ in projected])
+    z = [stages.trimul_contract(mod, a, b) for a, b in zip(a_full, b_full)]
+    del a_full, b_full
+    z_rows = exchange.channels_to_rows(z)  # [c, rows, n]
+    for pair, zr, (_, _, gate) in zip(pairs, z_rows, projected):
+        stages.trimul_output(mod, zr, gate, pair)
 
 
 def _attention(mod, pairs, pair_mask, exchange, stages):
     g = exchange.world
     rows, n, _ = pairs[0].shape
     prepared = [stages.attention_prepare(mod, pair) for pair in pairs]
-    biases = _bias_full([bias for _, bias in prepared], exchange)
+    biases = exchange.gather_rows([bias for _, bias in prepared])
     if not mod.transpose:
         for pair, (x, _), bias, r in zip(pairs, prepared, biases, exchange.ranks):
             stages.attention_rows(mod, x, pair_mask[shard_rows(n, g, r)], bias, out=pair)
         return
     # ending node: attention runs over pair columns; mask rows indexed by the column
-    cols = _transpose_blocks([x for x, _ in prepared], exchange)
+    cols = exchange.transpose([x for x, _ in prepared])
     del prepared
     updates = [stages.attention_rows(mod, xt, pair_mask[shard_rows(n, g, r)], bias)
                for xt, bias, r in zip(cols, biases, exchange.ranks)]
-    for pair, upd in zip(pairs, _transpose_blocks(updates, exchange)):
+    for pair, upd in zip(pairs, exchange.transpose(updates)):
         pair += upd
 
 
 def pairformer_block(block: PairformerBlock, pairs: list[torch.Tensor], pair_mask: torch.Tensor,
                      single: torch.Tensor | None, seq_mask: torch.Tensor | None,
-                     exchange: Exchange, stages=None):
+                     exchange, stages=None):
     """One Pairformer block on a row-sharded pair, updated in place.
 
     pairs: this process's row blocks ([N/G, N, c] f32 contiguous, one per local
@@ -249,6 +400,6 @@ def pairformer_block(block: PairformerBlock, pairs: list[torch.Tensor], pair_mas
         stages.transition(block, pair)
     if not block.with_single:
         return pairs
-    logits = _bias_full([stages.pair_logits_rows(block, pair) for pair in pairs], exchange)
+    logits = exchange.gather_rows([stages.pair_logits_rows(block, pair) for pair in pairs])
     stages.single_track(block, single, seq_mask, logits[0])
     return pairs, single
