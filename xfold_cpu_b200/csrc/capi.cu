@@ -1626,8 +1626,8 @@ XFB_API int xfb_exchange_copy(const xfb_copy_box* boxes, int count, void* stream
     const uint64_t vecs = static_cast<uint64_t>(b.d0) * b.d1 * (b.d2_bytes / 16);
     XFB_REQUIRE(vecs == 0 || (aligned16(b.src) && aligned16(b.dst)),
                 "exchange copy pointers must be 16-byte aligned");
-    XFB_REQUIRE(b.d0 < (1ll << 32) && b.d1 < (1ll << 32) && b.d2_bytes / 16 < (1ll << 32),
-                "exchange copy extent too large");
+    XFB_REQUIRE(static_cast<uint64_t>(b.d0) * b.d1 * (b.d2_bytes / 16) < (1ull << 32) - (1ull << 28),
+                "exchange copy box too large (at most 2^32 - 2^28 vectors of 16 bytes)");
     xfb::CopyBox& k = kb.box[i];
     k.src = static_cast<const uint4*>(b.src);
     k.dst = static_cast<uint4*>(b.dst);
@@ -1643,7 +1643,7 @@ XFB_API int xfb_exchange_copy(const xfb_copy_box* boxes, int count, void* stream
   if (largest == 0) return XFB_OK;
   int sms;
   XFB_TRY(sm_count(&sms));
-  const uint64_t want = (largest + 255) / 256;
+  const uint64_t want = (largest + 1023) / 1024;  // four vectors per thread
   const uint64_t cap = std::max<uint64_t>(1, static_cast<uint64_t>(sms) * 8 / count);
   dim3 grid(static_cast<unsigned>(std::min(want, cap)), count);
   xfb::exchange_copy_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(kb);

@@ -29,20 +29,34 @@ struct CopyBoxes {
   int count;
 };
 
-// blockIdx.y selects the box; blocks along x stride over its vectors.
+// blockIdx.y selects the box; blocks along x stride over its vectors, four
+// independent vectors per thread per step so several loads are in flight
+// before the (remote) stores.  Boxes hold fewer than 2^32 vectors.
 __global__ void __launch_bounds__(256) exchange_copy_kernel(const __grid_constant__ CopyBoxes boxes) {
   const CopyBox& b = boxes.box[blockIdx.y];
-  const uint64_t run = b.d2;
-  const uint64_t plane = run * b.d1;
-  const uint64_t total = plane * b.d0;
-  for (uint64_t v = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const uint64_t i0 = v / plane;
-    const uint64_t r = v - i0 * plane;
-    const uint64_t i1 = r / run;
-    const uint64_t i2 = r - i1 * run;
-    const uint4 x = b.src[i0 * b.s0 + i1 * b.s1 + i2];
-    b.dst[i0 * b.t0 + i1 * b.t1 + i2] = x;
+  const uint32_t run = b.d2;
+  const uint32_t plane = run * b.d1;
+  const uint32_t total = plane * b.d0;
+  const uint32_t nthreads = gridDim.x * blockDim.x;
+  for (uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < total; v0 += 4 * nthreads) {
+    uint4 x[4];
+    int64_t dst[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t v = v0 + k * nthreads;
+      dst[k] = -1;
+      if (v < total) {
+        const uint32_t i0 = v / plane;
+        const uint32_t r = v - i0 * plane;
+        const uint32_t i1 = r / run;
+        const uint32_t i2 = r - i1 * run;
+        x[k] = b.src[i0 * b.s0 + i1 * b.s1 + i2];
+        dst[k] = i0 * b.t0 + i1 * b.t1 + i2;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (dst[k] >= 0) b.dst[dst[k]] = x[k];
   }
   __threadfence_system();
 }
