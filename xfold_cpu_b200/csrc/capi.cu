@@ -316,6 +316,18 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
   a.head_scale = head_scale;
   int sms;
   XFB_TRY(sm_count(&sms));
+  if (c == 128 && heads > 0 && mod_scale == nullptr && mod_shift == nullptr && ldx % 4 == 0 &&
+      (y == nullptr || ldy % 4 == 0)) {
+    // head projection on the tensor core, 128-row tiles
+    const int blocks = static_cast<int>(std::min<int64_t>((rows + 127) / 128, int64_t(sms) * 4));
+    if (x_dtype == XFB_F32) {
+      xfb::ln_heads_tc_kernel<float><<<blocks, 256, 0, st>>>(a);
+    } else {
+      xfb::ln_heads_tc_kernel<bf16><<<blocks, 256, 0, st>>>(a);
+    }
+    XFB_LAUNCHED();
+    return XFB_OK;
+  }
   const int64_t warps = (rows + 0);
   const int blocks = static_cast<int>(std::min<int64_t>((warps + 7) / 8, int64_t(sms) * 16));
   const dim3 block(256);

@@ -201,6 +201,144 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
 }
 
 // Channel-major LayerNorm: x(ch, i, j) = in[ch*chan_stride + i*pitch + j].
+// ln_heads_tc_kernel: LayerNorm of 128-wide rows plus a projection onto up to
+// 16 heads (the attention pair bias, the single track's pair logits) on the
+// tensor core.  Per tile of 128 rows: 8 warps normalise 16 rows each into a
+// 128B-swizzled bf16 A tile (and into y when requested); one thread issues
+// M=128 N=16 K=16 MMAs against the head weights (B: 16 x 128 bf16, rows past
+// `heads` zero) into TMEM; warps 0-3 read heads 0-7 and warps 4-7 heads 8-15
+// back, one row per thread, and store them head-major, coalesced along rows.
+// The products are those of ln_rows_kernel's head path: bf16(normalised x) times
+// bf16 weights, accumulated in f32.
+template <typename InT>
+__global__ void __launch_bounds__(256) ln_heads_tc_kernel(LnArgs a) {
+  __shared__ __align__(1024) uint8_t sA[2 * 16384];  // k-halves of 64 channels
+  __shared__ __align__(1024) uint8_t sB[2 * 2048];   // 16 heads x 64 channels per half
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 32);
+    tmem_relinquish();
+  }
+  // head weights into the swizzled B tile (K-major, one 128-byte row per head and half)
+  for (int idx = threadIdx.x; idx < 16 * 128; idx += blockDim.x) {
+    const int n = idx >> 7, ch = idx & 127;
+    const int h = ch >> 6, k = ch & 63;
+    const __nv_bfloat16 w = n < a.heads ? a.wh[n * 128 + ch] : __float2bfloat16_rn(0.f);
+    *reinterpret_cast<__nv_bfloat16*>(sB + h * 2048 + n * 128 + (((k >> 3) ^ (n & 7)) << 4) +
+                                      (k & 7) * 2) = w;
+  }
+  float wv[4], bv[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    wv[e] = a.w ? a.w[lane * 4 + e] : 1.f;
+    bv[e] = a.b ? a.b[lane * 4 + e] : 0.f;
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  constexpr uint32_t kIdesc = idesc_bf16(128, 16, false, false);
+  // this lane's 8 bytes in a row of the A tile: channels 4*lane .. 4*lane+3
+  const int half = lane >> 4;
+  const int chunk = (lane & 15) >> 1;
+  const int within = (lane & 1) * 8;
+  const int64_t tiles = (a.rows + 127) / 128;
+  uint32_t phase = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int64_t row0 = tile * 128;
+    // ---- LayerNorm of 16 rows per warp, next row's load in flight
+    float nxt[4];
+    auto load = [&](int r, float (&v)[4]) {
+      const int64_t row = row0 + warp * 16 + r;
+      if (row < a.rows) {
+        load_vec4<InT>(reinterpret_cast<const InT*>(a.x) + row * a.ldx + lane * 4, v);
+      } else {
+        v[0] = v[1] = v[2] = v[3] = 0.f;
+      }
+    };
+    load(0, nxt);
+#pragma unroll 1
+    for (int r = 0; r < 16; ++r) {
+      float v[4] = {nxt[0], nxt[1], nxt[2], nxt[3]};
+      if (r + 1 < 16) load(r + 1, nxt);
+      const int trow = warp * 16 + r;
+      const int64_t row = row0 + trow;
+      const float mean = warp_sum(v[0] + v[1] + v[2] + v[3]) * (1.f / 128);
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ss += (v[e] - mean) * (v[e] - mean);
+      const float rstd = rsqrtf(warp_sum(ss) * (1.f / 128) + a.eps);
+      uint2 pk = make_uint2(0u, 0u);
+      if (row < a.rows) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = (v[e] - mean) * rstd * wv[e] + bv[e];
+        pk.x = pack_bf16x2(v[0], v[1]);
+        pk.y = pack_bf16x2(v[2], v[3]);
+        if (a.y != nullptr) *reinterpret_cast<uint2*>(a.y + row * a.ldy + lane * 4) = pk;
+      }
+      *reinterpret_cast<uint2*>(sA + half * 16384 + trow * 128 + ((chunk ^ (trow & 7)) << 4) +
+                                within) = pk;
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- head projection on the tensor core
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          umma_bf16(tmem, sw128_desc(a_addr + h * 16384 + j * 32, 16, 1024),
+                    sw128_desc(b_addr + h * 2048 + j * 32, 16, 1024), kIdesc, (h | j) ? 1u : 0u);
+      umma_commit(&bar);
+    }
+    const bool ok = mbar_wait(&bar, phase, kErrWaitEpilogue, &abort_flag);
+    phase ^= 1;
+    tc_fence_after();
+    // ---- heads back from TMEM: warps w and w+4 share lane quarter w % 4
+    {
+      const int quarter = warp & 3;
+      const int hbase = (warp >> 2) * 8;
+      float hv[8];
+      uint32_t r8[8];
+      __syncwarp();
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+          : "=r"(r8[0]), "=r"(r8[1]), "=r"(r8[2]), "=r"(r8[3]), "=r"(r8[4]), "=r"(r8[5]),
+            "=r"(r8[6]), "=r"(r8[7])
+          : "r"(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + hbase));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hv[e] = __uint_as_float(r8[e]);
+      const int64_t row = row0 + quarter * 32 + lane;
+      if (ok && row < a.rows) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (hbase + e < a.heads)
+            a.head_out[(hbase + e) * a.head_ld + row] = __float2bfloat16_rn(hv[e] * a.head_scale);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // TMEM and the A tile are reused by the next tile
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
 template <int C>
 __global__ void __launch_bounds__(128) ln_channel_major_kernel(
     const __nv_bfloat16* in, int rows, int n, int pitch, int64_t chan_stride, const float* w,
