@@ -32,7 +32,8 @@ namespace xfb {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of bf16
 constexpr int kGemmEpiThreads = 256;
-constexpr int kGemmThreads = kGemmEpiThreads + 64;
+constexpr int kGemmThreads = kGemmEpiThreads + 96;
+constexpr int kGemmStoreWarp = 10;
 constexpr int kGemmProducerWarp = 8;
 constexpr int kGemmMmaWarp = 9;
 
@@ -63,8 +64,9 @@ struct GemmSmem {
   static constexpr int kAuxOff = STAGES * kStageBytes;
   static constexpr int kStagingOff = kAuxOff + 2 * kAuxStride;
   static constexpr int kBarOff = kStagingOff + Epi::kStagingBufs * kStagingStride;
-  // full[S], empty[S], tfull[2], tempty[2], aux_full[2], aux_empty[2]
-  static constexpr int kNumBars = 2 * STAGES + 8;
+  // full[S], empty[S], tfull[2], tempty[2], aux_full[2], aux_empty[2],
+  // staging_full[2], staging_free[2]
+  static constexpr int kNumBars = 2 * STAGES + 12;
   static constexpr int kTotal = kBarOff + kNumBars * 8 + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;  // slack for 1024-byte alignment
   static_assert(kLaunchBytes <= 232448, "GEMM shared memory exceeds 227 KB");
@@ -90,7 +92,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* aux_full = tempty + 2;
   uint64_t* aux_empty = aux_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_empty + 2);
+  uint64_t* staging_full = aux_empty + 2;
+  uint64_t* staging_free = staging_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(staging_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -106,6 +110,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[b], kGemmEpiThreads);
       mbar_init(&aux_full[b], 1);
       mbar_init(&aux_empty[b], kGemmEpiThreads);
+      mbar_init(&staging_full[b], kGemmEpiThreads);
+      mbar_init(&staging_free[b], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -216,9 +222,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
+  } else if (warp == kGemmStoreWarp) {
+    // ------------------------------------------------ bulk-store issuer
+    // Takes each staged tile once every epilogue thread has written it, issues
+    // the epilogue's TMA store, and frees the staging buffer as soon as that
+    // store has read it.  The epilogue warps never wait for one another.
+    if constexpr (Epi::kStagingBytes > 0) {
+      if (lane == 0) {
+        constexpr int NB = Epi::kStagingBufs;
+        int iter = 0;
+        EpiCtx ctx;
+        ctx.row = 0;
+        ctx.half = 0;
+        ctx.tmem = 0;
+        ctx.aux = nullptr;
+        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
+          const int b = iter % NB;
+          const uint32_t ph = (iter / NB) & 1;
+          const bool ok = mbar_wait(&staging_full[b], ph, kErrWaitEpilogue, abort_flag);
+          const int bat = tile / tiles_per_batch;
+          const int rem = tile - bat * tiles_per_batch;
+          ctx.bat = bat;
+          ctx.m0 = (rem / shape.n_tiles) * kGemmBM;
+          ctx.n0 = (rem % shape.n_tiles) * BN;
+          ctx.staging = smem + L::kStagingOff + b * L::kStagingStride;
+          if (ok && !*abort_flag) epi.store(ctx);
+          bulk_commit();
+          // free the buffer as soon as this store has read it: the epilogue
+          // warps are then never waiting on the next tile's handoff
+          bulk_wait_read<0>();
+          mbar_arrive(&staging_free[b]);
+        }
+        bulk_wait<0>();
+      }
+    }
   } else {
     // ------------------------------------------------ epilogue warps 0-7
-    const bool leader = threadIdx.x == 0;
+    constexpr int NB = Epi::kStagingBufs;
     int acc = 0;
     uint32_t acc_phase = 0;
     int iter = 0;
@@ -231,40 +271,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ctx.bat = bat;
       ctx.m0 = (rem / shape.n_tiles) * kGemmBM;
       ctx.n0 = (rem % shape.n_tiles) * BN;
-      // Every epilogue thread runs every tile and every barrier: a wait that gave
-      // up (the CTA is aborting) skips the work but not the named barriers.
+      // Every epilogue thread runs every tile and arrives on every barrier: a
+      // wait that gave up (the CTA is aborting) skips the work, not the arrivals.
       bool ok = mbar_wait(&tfull[acc], acc_phase, kErrWaitEpilogue, abort_flag);
       if constexpr (kAux) {
         ok = mbar_wait(&aux_full[acc], acc_phase, kErrWaitEpilogue, abort_flag) && ok;
       }
       tc_fence_after();
       ctx.tmem = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + acc * BN;
-      ctx.staging = smem + L::kStagingOff + (iter % Epi::kStagingBufs) * L::kStagingStride;
+      ctx.staging = smem + L::kStagingOff + (iter % NB) * L::kStagingStride;
       ctx.aux = kAux ? smem + L::kAuxOff + acc * L::kAuxStride : nullptr;
       if constexpr (Epi::kStagingBytes > 0) {
-        // the bulk store that last read this staging buffer must be done reading
-        if (leader) bulk_wait_read<Epi::kStagingBufs - 1>();
-        named_barrier(1, kGemmEpiThreads);
+        // the store that last read this staging buffer must be done reading it
+        if (iter >= NB)
+          ok = mbar_wait(&staging_free[iter % NB], ((iter / NB) - 1) & 1, kErrWaitEpilogue,
+                         abort_flag) && ok;
       }
       if (ok) epi.compute(ctx);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if constexpr (kAux) mbar_arrive(&aux_empty[acc]);
-      if constexpr (Epi::kStagingBytes > 0) {
-        named_barrier(1, kGemmEpiThreads);
-        if (leader && ok && !*abort_flag) {
-          epi.store(ctx);
-          bulk_commit();
-        }
-      }
+      if constexpr (Epi::kStagingBytes > 0) mbar_arrive(&staging_full[iter % NB]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
-    }
-    if constexpr (Epi::kStagingBytes > 0) {
-      if (leader) bulk_wait<0>();
     }
   }
 
