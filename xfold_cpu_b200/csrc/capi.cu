@@ -231,7 +231,7 @@ int run_gemm(const void* A, int64_t lda, int64_t a_bs, const void* B, int64_t ld
   using L = xfb::GemmSmem<BN, STAGES, Epi>;
   auto kernel = xfb::gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   XFB_TRY(set_smem(kernel, L::kLaunchBytes));
-  kernel<<<grid, xfb::kGemmThreads, L::kLaunchBytes, st>>>(ta, tb, sh, epi);
+  kernel<<<grid, xfb::GemmWarps<Epi>::kThreads, L::kLaunchBytes, st>>>(ta, tb, sh, epi);
   XFB_LAUNCHED();
   return XFB_OK;
 }

@@ -25,17 +25,41 @@
 //   Epi::store(ctx)    (one thread) bulk stores from the staging buffer
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace xfb {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int kGemmEpiThreads = 256;
-constexpr int kGemmThreads = kGemmEpiThreads + 96;
-constexpr int kGemmStoreWarp = 10;
-constexpr int kGemmProducerWarp = 8;
-constexpr int kGemmMmaWarp = 9;
+constexpr int kGemmEpiThreads = 256;  // one epilogue group: 8 warps
+
+// Epilogues that declare kGroups = 2 (and have two staging buffers) run two
+// epilogue groups of 8 warps: group g takes the tiles that use TMEM accumulator
+// g and staging buffer g, so two tiles' epilogues are in flight at once.  It
+// pays where the epilogue is long per tile (the triangle projection), and costs
+// elsewhere (registers drop to 96 with 19 warps).
+template <class E, class = void>
+struct EpiGroupsOf {
+  static constexpr int value = 1;
+};
+template <class E>
+struct EpiGroupsOf<E, std::void_t<decltype(E::kGroups)>> {
+  static constexpr int value = E::kGroups;
+};
+
+// Warp layout of the GEMM kernel for epilogue Epi: the epilogue group(s), then
+// the TMA producer, the MMA issuer and the bulk-store issuer.
+template <class Epi>
+struct GemmWarps {
+  static constexpr int kGroups =
+      (Epi::kStagingBytes > 0 && Epi::kStagingBufs == 2 && EpiGroupsOf<Epi>::value == 2) ? 2 : 1;
+  static constexpr int kProducer = 8 * kGroups;
+  static constexpr int kMma = kProducer + 1;
+  static constexpr int kStore = kProducer + 2;
+  static constexpr int kThreads = kGemmEpiThreads * kGroups + 96;
+};
 
 struct GemmShape {
   int M, N, K, batch;
@@ -73,12 +97,16 @@ struct GemmSmem {
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(GemmWarps<Epi>::kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, GemmShape shape,
                      const __grid_constant__ Epi epi) {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128, 192 or 256");
   using L = GemmSmem<BN, STAGES, Epi>;
+  using W = GemmWarps<Epi>;
+  constexpr int kGemmProducerWarp = W::kProducer;
+  constexpr int kGemmMmaWarp = W::kMma;
+  constexpr int kGemmStoreWarp = W::kStore;
   constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256 : 512;
   constexpr uint32_t kIdesc = idesc_bf16(kGemmBM, BN, A_MN, B_MN);
   constexpr bool kAux = Epi::kAuxBytes > 0;
@@ -257,15 +285,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue warps 0-7
+    // ------------------------------------------------ epilogue warps (1 or 2 groups of 8)
     constexpr int NB = Epi::kStagingBufs;
-    int acc = 0;
+    constexpr int G = W::kGroups;
+    const int group = warp >> 3;
+    // with two groups, group g always uses accumulator g (tile iterations g, g+2, ...)
+    int acc = group;
     uint32_t acc_phase = 0;
-    int iter = 0;
+    int iter = group;
     EpiCtx ctx;
     ctx.row = (warp & 3) * 32 + lane;
-    ctx.half = warp >> 2;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
+    ctx.half = (warp & 7) >> 2;
+    for (int tile = blockIdx.x + group * gridDim.x; tile < total_tiles;
+         tile += G * gridDim.x, iter += G) {
       const int bat = tile / tiles_per_batch;
       const int rem = tile - bat * tiles_per_batch;
       ctx.bat = bat;
@@ -293,7 +325,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_arrive(&tempty[acc]);
       if constexpr (kAux) mbar_arrive(&aux_empty[acc]);
       if constexpr (Epi::kStagingBytes > 0) mbar_arrive(&staging_full[iter % NB]);
-      if (++acc == 2) {
+      if constexpr (G == 2) {
+        acc_phase ^= 1;
+      } else if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
@@ -584,6 +618,7 @@ struct EpiGLU {
 struct EpiTriProj {
   static constexpr int kStagingBytes = 32768;
   static constexpr int kStagingBufs = 2;
+  static constexpr int kGroups = 2;
   static constexpr int kAuxBytes = 0;
   CUtensorMap a_map, b_map, g_map;
   const float* mask;  // [n][n] or null
