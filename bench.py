@@ -267,6 +267,58 @@ def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
     return results
 
 
+def _diffusion_c5(dev, steps: int) -> dict:
+    """BASELINE config C5's token transformer: 24 blocks (6 super-blocks of 4),
+    N = 768 tokens, c = 768, 16 heads of 48, single cond 384, pair cond 128,
+    random init N(0, 0.02), seed 4.  The pair logits are computed once, as the
+    reference caches them across denoising steps; one call = the 24 blocks of
+    one denoising step, timed eager and as a replayed CUDA graph."""
+    import torch
+
+    from xfold_cpu_b200 import _capi
+    from xfold_cpu_b200.nn import DiffusionTransformer, init_params_
+
+    n, c = 768, 768
+    mod = DiffusionTransformer(c_act=c).eval()
+    init_params_(mod, seed=4)
+    mod = mod.to(dev)
+    g = torch.Generator(device=dev).manual_seed(4)
+    act = torch.randn(n, c, device=dev, generator=g)
+    cond = torch.randn(n, 384, device=dev, generator=g)
+    pair_cond = torch.randn(n, n, 128, device=dev, generator=g)
+    mask = torch.ones(n, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {"n_token": n, "c_act": c, "blocks": 24, "heads": 16, "head_dim": 48,
+           "data": "synthetic, random init"}
+    with torch.inference_mode():
+        logits = mod.pair_logits(pair_cond)
+        work = act.clone()
+
+        def eager():
+            work.copy_(act)
+            mod.run_blocks(work, mask, cond, logits)
+
+        step = mod.capture(act, mask, cond, pair_cond)
+        for name, fn in (("eager_ms", eager), ("graph_ms", lambda: step(act, cond))):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            l0 = _capi.launch_count()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = max(steps, 10)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            out[name] = round(e0.elapsed_time(e1) / reps, 4)
+            if name == "eager_ms":
+                out["kernel_launches_per_step"] = int((_capi.launch_count() - l0) // reps)
+        del step
+    return out
+
+
 def run_cuda(args) -> None:
     import torch
 
@@ -367,6 +419,7 @@ def run_cuda(args) -> None:
         finite = bool(torch.isfinite(out_pair).all() and torch.isfinite(out_single).all())
 
         roof = _kernel_roofline(dev, args.steps, peaks) if rank == 0 else {}
+        c5 = _diffusion_c5(dev, args.steps) if rank == 0 and world == 1 else None
 
     if rank != 0:
         return
@@ -400,6 +453,7 @@ def run_cuda(args) -> None:
         "clocks": clocks,
         "cpu_baseline": base,
         "finite": finite,
+        "extras": {"diffusion_transformer_c5": c5} if c5 else None,
     }
     print(json.dumps(line), flush=True)
 

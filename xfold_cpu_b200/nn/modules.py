@@ -334,15 +334,63 @@ class DiffusionTransformer(nn.Module):
             self._logits, self._logits_key = logits, key
         return self._logits
 
-    def forward(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
-                pair_cond: torch.Tensor) -> torch.Tensor:
-        logits = self.pair_logits(pair_cond)
+    def run_blocks(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
+                   logits: list[list[torch.Tensor]]) -> torch.Tensor:
+        """The blocks of forward() with the pair logits given (act updated in place)."""
         for s in range(self.num_super_blocks):
             for j in range(self.super_block_size):
                 i = s * self.super_block_size + j
                 self.self_attention[i].accumulate_(act, mask, logits[s][j], single_cond)
                 self.transition_block[i].accumulate_(act, single_cond)
         return act
+
+    def forward(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
+                pair_cond: torch.Tensor) -> torch.Tensor:
+        return self.run_blocks(act, mask, single_cond, self.pair_logits(pair_cond))
+
+    def capture(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
+                pair_cond: torch.Tensor) -> "DiffusionStepGraph":
+        """Records the transformer's blocks for these shapes into a CUDA graph.
+
+        The reference runs this transformer 24 blocks deep at every denoising
+        step of every sample (xfold/alphafold3.py:328-395 call the diffusion
+        head, xfold/nn/diffusion_head.py:234 calls the transformer) with the
+        pair conditioning fixed: its logits are computed here once,
+        and each replay launches every kernel of the 24 blocks with one call.
+        The tensors given are copied into the graph's own input buffers; see
+        DiffusionStepGraph for replaying with new act / single_cond."""
+        return DiffusionStepGraph(self, act, mask, single_cond, pair_cond)
+
+
+class DiffusionStepGraph:
+    """A CUDA graph of DiffusionTransformer.run_blocks for fixed shapes and
+    pair conditioning.  __call__(act, single_cond) copies the inputs into the
+    graph's buffers, replays the graph on the current stream and returns the
+    graph's output buffer (overwritten by the next call)."""
+
+    def __init__(self, module: DiffusionTransformer, act, mask, single_cond, pair_cond) -> None:
+        self.module = module
+        self.logits = module.pair_logits(pair_cond)
+        self.act = act.detach().clone()
+        self.mask = mask.detach().clone()
+        self.single_cond = single_cond.detach().clone()
+        work = self.act.clone()
+        # warm-up on a side stream: weight caches filled, kernels' attributes set
+        side = torch.cuda.Stream(device=self.act.device)
+        side.wait_stream(torch.cuda.current_stream(self.act.device))
+        with torch.cuda.stream(side):
+            module.run_blocks(work, self.mask, self.single_cond, self.logits)
+        torch.cuda.current_stream(self.act.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self.act.clone()
+            module.run_blocks(self.out, self.mask, self.single_cond, self.logits)
+
+    def __call__(self, act: torch.Tensor, single_cond: torch.Tensor) -> torch.Tensor:
+        self.act.copy_(act)
+        self.single_cond.copy_(single_cond)
+        self.graph.replay()
+        return self.out
 
 
 class PairformerBlock(nn.Module):
