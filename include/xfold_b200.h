@@ -337,6 +337,18 @@ XFB_API int xfb_ipc_handle(const void* ptr, void* handle, int64_t* offset);
 XFB_API int xfb_ipc_open(const void* handle, int64_t offset, void** peer_ptr);
 XFB_API int xfb_ipc_close(void* peer_ptr, int64_t offset);
 
+/* Conditioning projections of one diffusion step, for every block at once:
+ * out = act(x W^T + bias) bf16, where x [m][k] bf16 is the (LayerNorm'd) single
+ * conditioning and W [n][k] bf16 stacks the blocks' AdaLN scale / shift weights
+ * (LayerNorm weight folded in) or AdaLNZero gate weights.  The n columns are
+ * written as n / chunk contiguous [m][chunk] tensors; act = sigmoid on every
+ * chunk (sig_mode 2), on the even chunks (1) or none (0).  Replaces, per block,
+ * AdaptiveLayerNorm's conditioning (xfold/nn/diffusion_transformer.py:51-62) and
+ * AdaLNZero's gate (:85-94), which the reference recomputes for each block. */
+XFB_API int xfb_conditioning(const void* x, int64_t m, int64_t k, const void* weight, int64_t n,
+                             const float* bias, int64_t chunk, int sig_mode, void* out,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

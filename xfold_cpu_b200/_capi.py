@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_ipc_handle": (_i, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),
     "xfb_ipc_open": (_i, [_p, _i64, ctypes.POINTER(ctypes.c_void_p)]),
     "xfb_ipc_close": (_i, [_p, _i64]),
+    "xfb_conditioning": (_i, [_p, _i64, _i64, _p, _i64, _p, _i64, _i, _p, _p]),
 }
 
 

@@ -1708,4 +1708,30 @@ XFB_API int xfb_ipc_close(void* peer_ptr, int64_t offset) {
   return XFB_OK;
 }
 
+
+// ---------------------------------------------------------------- diffusion conditioning
+
+XFB_API int xfb_conditioning(const void* x, int64_t m, int64_t k, const void* weight, int64_t n,
+                             const float* bias, int64_t chunk, int sig_mode, void* out,
+                             void* stream) {
+  XFB_REQUIRE(m >= 0 && k > 0 && n >= 0, "conditioning expects m, n >= 0 and k > 0");
+  XFB_REQUIRE(k % 8 == 0, "conditioning input width must be a multiple of 8");
+  XFB_REQUIRE(chunk > 0 && chunk % 16 == 0 && n % chunk == 0,
+              "conditioning chunks must be multiples of 16 columns that divide n");
+  XFB_REQUIRE(sig_mode >= 0 && sig_mode <= 2, "sig_mode must be 0, 1 or 2");
+  XFB_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out),
+              "conditioning buffers must be 16-byte aligned");
+  XFB_REQUIRE(m * n < (1ll << 40) && m < (1 << 30) && n < (1 << 30), "conditioning too large");
+  if (m == 0 || n == 0) return XFB_OK;
+  xfb::EpiCond<256> epi;
+  epi.out = static_cast<bf16*>(out);
+  epi.bias = bias;
+  epi.M = static_cast<int>(m);
+  epi.N = static_cast<int>(n);
+  epi.chunk = static_cast<int>(chunk);
+  epi.sig_mode = sig_mode;
+  return run_gemm<256, false, false>(x, k, 0, weight, k, 0, m, n, k, 1, epi,
+                                     static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

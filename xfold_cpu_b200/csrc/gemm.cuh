@@ -798,4 +798,44 @@ struct EpiAttProjDirect {
   }
 };
 
+// Conditioning projections of a diffusion step (AdaLN scale / shift and the
+// AdaLNZero gates of every block at once): out = act(x W^T + b), bf16.  The N
+// output columns are cut into chunks of `chunk` columns stored one after
+// another, [N / chunk][M][chunk], so each block's tensor is contiguous; act is
+// the logistic function on every chunk (sig_mode 2), on the even chunks
+// (sig_mode 1: [scale, shift] pairs) or nowhere (0).  Direct 16-byte stores.
+template <int BN>
+struct EpiCond {
+  static constexpr int kStagingBytes = 0;
+  static constexpr int kStagingBufs = 1;
+  static constexpr int kAuxBytes = 0;
+  __nv_bfloat16* out;
+  const float* bias;
+  int M, N, chunk, sig_mode;
+
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+  __device__ void store(const EpiCtx&) const {}
+
+  __device__ void compute(const EpiCtx& c) const {
+    constexpr int kHalf = BN / 2;
+    const int row = c.m0 + c.row;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kHalf; c0 += 16) {
+      float v[16];
+      tmem_ld16(c.tmem + c.half * kHalf + c0, v);
+      const int col = c.n0 + c.half * kHalf + c0;
+      if (row >= M || col >= N) continue;  // N and chunk are multiples of 16
+      const int q = col / chunk;
+      const bool sig = sig_mode == 2 || (sig_mode == 1 && (q & 1) == 0);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float x = bf16r(v[i] + (bias ? bias[col + i] : 0.f));
+        v[i] = sig ? sigmoidf_stable(x) : x;
+      }
+      __nv_bfloat16* dst = out + (static_cast<int64_t>(q) * M + row) * chunk + (col - q * chunk);
+      store16_bf16(dst, v);
+    }
+  }
+};
+
 }  // namespace xfb

@@ -526,3 +526,19 @@ def pair_logits_rows(pair: torch.Tensor, norm_weight: torch.Tensor | None,
     _capi.call("xfb_pair_logits_rows", _ptr(pair), _code(pair), rows, n, c, heads, _ptr(nw),
                _ptr(nb), float(eps), _ptr(w), _ptr(logits), _stream(device))
     return logits
+
+
+def conditioning(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, chunk: int,
+                 sig_mode: int) -> torch.Tensor:
+    """act(x @ weight^T + bias) as [n / chunk, m, chunk] bf16 (one contiguous
+    tensor per chunk); act = sigmoid on every chunk (sig_mode 2), on the even
+    chunks (1) or none (0)."""
+    device = _check_cuda(x, weight, bias)
+    x, weight = _contig(x, torch.bfloat16), _contig(weight, torch.bfloat16)
+    m, k = x.shape
+    n = weight.shape[0]
+    out = torch.empty((n // chunk, m, chunk), dtype=torch.bfloat16, device=device)
+    b = _contig(bias, torch.float32)
+    _capi.call("xfb_conditioning", _ptr(x), m, k, _ptr(weight), n, _ptr(b), chunk, sig_mode,
+               _ptr(out), _stream(device))
+    return out

@@ -221,13 +221,15 @@ class DiffusionTransition(nn.Module):
                                             use_single_cond)
         self._w2 = WeightCache()
 
-    def _run(self, x, single_cond, out, accumulate):
+    def _run(self, x, single_cond, out, accumulate, cond=None):
         config.require_cuda("gated_linear_unit_implementation")
         assert (single_cond is None) == (self.use_single_cond is False)
         w1 = self._glu_weight_cache.get((self.transition1.weight,), native.pack_glu_weight)
         ln = self.adaptive_layernorm.layer_norm
         scale = shift = gate = None
-        if self.use_single_cond:
+        if cond is not None:  # (sigmoid(scale), shift, gate) computed for every block at once
+            scale, shift, gate = cond
+        elif self.use_single_cond:
             scale, shift = self.adaptive_layernorm.modulation(single_cond)
             gate = self.adaptive_zero_init.out_gate(single_cond)
         return native.transition(x, ln.weight, ln.bias, ln.eps, w1,
@@ -238,10 +240,10 @@ class DiffusionTransition(nn.Module):
     def forward(self, x: torch.Tensor, single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
         return self._run(x, single_cond, None, False)
 
-    def accumulate_(self, x, single_cond=None):
+    def accumulate_(self, x, single_cond=None, cond=None):
         if _fused_target(x):
-            return self._run(x, single_cond, x, True)
-        x += self.forward(x, single_cond)
+            return self._run(x, single_cond, x, True, cond)
+        x += self._run(x, single_cond, None, False, cond)
         return x
 
 
@@ -263,7 +265,7 @@ class SelfAttention(nn.Module):
         self._packed = WeightCache()
         self._wo = WeightCache()
 
-    def _run(self, x, mask, pair_logits, single_cond, out, accumulate):
+    def _run(self, x, mask, pair_logits, single_cond, out, accumulate, cond=None):
         config.require_cuda("dot_product_attention_implementation")
         assert (single_cond is None) == (self.use_single_cond is False)
         packed = self._packed.get(
@@ -271,7 +273,9 @@ class SelfAttention(nn.Module):
              self.gating_query.weight), native.pack_attention_weights)
         ln = self.adaptive_layernorm.layer_norm
         scale = shift = gate = None
-        if self.use_single_cond:
+        if cond is not None:  # (sigmoid(scale), shift, gate) computed for every block at once
+            scale, shift, gate = cond
+        elif self.use_single_cond:
             scale, shift = self.adaptive_layernorm.modulation(single_cond)
             gate = self.adaptive_zero_init.out_gate(single_cond)
         return native.self_attention(
@@ -283,10 +287,10 @@ class SelfAttention(nn.Module):
                 single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
         return self._run(x, mask, pair_logits, single_cond, None, False)
 
-    def accumulate_(self, x, mask, pair_logits=None, single_cond=None):
+    def accumulate_(self, x, mask, pair_logits=None, single_cond=None, cond=None):
         if _fused_target(x):
-            return self._run(x, mask, pair_logits, single_cond, x, True)
-        x += self.forward(x, mask, pair_logits, single_cond)
+            return self._run(x, mask, pair_logits, single_cond, x, True, cond)
+        x += self._run(x, mask, pair_logits, single_cond, None, False, cond)
         return x
 
 
@@ -313,6 +317,55 @@ class DiffusionTransformer(nn.Module):
              for _ in range(num_blocks)])
         self._logits_key = None
         self._logits = None
+        self._cond_w = WeightCache()
+        self._gate_w = WeightCache()
+
+    def _adaln_modules(self):
+        for i in range(self.num_blocks):
+            yield self.self_attention[i].adaptive_layernorm
+            yield self.transition_block[i].adaptive_layernorm
+
+    def _zero_modules(self):
+        for i in range(self.num_blocks):
+            yield self.self_attention[i].adaptive_zero_init
+            yield self.transition_block[i].adaptive_zero_init
+
+    def conditioning(self, single_cond: torch.Tensor):
+        """Every block's AdaLN (sigmoid(scale), shift) and AdaLNZero gate for one
+        denoising step: the reference recomputes them in each block
+        (diffusion_transformer.py:51-62, :85-94) from the same single_cond.
+
+        LayerNorm(single_cond) without its weight, then one GEMM against the
+        blocks' scale / shift weights with that LayerNorm weight folded in, and
+        one GEMM of single_cond against the gate weights.  Returns per block
+        (attention, transition) triples of contiguous [N, c_act] bf16 views."""
+        ada = list(self._adaln_modules())
+        zero = list(self._zero_modules())
+
+        def build_mod(*_):
+            ws, bs = [], []
+            for m in ada:
+                g = m.single_cond_layer_norm.weight.float()
+                ws += [m.single_cond_scale.weight.float() * g, m.single_cond_bias.weight.float() * g]
+                bs += [m.single_cond_scale.bias.float(), torch.zeros_like(m.single_cond_scale.bias.float())]
+            return torch.cat(ws).bfloat16().contiguous(), torch.cat(bs).contiguous()
+
+        def build_gate(*_):
+            w = torch.cat([z.adaptive_zero_cond.weight.float() for z in zero]).bfloat16()
+            b = torch.cat([z.adaptive_zero_cond.bias.float() for z in zero])
+            return w.contiguous(), b.contiguous()
+
+        mod_src = [t for m in ada for t in (m.single_cond_layer_norm.weight, m.single_cond_scale.weight,
+                                            m.single_cond_scale.bias, m.single_cond_bias.weight)]
+        gate_src = [t for z in zero for t in (z.adaptive_zero_cond.weight, z.adaptive_zero_cond.bias)]
+        w_mod, b_mod = self._cond_w.get(mod_src, build_mod)
+        w_gate, b_gate = self._gate_w.get(gate_src, build_gate)
+        eps = ada[0].single_cond_layer_norm.eps
+        sc = native.layer_norm(single_cond, None, None, eps)
+        mod = native.conditioning(sc, w_mod, b_mod, self.c_act, 1)  # [4 * blocks, N, c]
+        gate = native.conditioning(single_cond, w_gate, b_gate, self.c_act, 2)  # [2 * blocks, N, c]
+        return [((mod[4 * i], mod[4 * i + 1], gate[2 * i]),
+                 (mod[4 * i + 2], mod[4 * i + 3], gate[2 * i + 1])) for i in range(self.num_blocks)]
 
     def pair_logits(self, pair_cond: torch.Tensor) -> list[torch.Tensor]:
         """[super_block][j] -> [H, N, N] bf16 logits; cached per pair_cond version
@@ -336,12 +389,15 @@ class DiffusionTransformer(nn.Module):
 
     def run_blocks(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
                    logits: list[list[torch.Tensor]]) -> torch.Tensor:
-        """The blocks of forward() with the pair logits given (act updated in place)."""
+        """The blocks of forward() with the pair logits given (act updated in place);
+        the conditioning of all blocks is computed first, in one pass."""
+        cond = self.conditioning(single_cond)
         for s in range(self.num_super_blocks):
             for j in range(self.super_block_size):
                 i = s * self.super_block_size + j
-                self.self_attention[i].accumulate_(act, mask, logits[s][j], single_cond)
-                self.transition_block[i].accumulate_(act, single_cond)
+                self.self_attention[i].accumulate_(act, mask, logits[s][j], single_cond,
+                                                   cond=cond[i][0])
+                self.transition_block[i].accumulate_(act, single_cond, cond=cond[i][1])
         return act
 
     def forward(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
