@@ -327,6 +327,17 @@ typedef struct {
  * sees every store.  No counterpart in the reference (it has no multi-GPU pair). */
 XFB_API int xfb_exchange_copy(const xfb_copy_box* boxes, int count, void* stream);
 
+/* Barrier after an exchange copy, without a collective call (no counterpart in
+ * the reference).  xfb_exchange_signal writes `epoch` into slot `rank` of every
+ * GPU's uint32 flag array (peer_flags[s]: GPU s's array as mapped here, world
+ * <= 16) with system-scope release stores, ordered after the work already on
+ * `stream`; xfb_exchange_wait makes `stream` wait until every slot of this
+ * GPU's own array holds at least `epoch` (giving up after 2 s, with the
+ * device error code 0x105).  Epochs increase by one per exchange. */
+XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,
+                                void* stream);
+XFB_API int xfb_exchange_wait(const void* flags, int world, uint32_t epoch, void* stream);
+
 /* CUDA IPC for the exchange receive buffers (no counterpart in the reference).
  * xfb_ipc_handle: the IPC handle (xfb_ipc_handle_bytes() bytes) of the device
  * allocation holding ptr, and ptr's byte offset in it.  xfb_ipc_open: maps a

@@ -92,6 +92,8 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_ipc_handle": (_i, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),
     "xfb_ipc_open": (_i, [_p, _i64, ctypes.POINTER(ctypes.c_void_p)]),
     "xfb_ipc_close": (_i, [_p, _i64]),
+    "xfb_exchange_signal": (_i, [_p, _i, _i, ctypes.c_uint32, _p]),
+    "xfb_exchange_wait": (_i, [_p, _i, ctypes.c_uint32, _p]),
     "xfb_conditioning": (_i, [_p, _i64, _i64, _p, _i64, _p, _i64, _i, _p, _p]),
 }
 

@@ -1734,4 +1734,35 @@ XFB_API int xfb_conditioning(const void* x, int64_t m, int64_t k, const void* we
                                      static_cast<cudaStream_t>(stream));
 }
 
+
+XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,
+                                void* stream) {
+  XFB_REQUIRE(world > 0 && world <= xfb::kMaxPeers && rank >= 0 && rank < world,
+              "exchange barrier takes 1..16 GPUs");
+  XFB_REQUIRE(peer_flags != nullptr, "peer flag pointers missing");
+  xfb::PeerFlags p;
+  memset(&p, 0, sizeof(p));
+  for (int s = 0; s < world; ++s) {
+    XFB_REQUIRE(peer_flags[s] != nullptr && (reinterpret_cast<uintptr_t>(peer_flags[s]) & 3) == 0,
+                "peer flag arrays must be 4-byte aligned device pointers");
+    p.flags[s] = static_cast<uint32_t*>(peer_flags[s]);
+  }
+  p.world = world;
+  p.rank = rank;
+  p.epoch = epoch;
+  xfb::exchange_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+XFB_API int xfb_exchange_wait(const void* flags, int world, uint32_t epoch, void* stream) {
+  XFB_REQUIRE(world > 0 && world <= xfb::kMaxPeers, "exchange barrier takes 1..16 GPUs");
+  XFB_REQUIRE(flags != nullptr && (reinterpret_cast<uintptr_t>(flags) & 3) == 0,
+              "flag array must be a 4-byte aligned device pointer");
+  xfb::exchange_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint32_t*>(flags), world, epoch);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
 }  // extern "C"

@@ -26,6 +26,7 @@ enum DeviceError : unsigned int {
   kErrWaitMma = 0x102,       // MMA issuer waited too long for operands / accumulator
   kErrWaitEpilogue = 0x103,  // epilogue waited too long for an accumulator
   kErrWaitSoftmax = 0x104,   // attention softmax warps waited too long
+  kErrWaitPeer = 0x105,      // an exchange barrier waited too long for another GPU
   kErrWaitTest = 0x1ff,      // deliberate expiry used by the timeout self-test
 };
 

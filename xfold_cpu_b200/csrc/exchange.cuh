@@ -61,4 +61,45 @@ __global__ void __launch_bounds__(256) exchange_copy_kernel(const __grid_constan
   __threadfence_system();
 }
 
+// Barrier of an exchange between GPUs, lighter than a collective call.  After
+// this GPU's copy kernel (same stream, so its stores are complete and fenced),
+// exchange_signal_kernel writes `epoch` into slot `rank` of every GPU's flag
+// array with system-scope release stores; exchange_wait_kernel then spins,
+// with acquire loads, until every slot of this GPU's own array holds at least
+// `epoch`.  The spin gives up after XFB_WAIT_NS of global time, records
+// kErrWaitPeer and returns, so a peer that never signals cannot hang this GPU.
+constexpr int kMaxPeers = 16;
+
+struct PeerFlags {
+  uint32_t* flags[kMaxPeers];  // each GPU's flag array, as mapped in this process
+  int world;
+  int rank;
+  uint32_t epoch;
+};
+
+__global__ void exchange_signal_kernel(const __grid_constant__ PeerFlags p) {
+  const int s = threadIdx.x;
+  if (s < p.world) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[s] + p.rank), "r"(p.epoch)
+                 : "memory");
+  }
+}
+
+__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch) {
+  const int s = threadIdx.x;
+  if (s >= world) return;
+  const uint64_t start = global_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+    if (static_cast<int32_t>(v - epoch) >= 0) break;
+    if (global_ns() - start > XFB_WAIT_NS) {
+      record_error(kErrWaitPeer);
+      break;
+    }
+    __nanosleep(200);
+  }
+}
+
 }  // namespace xfb

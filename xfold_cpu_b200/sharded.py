@@ -23,8 +23,9 @@ the arithmetic crosses rows:
 
 Exchanges go through one of three classes with the same four patterns:
 `PeerExchange` (one shard per GPU: the library's copy kernel stores each chunk
-straight into the peers' receive buffers over NVLink, then a one-element NCCL
-all-reduce is the barrier), `ProcessGroupExchange` (one shard per process over
+straight into the peers' receive buffers over NVLink, then a flag barrier --
+release stores of an epoch into every GPU's flag array and a bounded wait -- or
+a one-element NCCL all-reduce), `ProcessGroupExchange` (one shard per process over
 torch.distributed all-to-all / all-gather -- NCCL on GPUs, gloo on CPU) and
 `LocalExchange` (all shards in one process, for checking the sharded arithmetic
 on one device).  No kernel reads another GPU's memory: peer traffic is stores
@@ -137,16 +138,22 @@ class PeerExchange:
     """One shard per GPU; each pattern is one launch of the library's exchange
     copy kernel that stores straight into the peers' receive buffers over NVLink
     (mapped into this process by CUDA IPC), each chunk at its final position, so
-    no permute copies are needed on either side.  A one-element NCCL all-reduce
-    after the copy is the barrier: when it completes on a rank, every rank's
-    stores into that rank's buffer have landed.  Receive buffers alternate
-    between two copies per pattern, so the barrier after an exchange also
-    guarantees that nobody still reads the copy the next exchange overwrites
-    (every consumer of a buffer is enqueued before its rank's next barrier).
+    no permute copies are needed on either side.  After the copy comes a
+    barrier: by default the library's flag barrier (each GPU writes an epoch
+    into a flag slot on every GPU with system-scope release stores, then waits,
+    bounded, until its own slots hold it); with barrier="nccl" (or
+    XFB_EXCHANGE_BARRIER=nccl) a one-element NCCL all-reduce.  When the barrier
+    completes on a rank, every rank's stores into that rank's buffer have
+    landed.  Receive buffers alternate between two copies per pattern, so the
+    barrier after an exchange also guarantees that nobody still reads the copy
+    the next exchange overwrites (every consumer of a buffer is enqueued before
+    its rank's next barrier).
     The returned tensors are views of those buffers: valid until the same
     pattern with the same shape has run twice more."""
 
-    def __init__(self, group=None) -> None:
+    def __init__(self, group=None, barrier: str | None = None) -> None:
+        import os
+
         import torch.distributed as dist
 
         self._dist = dist
@@ -156,6 +163,11 @@ class PeerExchange:
         self.ranks = [self.rank]
         self._bufs: dict = {}
         self._flag = None
+        self.barrier = barrier or os.environ.get("XFB_EXCHANGE_BARRIER", "flags")
+        if self.barrier not in ("flags", "nccl"):
+            raise ValueError("barrier must be 'flags' or 'nccl'")
+        self._flags = None  # (local flag array, ctypes array of every GPU's array)
+        self._epoch = 0
 
     # -- receive buffers, shared once per (pattern, shape, dtype)
     def _recv(self, kind, shape, dtype, device):
@@ -177,14 +189,32 @@ class PeerExchange:
         return local, peers
 
     def _copy_and_sync(self, boxes, device):
+        import ctypes
+
         from . import _capi
 
+        stream = torch.cuda.current_stream(device).cuda_stream
         arr = (_capi.CopyBox * len(boxes))(*boxes)
-        _capi.call("xfb_exchange_copy", ctypes_addressof(arr), len(boxes),
-                   torch.cuda.current_stream(device).cuda_stream)
-        if self._flag is None:
-            self._flag = torch.zeros(1, dtype=torch.int32, device=device)
-        self._dist.all_reduce(self._flag, group=self.group)
+        _capi.call("xfb_exchange_copy", ctypes_addressof(arr), len(boxes), stream)
+        if self.barrier == "nccl":
+            if self._flag is None:
+                self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+            self._dist.all_reduce(self._flag, group=self.group)
+            return
+        if self._flags is None:
+            local = torch.zeros(16, dtype=torch.int32, device=device)
+            metas = [None] * self.world
+            self._dist.all_gather_object(metas, _ipc_handle(local), group=self.group)
+            ptrs = [local.data_ptr() if r == self.rank else _ipc_open(*meta)
+                    for r, meta in enumerate(metas)]
+            torch.cuda.synchronize(device)  # the zero fill is done before any peer signals
+            self._dist.barrier(group=self.group)
+            self._flags = (local, (ctypes.c_void_p * self.world)(*ptrs))
+        self._epoch += 1
+        local, peers = self._flags
+        _capi.call("xfb_exchange_signal", ctypes_addressof(peers), self.world, self.rank,
+                   self._epoch, stream)
+        _capi.call("xfb_exchange_wait", local.data_ptr(), self.world, self._epoch, stream)
 
     def _box(self, src_ptr, dst_ptr, d0, d1, d2_bytes, s0, s1, t0, t1):
         from . import _capi
