@@ -360,6 +360,55 @@ XFB_API int xfb_conditioning(const void* x, int64_t m, int64_t k, const void* we
                              const float* bias, int64_t chunk, int sig_mode, void* out,
                              void* stream);
 
+/* ---- Atom transformer: windowed cross-attention (DiffusionCrossAttTransformer,
+ * xfold/nn/diffusion_transformer.py:275-411).  The reference computes these
+ * with torch einsum; its native extension has no counterpart.
+ *
+ * xfb_cross_pair_logits: the transformer's cached pair logits (:376-380):
+ * LayerNorm over the c = 16 channels of pair_cond [subsets][nq][nk][16]
+ * (norm_bias may be null: the reference's LayerNorm has none), projection by
+ * w [blocks*heads][16] bf16 (pair_logits_projection.weight, rows ordered
+ * (block, head)), written bf16 as logits [blocks][subsets][heads][nq][nk]
+ * (the reference's rearrange 'n q k (b h) -> b n h q k'). */
+XFB_API int xfb_cross_pair_logits(const void* pair_cond, int pair_dtype, int64_t subsets,
+                                  int64_t nq, int64_t nk, int64_t c, int64_t blocks,
+                                  int64_t heads, const float* norm_weight, const float* norm_bias,
+                                  double eps, const void* w, void* logits, void* stream);
+
+/* xfb_cross_attention: CrossAttention.forward (:307-350) for subsets windows of
+ * nq = 32 queries and nk = 128 keys, c = 128, 4 heads (the sizes the
+ * reference's DiffusionCrossAttTransformer builds).
+ *   x_q      [subsets*32][128] queries_act (f32 or bf16)
+ *   keys     key_index != null: keys are rows of x_q (flattened, source_rows
+ *            rows): key row r = x_q[key_index[r]] where key_valid[r] != 0 (or
+ *            key_valid null), zeros elsewhere -- atom_layout.convert with the
+ *            queries_to_keys GatherInfo (xfold/nn/atom_layout.py:88-160), fused
+ *            into the keys' LayerNorm; an index outside [0, source_rows) reads
+ *            zeros and sets the device error 0x106.  key_index == null: x_k
+ *            [subsets*128][128] holds the keys.
+ *   mask_q [subsets*32], mask_k [subsets*128] f32 (0 = masked) or null: the
+ *            reference's bias 1e9 * !mask_q[q] * !mask_k[k] (:318-322) enters the
+ *            logits before the pair logits.
+ *   pair_logits [subsets][4][32][128] bf16 or null.
+ *   q_mod_* / k_mod_* [rows][128] bf16: AdaLN sigmoid(scale) and shift of the
+ *            q / k adaptive LayerNorms (no-affine LayerNorm, eps); null = plain.
+ *   packed   [512][128] bf16: q_projection | gating_query | k_projection |
+ *            v_projection weights (nn.Linear layout); q_bias [128] f32 or null.
+ *   wo       [128][128] bf16 adaptive_zero_init.transition2.weight; out_gate
+ *            [subsets*32][128] bf16 sigmoid(adaptive_zero_cond(single_cond_q))
+ *            or null.
+ *   out      [subsets*32][128]: the update (accumulate = 0) or added into an f32
+ *            residual (accumulate = 1, the caller's queries_act += ...). */
+XFB_API int64_t xfb_cross_attention_workspace(int64_t subsets);
+XFB_API int xfb_cross_attention(
+    const void* x_q, int x_dtype, int64_t subsets, int64_t nq, int64_t nk, int64_t c,
+    int64_t heads, const void* x_k, const int64_t* key_index, const uint8_t* key_valid,
+    int64_t source_rows, const float* mask_q, const float* mask_k, const void* pair_logits,
+    double eps, const void* q_mod_scale, const void* q_mod_shift, const void* k_mod_scale,
+    const void* k_mod_shift, const void* packed, const float* q_bias, const void* wo,
+    const void* out_gate, void* out, int out_dtype, int accumulate, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

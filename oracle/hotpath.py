@@ -209,6 +209,72 @@ def pair_logits(pair, params, prefix=""):
     return linear(x, P("single_pair_logits_projection.weight")).permute(2, 0, 1)
 
 
+def atom_layout_convert(gather_idxs, gather_mask, arr):
+    """atom_layout.convert with layout_axes=(-3, -2) (xfold/nn/atom_layout.py:88-160)
+    for arr [A, B, c]: flatten the two layout axes, gather rows by gather_idxs,
+    zero rows whose gather_mask is False."""
+    flat = arr.reshape(-1, arr.shape[-1])
+    out = flat[gather_idxs.long()]
+    return out * gather_mask.to(out.dtype)[..., None]
+
+
+def cross_attention(x_q, x_k, mask_q, mask_k, pair_logits, params, single_cond_q, single_cond_k,
+                    num_head=4, prefix=""):
+    """CrossAttention.forward (xfold/nn/diffusion_transformer.py:307-350) on
+    [subsets, queries, c] / [subsets, keys, c]: AdaLN of both sides, the
+    reference's bias 1e9 * !mask_q[q] * !mask_k[k] (:318-322) added to the
+    scaled logits before the pair logits (:336-340), softmax, gate, AdaLNZero."""
+    P = lambda n: _p(params, prefix, n)
+    bias = 1e9 * mask_q.logical_not()[..., None, :, None] * mask_k.logical_not()[..., None, None, :]
+    xq = adaptive_layer_norm(x_q, single_cond_q, params, True, prefix + "q_adaptive_layernorm.")
+    xk = adaptive_layer_norm(x_k, single_cond_k, params, True, prefix + "k_adaptive_layernorm.")
+    c = xq.shape[-1]
+    d = c // num_head
+    q = linear(xq, P("q_projection.weight"), P("q_projection.bias"))
+    k = linear(xk, P("k_projection.weight"))
+    q = q.reshape(q.shape[:-1] + (num_head, d))
+    k = k.reshape(k.shape[:-1] + (num_head, d))
+    logits = torch.einsum("...qhc,...khc->...hqk", q * d ** (-0.5), k) + bias
+    if pair_logits is not None:
+        logits = logits + pair_logits
+    weights = torch.softmax(logits, dim=-1)
+    v = linear(xk, P("v_projection.weight"))
+    v = v.reshape(v.shape[:-1] + (num_head, d))
+    o = torch.einsum("...hqk,...khc->...qhc", weights, v)
+    o = o.reshape(o.shape[:-2] + (-1,))
+    o = o * torch.sigmoid(linear(xq, P("gating_query.weight")))
+    return ada_ln_zero(o, single_cond_q, params, True, prefix + "adaptive_zero_init.")
+
+
+def cross_pair_logits(pair_cond, params, num_blocks=3, num_head=4, prefix=""):
+    """The cached pair logits of DiffusionCrossAttTransformer
+    (xfold/nn/diffusion_transformer.py:376-380): LN (weight only) then the
+    projection, rearranged 'n q k (b h) -> b n h q k'."""
+    P = lambda n: _p(params, prefix, n)
+    x = layer_norm(pair_cond, P("pair_input_layer_norm.weight"), None)
+    y = linear(x, P("pair_logits_projection.weight"))  # [n, q, k, b*h]
+    s, nq, nk, _ = y.shape
+    return y.reshape(s, nq, nk, num_blocks, num_head).permute(3, 0, 4, 1, 2)
+
+
+def diffusion_cross_att_transformer(queries_act, queries_mask, gather_idxs, gather_mask,
+                                    keys_mask, queries_single_cond, keys_single_cond, pair_cond,
+                                    params, num_blocks=3, num_head=4, prefix=""):
+    """DiffusionCrossAttTransformer.forward (xfold/nn/diffusion_transformer.py:382-411):
+    per block, keys gathered from the current queries, then the cross-attention
+    and the conditioned transition updates.  Returns the new queries_act."""
+    logits = cross_pair_logits(pair_cond, params, num_blocks, num_head, prefix)
+    act = queries_act.clone()
+    for i in range(num_blocks):
+        keys = atom_layout_convert(gather_idxs, gather_mask, act)
+        act = act + cross_attention(act, keys, queries_mask, keys_mask, logits[i], params,
+                                    queries_single_cond, keys_single_cond, num_head,
+                                    f"{prefix}cross_attention.{i}.")
+        act = act + diffusion_transition(act, queries_single_cond, params, True,
+                                         f"{prefix}transition_block.{i}.")
+    return act
+
+
 def pairformer_block(pair, pair_mask, single, seq_mask, params, n_heads=16, n_heads_pair=4,
                      with_single=True, prefix=""):
     """PairformerBlock.forward (xfold/nn/pairformer.py:77-114): five in-place

@@ -2,7 +2,10 @@
 reference implementation itself (xfold, torch backend, CPU).
 
 Usage (from the repository root, with the reference checkout available):
-    PYTHONPATH=<xfold checkout> python tests/golden/make_golden.py
+    PYTHONPATH=<xfold checkout> python tests/golden/make_golden.py [fixture ...]
+
+With fixture names, only those files are written (the random stream is the
+same, so every fixture is reproducible on its own).
 
 Each fixture holds the inputs, the module's state_dict (parameter names of
 the reference modules) and the reference outputs, in float32; `bf16:` entries
@@ -35,7 +38,12 @@ def _init(module: torch.nn.Module, seed: int, std: float = 0.2) -> None:
                 p.copy_(0.1 * torch.randn(p.shape, generator=g))
 
 
+ONLY: set[str] = set()  # fixture names given on the command line; empty = all
+
+
 def _save(name: str, module, inputs: dict, outputs: dict) -> None:
+    if ONLY and name not in ONLY:
+        return
     arrays = {}
     if module is not None:
         for k, v in module.state_dict().items():
@@ -162,6 +170,62 @@ def main() -> None:
     _save("pairformer_block", mod, {"pair": pair, "single": single, "pair_mask": pmask, "seq_mask": seq},
           {"pair": p32, "single": s32, "bf16:pair": p16, "bf16:single": s16})
 
+    # --- CrossAttention of the atom transformer (small widths), masked queries
+    # and keys so that the 1e9 * !mask_q * !mask_k term of the reference is hit
+    from xfold.nn.atom_layout import GatherInfo
+    from xfold.nn.diffusion_transformer import CrossAttention, DiffusionCrossAttTransformer
+
+    s_, nq, nk, c, cs = 3, 4, 6, 16, 16  # the reference ties AdaLNZero's width to key_dim
+    mod = CrossAttention(key_dim=c, value_dim=c, c_single_cond=cs, num_head=4).eval()
+    _init(mod, 70)
+    x_q = torch.randn(s_, nq, c, generator=g)
+    x_k = torch.randn(s_, nk, c, generator=g)
+    mask_q = torch.rand(s_, nq, generator=g) > 0.3
+    mask_k = torch.rand(s_, nk, generator=g) > 0.3
+    mask_q[0, -1] = False
+    mask_k[0, -2:] = False
+    logits = torch.randn(s_, 4, nq, nk, generator=g)
+    scq = torch.randn(s_, nq, cs, generator=g)
+    sck = torch.randn(s_, nk, cs, generator=g)
+    fp32, bf16 = _both(lambda: mod(x_q, x_k, mask_q, mask_k, logits, scq, sck))
+    _save("cross_attention", mod,
+          {"x_q": x_q, "x_k": x_k, "mask_q": mask_q.float(), "mask_k": mask_k.float(),
+           "pair_logits": logits, "single_cond_q": scq, "single_cond_k": sck},
+          {"update": fp32, "bf16:update": bf16})
+
+    # --- DiffusionCrossAttTransformer: the reference's own forward (pair logits
+    # with two blocks, per-block key gather, residual updates) with its
+    # cross-attention modules swapped for small-width ones
+    nb = 2
+    mod = DiffusionCrossAttTransformer(c_query=c, c_single_cond=cs, c_pair_cond=16,
+                                       num_blocks=nb, num_head=4).eval()
+    mod.cross_attention = torch.nn.ModuleList(
+        [CrossAttention(key_dim=c, value_dim=c, c_single_cond=cs, num_head=4) for _ in range(nb)])
+    _init(mod, 80)
+    act = torch.randn(s_, nq, c, generator=g)
+    q_mask = torch.rand(s_, nq, generator=g) > 0.2
+    q_mask[-1, -1] = False
+    idx = torch.randint(0, s_ * nq, (s_, nk), generator=g)
+    gmask = torch.rand(s_, nk, generator=g) > 0.2
+    k_mask = q_mask.reshape(-1)[idx] & gmask
+    qsc = torch.randn(s_, nq, cs, generator=g)
+    ksc = torch.randn(s_, nk, cs, generator=g)
+    pair_cond = torch.randn(s_, nq, nk, 16, generator=g)
+    info = GatherInfo(gather_idxs=idx, gather_mask=gmask,
+                      input_shape=torch.tensor((s_, nq)))
+
+    def transformer():
+        mod._input_cache = type(mod._input_cache)()
+        return mod(act.clone(), q_mask, info, k_mask, qsc, ksc, pair_cond)
+
+    fp32, bf16 = _both(transformer)
+    _save("diffusion_cross_att_transformer", mod,
+          {"queries_act": act, "queries_mask": q_mask.float(), "gather_idxs": idx.float(),
+           "gather_mask": gmask.float(), "keys_mask": k_mask.float(),
+           "queries_single_cond": qsc, "keys_single_cond": ksc, "pair_cond": pair_cond},
+          {"queries_act": fp32, "bf16:queries_act": bf16})
+
 
 if __name__ == "__main__":
+    ONLY.update(sys.argv[1:])
     sys.exit(main())

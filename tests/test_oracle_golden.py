@@ -109,3 +109,49 @@ def test_pairformer_block():
     check(single, o["single"], 1e-5)
     check(o["bf16:pair"] - i["pair"], pair - i["pair"], BF16_TOL)
     check(o["bf16:single"] - i["single"], single - i["single"], BF16_TOL)
+
+
+def _cross(p, i, mask_q=None, mask_k=None):
+    return oracle.cross_attention(i["x_q"], i["x_k"],
+                                  i["mask_q"].bool() if mask_q is None else mask_q,
+                                  i["mask_k"].bool() if mask_k is None else mask_k,
+                                  i["pair_logits"], p, i["single_cond_q"], i["single_cond_k"], 4)
+
+
+def test_cross_attention():
+    p, i, o = load("cross_attention")
+    got = _cross(p, i)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_cross_attention_mask_term_is_pinned():
+    """Planted mistake: without the reference's 1e9 * !mask_q * !mask_k term
+    (all keys visible to every query, as the term leaves valid queries) the
+    masked query rows change and the fixture catches it."""
+    p, i, o = load("cross_attention")
+    ones_q = torch.ones_like(i["mask_q"], dtype=torch.bool)
+    wrong = _cross(p, i, mask_q=ones_q)
+    assert oracle.relative_error(wrong, o["update"]) > 1e-2
+
+
+def _cross_transformer(p, i, gather_idxs):
+    return oracle.diffusion_cross_att_transformer(
+        i["queries_act"], i["queries_mask"].bool(), gather_idxs, i["gather_mask"].bool(),
+        i["keys_mask"].bool(), i["queries_single_cond"], i["keys_single_cond"], i["pair_cond"], p,
+        num_blocks=2, num_head=4)
+
+
+def test_diffusion_cross_att_transformer():
+    p, i, o = load("diffusion_cross_att_transformer")
+    got = _cross_transformer(p, i, i["gather_idxs"].long())
+    check(got, o["queries_act"], FP32_TOL)
+    check(o["bf16:queries_act"] - i["queries_act"], got - i["queries_act"], BF16_TOL)
+
+
+def test_cross_att_transformer_gather_is_pinned():
+    """Planted mistake: a shifted queries -> keys gather must be caught."""
+    p, i, o = load("diffusion_cross_att_transformer")
+    rows = i["queries_act"].shape[0] * i["queries_act"].shape[1]
+    wrong = _cross_transformer(p, i, (i["gather_idxs"].long() + 1) % rows)
+    assert oracle.relative_error(wrong, o["queries_act"]) > 1e-3

@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "layer_norm.cuh"
+#include "window_attention.cuh"
 
 #ifndef XFB_NVCC_FLAGS
 #define XFB_NVCC_FLAGS "unknown"
@@ -293,7 +294,9 @@ int linear_core(const bf16* x, int64_t m, int64_t k, int64_t ldx, const bf16* w,
 int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t ldx,
                    const float* w, const float* b, double eps, bf16* y, int64_t ldy,
                    const bf16* mod_scale, const bf16* mod_shift, const bf16* wh, int heads,
-                   bf16* head_out, int64_t head_ld, cudaStream_t st, float head_scale = 1.f) {
+                   bf16* head_out, int64_t head_ld, cudaStream_t st, float head_scale = 1.f,
+                   const int64_t* gather_idx = nullptr, const uint8_t* gather_valid = nullptr,
+                   int64_t src_rows = 0) {
   if (rows <= 0) return XFB_OK;
   XFB_REQUIRE(x_dtype == XFB_F32 || x_dtype == XFB_BF16, "LayerNorm input must be f32 or bf16");
   XFB_REQUIRE(heads >= 0 && heads <= 16, "head projection supports at most 16 heads");
@@ -314,6 +317,10 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
   a.head_out = head_out;
   a.head_ld = head_ld;
   a.head_scale = head_scale;
+  a.gather_idx = gather_idx;
+  a.gather_valid = gather_valid;
+  a.src_rows = src_rows;
+  XFB_REQUIRE(gather_idx == nullptr || heads == 0, "row gather excludes the head projection");
   int sms;
   XFB_TRY(sm_count(&sms));
   if (c == 128 && heads > 0 && mod_scale == nullptr && mod_shift == nullptr && ldx % 4 == 0 &&
@@ -1734,6 +1741,140 @@ XFB_API int xfb_conditioning(const void* x, int64_t m, int64_t k, const void* we
                                      static_cast<cudaStream_t>(stream));
 }
 
+// ---------------------------------------------------------------- atom cross-attention
+
+XFB_API int xfb_cross_pair_logits(const void* pair_cond, int pair_dtype, int64_t subsets,
+                                  int64_t nq, int64_t nk, int64_t c, int64_t blocks,
+                                  int64_t heads, const float* norm_weight, const float* norm_bias,
+                                  double eps, const void* w, void* logits, void* stream) {
+  XFB_REQUIRE(pair_dtype == XFB_F32 || pair_dtype == XFB_BF16, "pair conditioning must be f32 or bf16");
+  XFB_REQUIRE(subsets >= 0 && nq > 0 && nk > 0, "cross pair logits expect subsets >= 0, nq, nk > 0");
+  XFB_REQUIRE(c == 16, "cross pair logits take 16 pair-conditioning channels");
+  XFB_REQUIRE(blocks > 0 && heads > 0 && blocks * heads <= 16, "blocks * heads must be 1..16");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(w != nullptr && logits != nullptr, "projection weight and output required");
+  XFB_REQUIRE(aligned16(pair_cond), "pair conditioning must be 16-byte aligned");
+  const int64_t pairs = nq * nk;
+  XFB_REQUIRE(pairs < (1 << 30), "window too large");
+  if (subsets == 0) return XFB_OK;
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int64_t total = subsets * pairs;
+  const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(sms) * 8));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pair_dtype == XFB_F32) {
+    xfb::cross_pair_logits_kernel<float><<<grid, 256, 0, st>>>(
+        static_cast<const float*>(pair_cond), subsets, static_cast<int>(pairs),
+        static_cast<int>(heads), static_cast<int>(blocks * heads), norm_weight, norm_bias,
+        static_cast<float>(eps), static_cast<const bf16*>(w), static_cast<bf16*>(logits));
+  } else {
+    xfb::cross_pair_logits_kernel<bf16><<<grid, 256, 0, st>>>(
+        static_cast<const bf16*>(pair_cond), subsets, static_cast<int>(pairs),
+        static_cast<int>(heads), static_cast<int>(blocks * heads), norm_weight, norm_bias,
+        static_cast<float>(eps), static_cast<const bf16*>(w), static_cast<bf16*>(logits));
+  }
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+namespace {
+struct CaWs {
+  bf16 *xq, *xk, *qg, *kv, *o;
+  float* bias;
+};
+void ca_layout(Carver& cv, int64_t subsets, CaWs* w) {
+  const int64_t mq = subsets * xfb::kWinQ, mk = subsets * xfb::kWinK;
+  w->xq = cv.take<bf16>(mq * xfb::kWinC);
+  w->xk = cv.take<bf16>(mk * xfb::kWinC);
+  w->qg = cv.take<bf16>(mq * 2 * xfb::kWinC);
+  w->kv = cv.take<bf16>(mk * 2 * xfb::kWinC);
+  w->o = cv.take<bf16>(mq * xfb::kWinC);
+  w->bias = cv.take<float>(2 * xfb::kWinC);
+}
+}  // namespace
+
+XFB_API int64_t xfb_cross_attention_workspace(int64_t subsets) {
+  if (subsets <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  CaWs w;
+  ca_layout(cv, subsets, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_cross_attention(
+    const void* x_q, int x_dtype, int64_t subsets, int64_t nq, int64_t nk, int64_t c,
+    int64_t heads, const void* x_k, const int64_t* key_index, const uint8_t* key_valid,
+    int64_t source_rows, const float* mask_q, const float* mask_k, const void* pair_logits,
+    double eps, const void* q_mod_scale, const void* q_mod_shift, const void* k_mod_scale,
+    const void* k_mod_shift, const void* packed, const float* q_bias, const void* wo,
+    const void* out_gate, void* out, int out_dtype, int accumulate, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(x_dtype == XFB_F32 || x_dtype == XFB_BF16, "activations must be f32 or bf16");
+  XFB_REQUIRE(subsets >= 0, "subset count must be non-negative");
+  XFB_REQUIRE(nq == xfb::kWinQ && nk == xfb::kWinK && c == xfb::kWinC && heads == xfb::kWinH,
+              "cross-attention windows are 32 queries x 128 keys, c = 128, 4 heads");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(packed != nullptr && wo != nullptr, "attention weights missing");
+  XFB_REQUIRE(key_index != nullptr ? source_rows >= 0 : x_k != nullptr,
+              "keys need either x_k or a gather index");
+  XFB_REQUIRE((q_mod_scale == nullptr) == (q_mod_shift == nullptr) &&
+                  (k_mod_scale == nullptr) == (k_mod_shift == nullptr),
+              "modulation needs both scale and shift");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(aligned16(x_q) && (x_k == nullptr || aligned16(x_k)) && aligned16(packed) &&
+                  aligned16(wo) && aligned16(out) &&
+                  (pair_logits == nullptr || aligned16(pair_logits)) &&
+                  (out_gate == nullptr || aligned16(out_gate)),
+              "cross-attention buffers must be 16-byte aligned");
+  if (subsets == 0) return XFB_OK;
+  XFB_REQUIRE(subsets < (1 << 24), "too many subsets");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  CaWs w;
+  ca_layout(cv, subsets, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t mq = subsets * nq, mk = subsets * nk;
+  const bf16* wcat = static_cast<const bf16*>(packed);  // rows: q | gate | k | v
+  // AdaLN of the queries and of the keys (gathered from the queries' rows)
+  XFB_TRY(run_layer_norm(x_q, x_dtype, mq, c, c, nullptr, nullptr, eps, w.xq, c,
+                         static_cast<const bf16*>(q_mod_scale), static_cast<const bf16*>(q_mod_shift),
+                         nullptr, 0, nullptr, 0, st));
+  if (key_index != nullptr) {
+    XFB_TRY(run_layer_norm(x_q, x_dtype, mk, c, c, nullptr, nullptr, eps, w.xk, c,
+                           static_cast<const bf16*>(k_mod_scale),
+                           static_cast<const bf16*>(k_mod_shift), nullptr, 0, nullptr, 0, st, 1.f,
+                           key_index, key_valid, source_rows));
+  } else {
+    XFB_TRY(run_layer_norm(x_k, x_dtype, mk, c, c, nullptr, nullptr, eps, w.xk, c,
+                           static_cast<const bf16*>(k_mod_scale),
+                           static_cast<const bf16*>(k_mod_shift), nullptr, 0, nullptr, 0, st));
+  }
+  // [q + q_bias | gate] and [k | v]
+  XFB_CUDA(cudaMemsetAsync(w.bias, 0, 2 * c * sizeof(float), st));
+  if (q_bias != nullptr)
+    XFB_CUDA(cudaMemcpyAsync(w.bias, q_bias, c * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  XFB_TRY(linear_core(w.xq, mq, c, c, wcat, 2 * c, w.bias, nullptr, 0, w.qg, 0, 0, 2 * c, st));
+  XFB_TRY(linear_core(w.xk, mk, c, c, wcat + 2 * c * c, 2 * c, nullptr, nullptr, 0, w.kv, 0, 0,
+                      2 * c, st));
+  {
+    XFB_TRY(set_smem(xfb::window_attention_kernel, xfb::WinSmem::kLaunchBytes));
+    xfb::WindowAttnArgs a;
+    a.qg = w.qg;
+    a.kv = w.kv;
+    a.bias = static_cast<const bf16*>(pair_logits);
+    a.mask_q = mask_q;
+    a.mask_k = mask_k;
+    a.out = w.o;
+    a.q_scale = 1.f / std::sqrt(static_cast<float>(c / heads));
+    xfb::window_attention_kernel<<<static_cast<unsigned>(subsets), 128, xfb::WinSmem::kLaunchBytes,
+                                   st>>>(a);
+    XFB_LAUNCHED();
+  }
+  return linear_core(w.o, mq, c, c, static_cast<const bf16*>(wo), c, nullptr,
+                     static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32, accumulate,
+                     c, st);
+}
 
 XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,
                                 void* stream) {

@@ -27,6 +27,7 @@ enum DeviceError : unsigned int {
   kErrWaitEpilogue = 0x103,  // epilogue waited too long for an accumulator
   kErrWaitSoftmax = 0x104,   // attention softmax warps waited too long
   kErrWaitPeer = 0x105,      // an exchange barrier waited too long for another GPU
+  kErrIndex = 0x106,         // a gather index outside its source (row read as zeros)
   kErrWaitTest = 0x1ff,      // deliberate expiry used by the timeout self-test
 };
 

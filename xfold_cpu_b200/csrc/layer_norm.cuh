@@ -60,6 +60,9 @@ struct LnArgs {
   __nv_bfloat16* head_out;         // [H][head_ld]
   int64_t head_ld;
   float head_scale;                // multiplies the head projection before rounding
+  const int64_t* gather_idx;       // [rows] source row of each output row, or null
+  const uint8_t* gather_valid;     // [rows] zero = the output row reads zeros; or null
+  int64_t src_rows;                // rows of x that gather_idx may address
 };
 
 // C = 32 * 4 * R channels: each lane holds R groups of 4 consecutive channels.
@@ -96,12 +99,28 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
     }
 
   for (int64_t row = warp_id; row < a.rows; row += warps_total) {
-    const InT* xr = reinterpret_cast<const InT*>(a.x) + row * a.ldx;
+    // optional row gather (the atom layout's queries -> keys): masked-out rows
+    // and indices outside the source read zeros
+    int64_t src = row;
+    bool zero = false;
+    if (a.gather_idx != nullptr) {
+      src = a.gather_idx[row];
+      zero = a.gather_valid != nullptr && a.gather_valid[row] == 0;
+      if (!zero && (src < 0 || src >= a.src_rows)) {
+        if (lane == 0) record_error(kErrIndex);
+        zero = true;
+      }
+      if (zero) src = 0;
+    }
+    const InT* xr = reinterpret_cast<const InT*>(a.x) + src * a.ldx;
     float v[R][V];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int ch = r * 32 * V + lane * V;
-      if constexpr (V == 4) {
+      if (zero) {
+#pragma unroll
+        for (int e = 0; e < V; ++e) v[r][e] = 0.f;
+      } else if constexpr (V == 4) {
         load_vec4<InT>(xr + ch, v[r]);
       } else {
         v[r][0] = static_cast<float>(xr[ch]);

@@ -542,3 +542,93 @@ def conditioning(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | Non
     _capi.call("xfb_conditioning", _ptr(x), m, k, _ptr(weight), n, _ptr(b), chunk, sig_mode,
                _ptr(out), _stream(device))
     return out
+
+
+# ----------------------------------------------------------------------------- atom cross-attention
+
+def cross_pair_logits(pair_cond: torch.Tensor, norm_weight: torch.Tensor | None,
+                      norm_bias: torch.Tensor | None, eps: float, weight: torch.Tensor,
+                      num_blocks: int, num_head: int) -> torch.Tensor:
+    """[blocks, subsets, heads, nq, nk] bf16 = rearrange(LN(pair_cond) @ weight^T,
+    'n q k (b h) -> b n h q k') (xfold/nn/diffusion_transformer.py:376-380)."""
+    device = _check_cuda(pair_cond, weight)
+    if pair_cond.dim() != 4:
+        raise ValueError("pair_cond must be [subsets, queries, keys, channels]")
+    s, nq, nk, c = pair_cond.shape
+    if weight.shape != (num_blocks * num_head, c):
+        raise ValueError("pair logits weight must be [blocks * heads, channels]")
+    pair_cond = _contig(pair_cond)
+    logits = torch.empty((num_blocks, s, num_head, nq, nk), dtype=torch.bfloat16, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    w = prepare_weight(weight)
+    _capi.call("xfb_cross_pair_logits", _ptr(pair_cond), _code(pair_cond), s, nq, nk, c,
+               num_blocks, num_head, _ptr(nw), _ptr(nb), float(eps), _ptr(w), _ptr(logits),
+               _stream(device))
+    return logits
+
+
+def pack_cross_attention_weights(q_w: torch.Tensor, gate_w: torch.Tensor, k_w: torch.Tensor,
+                                 v_w: torch.Tensor) -> torch.Tensor:
+    """[4c, c] bf16 rows q_projection | gating_query | k_projection | v_projection."""
+    return pack_attention_weights(q_w, gate_w, k_w, v_w)
+
+
+def cross_attention(x_q: torch.Tensor, keys, mask_q: torch.Tensor | None,
+                    mask_k: torch.Tensor | None, pair_logits: torch.Tensor | None, eps: float,
+                    packed: torch.Tensor, q_bias: torch.Tensor | None, wo: torch.Tensor,
+                    q_mod: tuple | None = None, k_mod: tuple | None = None,
+                    out_gate: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                    accumulate: bool = False,
+                    out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """CrossAttention update (xfold/nn/diffusion_transformer.py:307-350) over
+    windows of 32 queries x 128 keys, c = 128, 4 heads.
+
+    x_q [subsets, 32, 128]; keys is either x_k [subsets, 128, 128] or a pair
+    (index [subsets, 128] int64, valid [subsets, 128] bool) selecting rows of
+    x_q flattened to [subsets*32, 128] (valid False -> zero row), the
+    queries_to_keys gather fused into the keys' LayerNorm.  q_mod / k_mod are
+    (sigmoid(scale), shift) of the adaptive LayerNorms, out_gate the AdaLNZero
+    gate, all [rows, 128] bf16."""
+    device = _check_cuda(x_q, packed, wo, pair_logits, out_gate)
+    if x_q.dim() != 3:
+        raise ValueError("x_q must be [subsets, queries, channels]")
+    s, nq, c = x_q.shape
+    nk = 128
+    x_q = _contig(x_q)
+    x_k = index = valid = None
+    rows = s * nq
+    if isinstance(keys, torch.Tensor):
+        _check_cuda(keys)
+        if keys.dim() != 3 or keys.shape[0] != s or keys.shape[2] != c:
+            raise ValueError("x_k must be [subsets, keys, channels]")
+        nk = keys.shape[1]
+        x_k = _contig(keys, x_q.dtype)
+    else:
+        index, valid = keys
+        _check_cuda(index, valid)
+        if index.shape != valid.shape or index.dim() != 2 or index.shape[0] != s:
+            raise ValueError("key gather index and mask must both be [subsets, keys]")
+        nk = index.shape[1]
+        index = _contig(index, torch.int64)
+        valid = _contig(valid, torch.bool)
+    if mask_q is not None:
+        mask_q = _contig(mask_q.expand(s, nq), torch.float32)
+    if mask_k is not None:
+        mask_k = _contig(mask_k.expand(s, nk), torch.float32)
+    if pair_logits is not None:
+        if tuple(pair_logits.shape[-3:]) != (4, nq, nk):
+            raise ValueError("pair logits must be [subsets, heads, queries, keys]")
+        pair_logits = _contig(pair_logits, torch.bfloat16)
+    qs, qh = (None, None) if q_mod is None else (_contig(t, torch.bfloat16) for t in q_mod)
+    ks, kh = (None, None) if k_mod is None else (_contig(t, torch.bfloat16) for t in k_mod)
+    out_gate = _contig(out_gate, torch.bfloat16)
+    if out is None:
+        out = torch.empty((s, nq, c), dtype=out_dtype, device=device)
+    qb, wo = _contig(q_bias, torch.float32), prepare_weight(wo)
+    ws = _workspace(_capi.load().xfb_cross_attention_workspace(s), device)
+    _capi.call("xfb_cross_attention", _ptr(x_q), _code(x_q), s, nq, nk, c, 4, _ptr(x_k),
+               _ptr(index), _ptr(valid), rows, _ptr(mask_q), _ptr(mask_k), _ptr(pair_logits),
+               float(eps), _ptr(qs), _ptr(qh), _ptr(ks), _ptr(kh), _ptr(packed), _ptr(qb),
+               _ptr(wo), _ptr(out_gate), _ptr(out), _code(out), 1 if accumulate else 0, _ptr(ws),
+               ws.numel(), _stream(device))
+    return out

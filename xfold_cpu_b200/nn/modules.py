@@ -14,6 +14,8 @@ stream in place through the fused epilogue (the `x += op(x)` of the callers).
   DiffusionTransition      xfold/nn/diffusion_transformer.py:98-128
   SelfAttention            xfold/nn/diffusion_transformer.py:131-217
   DiffusionTransformer     xfold/nn/diffusion_transformer.py:220-272
+  CrossAttention           xfold/nn/diffusion_transformer.py:275-350
+  DiffusionCrossAttTransformer  xfold/nn/diffusion_transformer.py:353-411
   PairformerBlock          xfold/nn/pairformer.py:26-114
 """
 
@@ -26,6 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import native
+from . import atom_layout
 from ..fastnn import LayerNorm, WeightCache
 from ..fastnn import config
 
@@ -294,6 +297,43 @@ class SelfAttention(nn.Module):
         return x
 
 
+def _modulations(cache: WeightCache, ada: list, single_cond: torch.Tensor, c: int) -> torch.Tensor:
+    """(sigmoid(scale), shift) of every AdaptiveLayerNorm in `ada` from the same
+    single_cond: [2 * len(ada), N, c] bf16, chunks (scale_0, shift_0, scale_1, ...).
+
+    LayerNorm(single_cond) without its weight, then one GEMM against the
+    modules' scale / shift weights with that LayerNorm weight folded in
+    (diffusion_transformer.py:51-62 per module).  The modules share eps."""
+
+    def build(*_):
+        ws, bs = [], []
+        for m in ada:
+            g = m.single_cond_layer_norm.weight.float()
+            ws += [m.single_cond_scale.weight.float() * g, m.single_cond_bias.weight.float() * g]
+            bs += [m.single_cond_scale.bias.float(), torch.zeros_like(m.single_cond_scale.bias.float())]
+        return torch.cat(ws).bfloat16().contiguous(), torch.cat(bs).contiguous()
+
+    src = [t for m in ada for t in (m.single_cond_layer_norm.weight, m.single_cond_scale.weight,
+                                    m.single_cond_scale.bias, m.single_cond_bias.weight)]
+    w, b = cache.get(src, build)
+    sc = native.layer_norm(single_cond, None, None, ada[0].single_cond_layer_norm.eps)
+    return native.conditioning(sc, w, b, c, 1)
+
+
+def _gates(cache: WeightCache, zero: list, single_cond: torch.Tensor, c: int) -> torch.Tensor:
+    """sigmoid(adaptive_zero_cond(single_cond)) of every AdaLNZero in `zero`
+    (diffusion_transformer.py:85-94): [len(zero), N, c] bf16, one GEMM."""
+
+    def build(*_):
+        w = torch.cat([z.adaptive_zero_cond.weight.float() for z in zero]).bfloat16()
+        b = torch.cat([z.adaptive_zero_cond.bias.float() for z in zero])
+        return w.contiguous(), b.contiguous()
+
+    src = [t for z in zero for t in (z.adaptive_zero_cond.weight, z.adaptive_zero_cond.bias)]
+    w, b = cache.get(src, build)
+    return native.conditioning(single_cond, w, b, c, 2)
+
+
 class DiffusionTransformer(nn.Module):
     def __init__(self, c_act: int = 768, c_single_cond: int = 384, c_pair_cond: int = 128,
                  num_head: int = 16, num_blocks: int = 24, super_block_size: int = 4) -> None:
@@ -341,29 +381,8 @@ class DiffusionTransformer(nn.Module):
         (attention, transition) triples of contiguous [N, c_act] bf16 views."""
         ada = list(self._adaln_modules())
         zero = list(self._zero_modules())
-
-        def build_mod(*_):
-            ws, bs = [], []
-            for m in ada:
-                g = m.single_cond_layer_norm.weight.float()
-                ws += [m.single_cond_scale.weight.float() * g, m.single_cond_bias.weight.float() * g]
-                bs += [m.single_cond_scale.bias.float(), torch.zeros_like(m.single_cond_scale.bias.float())]
-            return torch.cat(ws).bfloat16().contiguous(), torch.cat(bs).contiguous()
-
-        def build_gate(*_):
-            w = torch.cat([z.adaptive_zero_cond.weight.float() for z in zero]).bfloat16()
-            b = torch.cat([z.adaptive_zero_cond.bias.float() for z in zero])
-            return w.contiguous(), b.contiguous()
-
-        mod_src = [t for m in ada for t in (m.single_cond_layer_norm.weight, m.single_cond_scale.weight,
-                                            m.single_cond_scale.bias, m.single_cond_bias.weight)]
-        gate_src = [t for z in zero for t in (z.adaptive_zero_cond.weight, z.adaptive_zero_cond.bias)]
-        w_mod, b_mod = self._cond_w.get(mod_src, build_mod)
-        w_gate, b_gate = self._gate_w.get(gate_src, build_gate)
-        eps = ada[0].single_cond_layer_norm.eps
-        sc = native.layer_norm(single_cond, None, None, eps)
-        mod = native.conditioning(sc, w_mod, b_mod, self.c_act, 1)  # [4 * blocks, N, c]
-        gate = native.conditioning(single_cond, w_gate, b_gate, self.c_act, 2)  # [2 * blocks, N, c]
+        mod = _modulations(self._cond_w, ada, single_cond, self.c_act)  # [4 * blocks, N, c]
+        gate = _gates(self._gate_w, zero, single_cond, self.c_act)  # [2 * blocks, N, c]
         return [((mod[4 * i], mod[4 * i + 1], gate[2 * i]),
                  (mod[4 * i + 2], mod[4 * i + 3], gate[2 * i + 1])) for i in range(self.num_blocks)]
 
@@ -447,6 +466,170 @@ class DiffusionStepGraph:
         self.single_cond.copy_(single_cond)
         self.graph.replay()
         return self.out
+
+
+class CrossAttention(nn.Module):
+    """Windowed cross-attention of the atom transformer: 32 queries x 128 keys
+    per subset, c = 128, 4 heads (the sizes DiffusionCrossAttTransformer builds);
+    other sizes raise ValueError."""
+
+    def __init__(self, key_dim: int = 128, value_dim: int = 128, c_single_cond: int = 128,
+                 num_head: int = 4) -> None:
+        super().__init__()
+        self.key_dim = key_dim
+        self.value_dim = value_dim
+        self.c_single_cond = c_single_cond
+        self.num_head = num_head
+        self.key_dim_per_head = key_dim // num_head
+        self.value_dim_per_head = value_dim // num_head
+        self.q_scale = self.key_dim_per_head ** (-0.5)
+        self.q_adaptive_layernorm = AdaptiveLayerNorm(key_dim, c_single_cond, use_single_cond=True)
+        self.k_adaptive_layernorm = AdaptiveLayerNorm(key_dim, c_single_cond, use_single_cond=True)
+        self.q_projection = nn.Linear(key_dim, key_dim, bias=True)
+        self.k_projection = nn.Linear(key_dim, key_dim, bias=False)
+        self.v_projection = nn.Linear(value_dim, value_dim, bias=False)
+        self.gating_query = nn.Linear(key_dim, value_dim, bias=False)
+        self.adaptive_zero_init = AdaLNZero(value_dim, value_dim, key_dim, use_single_cond=True)
+        self._packed = WeightCache()
+        self._wo = WeightCache()
+
+    def _run(self, x_q, keys, mask_q, mask_k, pair_logits, single_cond_q, single_cond_k, out,
+             accumulate, cond=None):
+        config.require_cuda("dot_product_attention_implementation")
+        if (self.key_dim, self.value_dim, self.num_head) != (128, 128, 4):
+            raise ValueError("the cuda backend's cross-attention takes key_dim = value_dim = 128, "
+                             "4 heads")
+        packed = self._packed.get(
+            (self.q_projection.weight, self.gating_query.weight, self.k_projection.weight,
+             self.v_projection.weight), native.pack_cross_attention_weights)
+        if cond is not None:  # (q_scale, q_shift, k_scale, k_shift, gate), all blocks at once
+            qs, qh, ks, kh, gate = cond
+        else:
+            qs, qh = self.q_adaptive_layernorm.modulation(single_cond_q.reshape(-1, self.c_single_cond))
+            ks, kh = self.k_adaptive_layernorm.modulation(single_cond_k.reshape(-1, self.c_single_cond))
+            gate = self.adaptive_zero_init.out_gate(single_cond_q.reshape(-1, self.c_single_cond))
+        eps = self.q_adaptive_layernorm.layer_norm.eps
+        return native.cross_attention(
+            x_q, keys, mask_q, mask_k, pair_logits, eps, packed, self.q_projection.bias,
+            _bf16(self._wo, self.adaptive_zero_init.transition2.weight), q_mod=(qs, qh),
+            k_mod=(ks, kh), out_gate=gate, out=out, accumulate=accumulate)
+
+    def forward(self, x_q: torch.Tensor, x_k: torch.Tensor, mask_q: torch.Tensor,
+                mask_k: torch.Tensor, pair_logits: Optional[torch.Tensor] = None,
+                single_cond_q: Optional[torch.Tensor] = None,
+                single_cond_k: Optional[torch.Tensor] = None) -> torch.Tensor:
+        assert mask_q.dim() == x_q.dim() - 1 and mask_k.dim() == x_k.dim() - 1
+        return self._run(x_q, x_k, mask_q, mask_k, pair_logits, single_cond_q, single_cond_k,
+                         None, False)
+
+    def accumulate_(self, x_q, keys, mask_q, mask_k, pair_logits=None, single_cond_q=None,
+                    single_cond_k=None, cond=None):
+        """x_q += forward(...), with keys either x_k or the (index, valid) gather
+        of x_q's rows (atom_layout.key_gather)."""
+        if _fused_target(x_q):
+            return self._run(x_q, keys, mask_q, mask_k, pair_logits, single_cond_q, single_cond_k,
+                             x_q, True, cond)
+        x_q += self._run(x_q, keys, mask_q, mask_k, pair_logits, single_cond_q, single_cond_k,
+                         None, False, cond)
+        return x_q
+
+
+class DiffusionCrossAttTransformer(nn.Module):
+    def __init__(self, c_query: int = 128, c_single_cond: int = 128, c_pair_cond: int = 16,
+                 num_blocks: int = 3, num_head: int = 4) -> None:
+        super().__init__()
+        self.c_query = c_query
+        self.c_single_cond = c_single_cond
+        self.c_pair_cond = c_pair_cond
+        self.num_blocks = num_blocks
+        self.num_head = num_head
+        self.pair_input_layer_norm = LayerNorm(c_pair_cond, bias=False)
+        self.pair_logits_projection = nn.Linear(c_pair_cond, num_blocks * num_head, bias=False)
+        self.cross_attention = nn.ModuleList(
+            [CrossAttention(num_head=num_head) for _ in range(num_blocks)])
+        self.transition_block = nn.ModuleList(
+            [DiffusionTransition(c_x=c_query, c_single_cond=c_single_cond, use_single_cond=True)
+             for _ in range(num_blocks)])
+        self._logits_key = None
+        self._logits = None
+        self._gather_key = None
+        self._gather = None
+        self._q_mod_w = WeightCache()
+        self._k_mod_w = WeightCache()
+        self._gate_w = WeightCache()
+
+    def pair_logits(self, pair_cond: torch.Tensor) -> torch.Tensor:
+        """[blocks, subsets, heads, q, k] bf16, cached per pair_cond version like
+        the reference's InputCache (diffusion_transformer.py:376-380)."""
+        try:
+            key = (pair_cond.data_ptr(), pair_cond._version, tuple(pair_cond.shape),
+                   self.pair_logits_projection.weight.data_ptr(),
+                   self.pair_logits_projection.weight._version,
+                   self.pair_input_layer_norm.weight.data_ptr(),
+                   self.pair_input_layer_norm.weight._version)
+        except RuntimeError:  # inference tensors carry no version counter: no reuse
+            key = None
+        if key is None or key != self._logits_key:
+            ln = self.pair_input_layer_norm
+            self._logits = native.cross_pair_logits(pair_cond, ln.weight, ln.bias, ln.eps,
+                                                    self.pair_logits_projection.weight,
+                                                    self.num_blocks, self.num_head)
+            self._logits_key = key
+        return self._logits
+
+    def key_gather(self, queries_to_keys, source_rows: int, device: torch.device):
+        """(index, valid) of the keys on the device, cached per GatherInfo."""
+        try:
+            key = (queries_to_keys.gather_idxs.data_ptr(), queries_to_keys.gather_idxs._version,
+                   queries_to_keys.gather_mask.data_ptr(), queries_to_keys.gather_mask._version,
+                   source_rows, device)
+        except RuntimeError:
+            key = None
+        if key is None or key != self._gather_key:
+            self._gather = atom_layout.key_gather(queries_to_keys, source_rows, device)
+            self._gather_key = key
+        return self._gather
+
+    def conditioning(self, queries_single_cond: torch.Tensor, keys_single_cond: torch.Tensor):
+        """Every block's conditioning for one call: per block
+        ((q_scale, q_shift, k_scale, k_shift, attention gate),
+         (transition scale, transition shift, transition gate)), [rows, c] bf16.
+        The reference recomputes each from the same single conditionings."""
+        c = self.c_query
+        qsc = queries_single_cond.reshape(-1, self.c_single_cond)
+        ksc = keys_single_cond.reshape(-1, self.c_single_cond)
+        q_ada, zero, k_ada = [], [], []
+        for i in range(self.num_blocks):
+            q_ada += [self.cross_attention[i].q_adaptive_layernorm,
+                      self.transition_block[i].adaptive_layernorm]
+            zero += [self.cross_attention[i].adaptive_zero_init,
+                     self.transition_block[i].adaptive_zero_init]
+            k_ada.append(self.cross_attention[i].k_adaptive_layernorm)
+        qm = _modulations(self._q_mod_w, q_ada, qsc, c)  # [4 * blocks, rows_q, c]
+        km = _modulations(self._k_mod_w, k_ada, ksc, c)  # [2 * blocks, rows_k, c]
+        gate = _gates(self._gate_w, zero, qsc, c)  # [2 * blocks, rows_q, c]
+        return [((qm[4 * i], qm[4 * i + 1], km[2 * i], km[2 * i + 1], gate[2 * i]),
+                 (qm[4 * i + 2], qm[4 * i + 3], gate[2 * i + 1])) for i in range(self.num_blocks)]
+
+    def run_blocks(self, queries_act, queries_mask, keys, keys_mask, queries_single_cond,
+                   keys_single_cond, logits):
+        """The blocks of forward() with the pair logits and the key gather given."""
+        cond = self.conditioning(queries_single_cond, keys_single_cond)
+        for i in range(self.num_blocks):
+            self.cross_attention[i].accumulate_(queries_act, keys, queries_mask, keys_mask,
+                                                logits[i], queries_single_cond, keys_single_cond,
+                                                cond=cond[i][0])
+            self.transition_block[i].accumulate_(queries_act, queries_single_cond, cond=cond[i][1])
+        return queries_act
+
+    def forward(self, queries_act: torch.Tensor, queries_mask: torch.Tensor, queries_to_keys,
+                keys_mask: torch.Tensor, queries_single_cond: torch.Tensor,
+                keys_single_cond: torch.Tensor, pair_cond: torch.Tensor) -> torch.Tensor:
+        """Updates queries_act [subsets, queries, c] in place and returns it."""
+        s, nq, _ = queries_act.shape
+        keys = self.key_gather(queries_to_keys, s * nq, queries_act.device)
+        return self.run_blocks(queries_act, queries_mask, keys, keys_mask, queries_single_cond,
+                               keys_single_cond, self.pair_logits(pair_cond))
 
 
 class PairformerBlock(nn.Module):
