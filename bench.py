@@ -279,9 +279,10 @@ def _diffusion_c5(dev, steps: int) -> dict:
     from xfold_cpu_b200.nn import DiffusionTransformer, init_params_
 
     n, c = 768, 768
-    mod = DiffusionTransformer(c_act=c).eval()
-    init_params_(mod, seed=4)
-    mod = mod.to(dev)
+    with torch.inference_mode(False):  # parameters with version counters: weight caches hit
+        mod = DiffusionTransformer(c_act=c).eval()
+        init_params_(mod, seed=4)
+        mod = mod.to(dev)
     g = torch.Generator(device=dev).manual_seed(4)
     act = torch.randn(n, c, device=dev, generator=g)
     cond = torch.randn(n, 384, device=dev, generator=g)
@@ -317,6 +318,124 @@ def _diffusion_c5(dev, steps: int) -> dict:
                 out["kernel_launches_per_step"] = int((_capi.launch_count() - l0) // reps)
         del step
     return out
+
+
+ATOM_SUBSETS = 192  # C5: N_atom = 6144 in windows of 32 queries
+
+
+def _atom_windows(subsets: int, masked_tail: int):
+    """Synthetic atom layout of C5: the keys of subset s are the 128 atoms
+    centred on its 32 queries (atoms outside [0, N_atom) invalid), the last
+    `masked_tail` atoms are padding (queries_mask False), keys_mask is the
+    queries mask gathered as the reference's encoder derives it."""
+    import torch
+
+    from xfold_cpu_b200.nn import GatherInfo
+
+    rows = subsets * 32
+    idx = (torch.arange(subsets)[:, None] * 32 - 48) + torch.arange(128)[None, :]
+    valid = (idx >= 0) & (idx < rows)
+    idx = torch.where(valid, idx, torch.zeros_like(idx))
+    qmask = torch.ones(rows, dtype=torch.bool)
+    qmask[rows - masked_tail:] = False
+    info = GatherInfo(gather_idxs=idx, gather_mask=valid, input_shape=torch.tensor((subsets, 32)))
+    return info, qmask.reshape(subsets, 32), qmask[idx] & valid
+
+
+def _atom_inputs(subsets: int, seed: int):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    act = torch.randn(subsets, 32, 128, generator=g)
+    qsc = torch.randn(subsets, 32, 128, generator=g)
+    pair_cond = torch.randn(subsets, 32, 128, 16, generator=g)
+    return act, qsc, pair_cond
+
+
+def _atom_c5(dev, steps: int) -> dict:
+    """BASELINE config C5's atom transformer: N_atom = 6144 (192 windows of 32
+    queries x 128 keys), c = 128, 4 heads, 3 blocks, 5 % padded atoms, random
+    init N(0, 0.02), seed 4.  One call = DiffusionCrossAttTransformer.forward
+    with its pair logits cached (the reference caches them across denoising
+    steps): the conditioning of the three blocks and the blocks, timed eager
+    and as a replayed CUDA graph.  The encoder and the decoder each make one
+    such call per denoising step."""
+    import torch
+
+    from xfold_cpu_b200 import _capi
+    from xfold_cpu_b200.nn import DiffusionCrossAttTransformer, atom_layout, init_params_
+
+    s = ATOM_SUBSETS
+    with torch.inference_mode(False):  # parameters with version counters: weight caches hit
+        mod = DiffusionCrossAttTransformer().eval()
+        init_params_(mod, seed=4)
+        mod = mod.to(dev)
+    info, qmask, kmask = _atom_windows(s, (s * 32) // 20)
+    act, qsc, pair_cond = (t.to(dev) for t in _atom_inputs(s, 4))
+    qmask, kmask = qmask.to(dev), kmask.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {"n_atom": s * 32, "subsets": s, "queries": 32, "keys": 128, "c_atom": 128, "heads": 4,
+           "blocks": 3, "data": "synthetic centred windows, random init"}
+    with torch.inference_mode():
+        ksc = atom_layout.convert(info, qsc, layout_axes=(-3, -2))
+        keys = mod.key_gather(info, s * 32, dev)
+        logits = mod.pair_logits(pair_cond)
+        work = act.clone()
+
+        def eager():
+            work.copy_(act)
+            mod.run_blocks(work, qmask, keys, kmask, qsc, ksc, logits)
+
+        step = mod.capture(act, qmask, info, kmask, qsc, ksc, pair_cond)
+        for name, fn in (("eager_ms", eager), ("graph_ms", lambda: step(act, qsc, ksc))):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            l0 = _capi.launch_count()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = max(steps, 20)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            out[name] = round(e0.elapsed_time(e1) / reps, 4)
+            if name == "eager_ms":
+                out["kernel_launches_per_call"] = int((_capi.launch_count() - l0) // reps)
+        del step
+    return out
+
+
+def cpu_baseline_atom(threads: int | None = None) -> dict:
+    """The CPU oracle (the reference's torch path restated, float32) of one
+    C5 atom-transformer call at full size, on the host's cores."""
+    import torch
+
+    import oracle
+    from xfold_cpu_b200.nn import DiffusionCrossAttTransformer, init_params_
+
+    if threads:
+        torch.set_num_threads(threads)
+    s = ATOM_SUBSETS
+    mod = DiffusionCrossAttTransformer()
+    init_params_(mod, seed=4)
+    params = {k: v.detach().clone() for k, v in mod.state_dict().items()}
+    info, qmask, kmask = _atom_windows(s, (s * 32) // 20)
+    act, qsc, pair_cond = _atom_inputs(s, 4)
+    ksc = oracle.atom_layout_convert(info.gather_idxs, info.gather_mask, qsc)
+    args = (act, qmask, info.gather_idxs, info.gather_mask, kmask, qsc, ksc, pair_cond, params)
+    with torch.inference_mode():
+        logits = oracle.cross_pair_logits(pair_cond, params)  # cached, as on the GPU
+        oracle.diffusion_cross_att_transformer(*args, logits=logits)  # warm-up
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            oracle.diffusion_cross_att_transformer(*args, logits=logits)
+        dt = (time.perf_counter() - t0) / reps
+    return {"value": round(dt * 1e3, 2), "unit": "ms/call", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{reps} full C5 atom-transformer calls (pair logits cached), "
+                                      "fp32 torch CPU oracle of the reference torch path"}
 
 
 def run_cuda(args) -> None:
@@ -420,10 +539,13 @@ def run_cuda(args) -> None:
 
         roof = _kernel_roofline(dev, args.steps, peaks) if rank == 0 else {}
         c5 = _diffusion_c5(dev, args.steps) if rank == 0 and world == 1 else None
+        atom = _atom_c5(dev, args.steps) if rank == 0 and world == 1 else None
 
     if rank != 0:
         return
     base = cpu_baseline(sample_n=256) if world == 1 else None
+    if atom is not None:
+        atom["cpu_port"] = cpu_baseline_atom()
     dominant = max(roof.values(), key=lambda r: r["ms_per_launch"]) if roof else None
     line = {
         "metric": METRIC, "value": round(step_ms / n_blocks, 4), "unit": UNIT, "n_gpus": world,
@@ -456,7 +578,7 @@ def run_cuda(args) -> None:
         "clocks": clocks,
         "cpu_baseline": base,
         "finite": finite,
-        "extras": {"diffusion_transformer_c5": c5} if c5 else None,
+        "extras": {"diffusion_transformer_c5": c5, "atom_transformer_c5": atom} if c5 else None,
     }
     print(json.dumps(line), flush=True)
 

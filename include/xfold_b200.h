@@ -352,7 +352,8 @@ XFB_API int xfb_ipc_close(void* peer_ptr, int64_t offset);
  * out = act(x W^T + bias) bf16, where x [m][k] bf16 is the (LayerNorm'd) single
  * conditioning and W [n][k] bf16 stacks the blocks' AdaLN scale / shift weights
  * (LayerNorm weight folded in) or AdaLNZero gate weights.  The n columns are
- * written as n / chunk contiguous [m][chunk] tensors; act = sigmoid on every
+ * written as n / chunk contiguous [m][chunk] tensors (chunk a multiple of 64
+ * that divides n); act = sigmoid on every
  * chunk (sig_mode 2), on the even chunks (1) or none (0).  Replaces, per block,
  * AdaptiveLayerNorm's conditioning (xfold/nn/diffusion_transformer.py:51-62) and
  * AdaLNZero's gate (:85-94), which the reference recomputes for each block. */

@@ -259,11 +259,13 @@ def cross_pair_logits(pair_cond, params, num_blocks=3, num_head=4, prefix=""):
 
 def diffusion_cross_att_transformer(queries_act, queries_mask, gather_idxs, gather_mask,
                                     keys_mask, queries_single_cond, keys_single_cond, pair_cond,
-                                    params, num_blocks=3, num_head=4, prefix=""):
+                                    params, num_blocks=3, num_head=4, prefix="", logits=None):
     """DiffusionCrossAttTransformer.forward (xfold/nn/diffusion_transformer.py:382-411):
     per block, keys gathered from the current queries, then the cross-attention
-    and the conditioned transition updates.  Returns the new queries_act."""
-    logits = cross_pair_logits(pair_cond, params, num_blocks, num_head, prefix)
+    and the conditioned transition updates.  Returns the new queries_act.
+    `logits` passes the pair logits the reference holds in its input cache."""
+    if logits is None:
+        logits = cross_pair_logits(pair_cond, params, num_blocks, num_head, prefix)
     act = queries_act.clone()
     for i in range(num_blocks):
         keys = atom_layout_convert(gather_idxs, gather_mask, act)

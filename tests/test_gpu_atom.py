@@ -185,3 +185,31 @@ def test_cross_attention_rejects_other_widths():
         mod(x, torch.randn(1, NK, 64, device=DEV), torch.ones(1, NQ, device=DEV),
             torch.ones(1, NK, device=DEV), None, torch.randn(1, NQ, 64, device=DEV),
             torch.randn(1, NK, 64, device=DEV))
+
+
+def test_cross_att_transformer_cuda_graph_matches_eager():
+    """A captured atom transformer replays the same kernels: bit-identical to
+    the eager blocks on inputs that were not the ones captured."""
+    s = 6
+    mod = DiffusionCrossAttTransformer().eval()
+    init_params_(mod, seed=43, std=0.05, perturb_layer_norm=True)
+    info, qmask, kmask = windows(s, 9)
+    g = torch.Generator().manual_seed(44)
+    act = torch.randn(s, NQ, C, generator=g)
+    qsc = torch.randn(s, NQ, C, generator=g)
+    pair_cond = torch.randn(s, NQ, NK, 16, generator=g)
+    mod = mod.to(DEV)
+    with torch.inference_mode():
+        qsc_d = qsc.to(DEV)
+        ksc_d = atom_layout.convert(info, qsc_d, layout_axes=(-3, -2))
+        args = (qmask.to(DEV), info, kmask.to(DEV))
+        step = mod.capture(act.to(DEV), *args, qsc_d, ksc_d, pair_cond.to(DEV))
+        for k in range(2):
+            a2 = torch.randn(s, NQ, C, generator=g).to(DEV)
+            q2 = torch.randn(s, NQ, C, generator=g).to(DEV)
+            k2 = atom_layout.convert(info, q2, layout_axes=(-3, -2))
+            got = step(a2, q2, k2).clone()
+            want = a2.clone()
+            mod(want, *args, q2, k2, pair_cond.to(DEV))
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), k

@@ -239,3 +239,23 @@ def test_bounded_wait_reports_timeout():
     # the context is still usable afterwards
     x = torch.ones(4, device=DEV)
     assert float(x.sum()) == 4.0
+
+
+@pytest.mark.parametrize("m,k,chunks,chunk,sig_mode", [
+    (200, 128, 6, 128, 1),   # atom rows: AdaLN (scale, shift) pairs
+    (768, 384, 4, 768, 2),   # token rows: AdaLNZero gates
+    (37, 128, 3, 128, 0),
+])
+def test_conditioning(m, k, chunks, chunk, sig_mode):
+    """act(x W^T + b) in the chunked [n / chunk, m, chunk] layout."""
+    g = _g(50 + sig_mode)
+    n = chunks * chunk
+    x = torch.randn(m, k, generator=g).bfloat16()
+    w = _w(g, n, k, std=0.1).bfloat16()
+    b = torch.randn(n, generator=g)
+    ref = (x.float() @ w.float().T + b).reshape(m, chunks, chunk).permute(1, 0, 2)
+    sig = torch.tensor([sig_mode == 2 or (sig_mode == 1 and q % 2 == 0) for q in range(chunks)])
+    ref = torch.where(sig[:, None, None], torch.sigmoid(ref), ref)
+    got = native.conditioning(x.to(DEV), w.to(DEV), b.to(DEV), chunk, sig_mode)
+    assert got.shape == (chunks, m, chunk)
+    assert oracle.relative_error(got.float().cpu(), ref) < TOL

@@ -1723,21 +1723,21 @@ XFB_API int xfb_conditioning(const void* x, int64_t m, int64_t k, const void* we
                              void* stream) {
   XFB_REQUIRE(m >= 0 && k > 0 && n >= 0, "conditioning expects m, n >= 0 and k > 0");
   XFB_REQUIRE(k % 8 == 0, "conditioning input width must be a multiple of 8");
-  XFB_REQUIRE(chunk > 0 && chunk % 16 == 0 && n % chunk == 0,
-              "conditioning chunks must be multiples of 16 columns that divide n");
+  XFB_REQUIRE(chunk > 0 && chunk % 64 == 0 && n % chunk == 0,
+              "conditioning chunks must be multiples of 64 columns that divide n");
   XFB_REQUIRE(sig_mode >= 0 && sig_mode <= 2, "sig_mode must be 0, 1 or 2");
-  XFB_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out),
+  XFB_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out) &&
+                  (bias == nullptr || aligned16(bias)),
               "conditioning buffers must be 16-byte aligned");
   XFB_REQUIRE(m * n < (1ll << 40) && m < (1 << 30) && n < (1 << 30), "conditioning too large");
   if (m == 0 || n == 0) return XFB_OK;
-  xfb::EpiCond<256> epi;
-  epi.out = static_cast<bf16*>(out);
+  xfb::EpiCondTma<128> epi;
+  XFB_TRY(make_out_map(&epi.out_map, out, false, chunk, m, n / chunk, chunk, m * chunk));
   epi.bias = bias;
-  epi.M = static_cast<int>(m);
-  epi.N = static_cast<int>(n);
+  epi.accumulate = 0;
   epi.chunk = static_cast<int>(chunk);
   epi.sig_mode = sig_mode;
-  return run_gemm<256, false, false>(x, k, 0, weight, k, 0, m, n, k, 1, epi,
+  return run_gemm<128, false, false>(x, k, 0, weight, k, 0, m, n, k, 1, epi,
                                      static_cast<cudaStream_t>(stream));
 }
 
@@ -1860,15 +1860,19 @@ XFB_API int xfb_cross_attention(
   {
     XFB_TRY(set_smem(xfb::window_attention_kernel, xfb::WinSmem::kLaunchBytes));
     xfb::WindowAttnArgs a;
+    const uint64_t kv_dims[2] = {static_cast<uint64_t>(2 * c), static_cast<uint64_t>(mk)};
+    const uint64_t kv_strides[1] = {static_cast<uint64_t>(2 * c * sizeof(bf16))};
+    const uint32_t kv_box[2] = {64u, static_cast<uint32_t>(nk)};
+    XFB_TRY(make_map_nd(&a.kv_map, false, 2, w.kv, kv_dims, kv_strides, kv_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
     a.qg = w.qg;
-    a.kv = w.kv;
     a.bias = static_cast<const bf16*>(pair_logits);
     a.mask_q = mask_q;
     a.mask_k = mask_k;
     a.out = w.o;
     a.q_scale = 1.f / std::sqrt(static_cast<float>(c / heads));
-    xfb::window_attention_kernel<<<static_cast<unsigned>(subsets), 128, xfb::WinSmem::kLaunchBytes,
-                                   st>>>(a);
+    xfb::window_attention_kernel<<<static_cast<unsigned>(subsets), xfb::kWinThreads,
+                                   xfb::WinSmem::kLaunchBytes, st>>>(a);
     XFB_LAUNCHED();
   }
   return linear_core(w.o, mq, c, c, static_cast<const bf16*>(wo), c, nullptr,

@@ -803,37 +803,55 @@ struct EpiAttProjDirect {
 // output columns are cut into chunks of `chunk` columns stored one after
 // another, [N / chunk][M][chunk], so each block's tensor is contiguous; act is
 // the logistic function on every chunk (sig_mode 2), on the even chunks
-// (sig_mode 1: [scale, shift] pairs) or nowhere (0).  Direct 16-byte stores.
+// (sig_mode 1: [scale, shift] pairs) or nowhere (0).  The tile is staged like
+// EpiOut's (64-column 128B-swizzled boxes) and each box goes out with one TMA
+// store at (column within its chunk, m0, chunk): `chunk` is a multiple of 64 so
+// no box straddles two chunks, and out_map is the 3-D view {chunk, M, N/chunk}.
 template <int BN>
-struct EpiCond {
-  static constexpr int kStagingBytes = 0;
-  static constexpr int kStagingBufs = 1;
-  static constexpr int kAuxBytes = 0;
-  __nv_bfloat16* out;
-  const float* bias;
-  int M, N, chunk, sig_mode;
-
-  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
-  __device__ void store(const EpiCtx&) const {}
+struct EpiCondTma : EpiOut<BN, false> {
+  static constexpr int kStagingBufs = 2;
+  int chunk, sig_mode;
 
   __device__ void compute(const EpiCtx& c) const {
     constexpr int kHalf = BN / 2;
-    const int row = c.m0 + c.row;
 #pragma unroll 1
     for (int c0 = 0; c0 < kHalf; c0 += 16) {
+      const int col = c.half * kHalf + c0;
       float v[16];
-      tmem_ld16(c.tmem + c.half * kHalf + c0, v);
-      const int col = c.n0 + c.half * kHalf + c0;
-      if (row >= M || col >= N) continue;  // N and chunk are multiples of 16
-      const int q = col / chunk;
+      tmem_ld16(c.tmem + col, v);
+      const int q = (c.n0 + col) / chunk;
       const bool sig = sig_mode == 2 || (sig_mode == 1 && (q & 1) == 0);
+      float bb[16];
+      if (this->bias != nullptr) {  // 16-byte aligned (checked by the launcher)
+        const float4* b4 = reinterpret_cast<const float4*>(this->bias + c.n0 + col);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float x = bf16r(v[i] + (bias ? bias[col + i] : 0.f));
-        v[i] = sig ? sigmoidf_stable(x) : x;
+        for (int k = 0; k < 4; ++k) {
+          const float4 w = __ldg(b4 + k);
+          bb[4 * k] = w.x;
+          bb[4 * k + 1] = w.y;
+          bb[4 * k + 2] = w.z;
+          bb[4 * k + 3] = w.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) bb[i] = 0.f;
       }
-      __nv_bfloat16* dst = out + (static_cast<int64_t>(q) * M + row) * chunk + (col - q * chunk);
-      store16_bf16(dst, v);
+      if (sig) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = sigmoid_ex2(bf16r(v[i] + bb[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = bf16r(v[i] + bb[i]);
+      }
+      this->write(c, col, v);
+    }
+  }
+
+  __device__ void store(const EpiCtx& c) const {
+#pragma unroll
+    for (int b = 0; b < BN / 64; ++b) {
+      const int n = c.n0 + b * 64;
+      tma_store_3d(&this->out_map, c.staging + b * (128 * 128), n % chunk, c.m0, n / chunk);
     }
   }
 };

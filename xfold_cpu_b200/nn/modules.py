@@ -615,6 +615,9 @@ class DiffusionCrossAttTransformer(nn.Module):
                    keys_single_cond, logits):
         """The blocks of forward() with the pair logits and the key gather given."""
         cond = self.conditioning(queries_single_cond, keys_single_cond)
+        # f32 masks once for all blocks (the kernels read 0 = masked)
+        queries_mask = queries_mask.to(torch.float32).contiguous()
+        keys_mask = keys_mask.to(torch.float32).contiguous()
         for i in range(self.num_blocks):
             self.cross_attention[i].accumulate_(queries_act, keys, queries_mask, keys_mask,
                                                 logits[i], queries_single_cond, keys_single_cond,
@@ -630,6 +633,53 @@ class DiffusionCrossAttTransformer(nn.Module):
         keys = self.key_gather(queries_to_keys, s * nq, queries_act.device)
         return self.run_blocks(queries_act, queries_mask, keys, keys_mask, queries_single_cond,
                                keys_single_cond, self.pair_logits(pair_cond))
+
+    def capture(self, queries_act, queries_mask, queries_to_keys, keys_mask, queries_single_cond,
+                keys_single_cond, pair_cond) -> "CrossAttStepGraph":
+        """Records the transformer's blocks for these shapes, masks, gather and
+        pair conditioning into a CUDA graph (the encoder and the decoder call
+        it at every denoising step, xfold/nn/atom_cross_attention.py:226-234,
+        :408-416); see CrossAttStepGraph."""
+        return CrossAttStepGraph(self, queries_act, queries_mask, queries_to_keys, keys_mask,
+                                 queries_single_cond, keys_single_cond, pair_cond)
+
+
+class CrossAttStepGraph:
+    """A CUDA graph of DiffusionCrossAttTransformer.run_blocks.  __call__(act,
+    queries_single_cond, keys_single_cond) copies the inputs into the graph's
+    buffers, replays it on the current stream and returns the graph's output
+    buffer (overwritten by the next call)."""
+
+    def __init__(self, module: DiffusionCrossAttTransformer, act, queries_mask, queries_to_keys,
+                 keys_mask, queries_single_cond, keys_single_cond, pair_cond) -> None:
+        s, nq, _ = act.shape
+        self.module = module
+        self.logits = module.pair_logits(pair_cond)
+        self.keys = tuple(t.clone() for t in module.key_gather(queries_to_keys, s * nq, act.device))
+        self.act = act.detach().clone()
+        self.qmask = queries_mask.detach().clone()
+        self.kmask = keys_mask.detach().clone()
+        self.qsc = queries_single_cond.detach().clone()
+        self.ksc = keys_single_cond.detach().clone()
+        args = (self.qmask, self.keys, self.kmask, self.qsc, self.ksc, self.logits)
+        work = self.act.clone()
+        side = torch.cuda.Stream(device=self.act.device)
+        side.wait_stream(torch.cuda.current_stream(self.act.device))
+        with torch.cuda.stream(side):
+            module.run_blocks(work, *args)
+        torch.cuda.current_stream(self.act.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self.act.clone()
+            module.run_blocks(self.out, *args)
+
+    def __call__(self, act: torch.Tensor, queries_single_cond: torch.Tensor,
+                 keys_single_cond: torch.Tensor) -> torch.Tensor:
+        self.act.copy_(act)
+        self.qsc.copy_(queries_single_cond)
+        self.ksc.copy_(keys_single_cond)
+        self.graph.replay()
+        return self.out
 
 
 class PairformerBlock(nn.Module):
