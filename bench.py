@@ -438,6 +438,55 @@ def cpu_baseline_atom(threads: int | None = None) -> dict:
                                       "fp32 torch CPU oracle of the reference torch path"}
 
 
+def run_only(args) -> None:
+    """Eager calls of one C5 transformer, for launch lists and captures: the
+    same modules and inputs as the extras of the default run."""
+    import torch
+
+    from xfold_cpu_b200 import _capi, native
+    from xfold_cpu_b200.nn import (DiffusionCrossAttTransformer, DiffusionTransformer,
+                                   atom_layout, init_params_)
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    native.check_device(dev)
+    if args.only == "atom":
+        s = ATOM_SUBSETS
+        mod = DiffusionCrossAttTransformer().eval()
+        init_params_(mod, seed=4)
+        mod = mod.to(dev)
+        info, qmask, kmask = _atom_windows(s, (s * 32) // 20)
+        act, qsc, pair_cond = (t.to(dev) for t in _atom_inputs(s, 4))
+        qmask, kmask = qmask.to(dev), kmask.to(dev)
+    else:
+        n = 768
+        mod = DiffusionTransformer(c_act=n).eval()
+        init_params_(mod, seed=4)
+        mod = mod.to(dev)
+        g = torch.Generator(device=dev).manual_seed(4)
+        act = torch.randn(n, n, device=dev, generator=g)
+        cond = torch.randn(n, 384, device=dev, generator=g)
+        pair_cond = torch.randn(n, n, 128, device=dev, generator=g)
+        mask = torch.ones(n, device=dev)
+    with torch.inference_mode():
+        if args.only == "atom":
+            ksc = atom_layout.convert(info, qsc, layout_axes=(-3, -2))
+            keys = mod.key_gather(info, s * 32, dev)
+            logits = mod.pair_logits(pair_cond)
+            call = lambda w: mod.run_blocks(w, qmask, keys, kmask, qsc, ksc, logits)
+        else:
+            logits = mod.pair_logits(pair_cond)
+            call = lambda w: mod.run_blocks(w, mask, cond, logits)
+        work = act.clone()
+        for _ in range(args.warmup + args.steps):
+            work.copy_(act)
+            call(work)
+        torch.cuda.synchronize(dev)
+    print(json.dumps({"only": args.only, "calls": args.warmup + args.steps,
+                      "device_error": _capi.device_error(clear=True),
+                      "finite": bool(torch.isfinite(work).all())}))
+
+
 def run_cuda(args) -> None:
     import torch
 
@@ -595,8 +644,13 @@ def main() -> None:
                     help="N_token (1024 for the metric; smaller only for profiling)")
     ap.add_argument("--skip-extras", action="store_true",
                     help="profiling mode: no e2e pass, kernel roofline or CPU baseline")
+    ap.add_argument("--only", choices=("atom", "diffusion"), default=None,
+                    help="run only the C5 atom or token transformer: --warmup + --steps eager "
+                         "calls, one JSON line (a profiling target)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_cuda(args)
