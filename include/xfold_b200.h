@@ -410,6 +410,47 @@ XFB_API int xfb_cross_attention(
     const void* out_gate, void* out, int out_dtype, int accumulate, void* workspace,
     int64_t workspace_bytes, void* stream);
 
+/* ---- Evoformer MSA stack (xfold/nn/pairformer.py:117-156).  The reference
+ * runs these in torch (einsum); its native extension has no counterpart.
+ *
+ * xfb_msa_attention: MSAAttention.forward (xfold/nn/attention.py:125-144) for
+ * msa [s][n][64] (f32 or bf16), msa_mask [s][n] f32 (null = all ones), pair
+ * [n][n][128]: LayerNorms act_norm (64) and pair_norm (128) with eps,
+ * pair_logits_w [8][128], v_w / gate_w / out_w [64][64] bf16 (nn.Linear
+ * layout), 8 heads of 8.  The [8][n][n] softmax weights over keys (pair
+ * logits + 1e9 (max_s mask - 1)) are shared by all s rows; out [s][n][64] is
+ * the update (accumulate = 0) or added into an f32 msa (accumulate = 1).
+ * n must be a multiple of 8. */
+XFB_API int64_t xfb_msa_attention_workspace(int64_t s, int64_t n);
+XFB_API int xfb_msa_attention(const void* msa, int msa_dtype, int64_t s, int64_t n,
+                              int64_t c_msa, const float* msa_mask, const void* pair,
+                              int pair_dtype, int64_t c_pair, int64_t heads,
+                              const float* act_norm_w, const float* act_norm_b,
+                              const float* pair_norm_w, const float* pair_norm_b, double eps,
+                              const void* pair_logits_w, const void* v_w, const void* gate_w,
+                              const void* out_w, void* out, int out_dtype, int accumulate,
+                              void* workspace, int64_t workspace_bytes, void* stream);
+
+/* xfb_outer_product_mean: OuterProductMean.forward (xfold/nn/primitives.py:62-75)
+ * for msa [s][n][64], mask [s][n] f32: LayerNorm (norm_w, norm_b, eps),
+ * left_w / right_w [32][64] bf16, output_w packed by
+ * xfb_pack_outer_product_weight (from the [32][32][c_out] parameter), output_b
+ * [c_out] f32, c_out = 128.  out [n][n][128] f32 receives the update
+ * (accumulate = 0) or has it added (accumulate = 1, the caller's
+ * pair += ...).  The outer products are formed one chunk of rows at a time
+ * (64 MiB of workspace per chunk). */
+XFB_API int64_t xfb_pack_outer_product_weight_bytes(int64_t c_out);
+XFB_API int xfb_pack_outer_product_weight(const void* output_w, int w_dtype, int64_t c_out,
+                                          void* packed, void* stream);
+XFB_API int64_t xfb_outer_product_mean_workspace(int64_t s, int64_t n);
+XFB_API int xfb_outer_product_mean(const void* msa, int msa_dtype, int64_t s, int64_t n,
+                                   int64_t c_msa, const float* mask, const float* norm_w,
+                                   const float* norm_b, double eps, const void* left_w,
+                                   const void* right_w, const void* packed_output_w,
+                                   const float* output_b, int64_t c_out, void* out,
+                                   int accumulate, void* workspace, int64_t workspace_bytes,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -277,6 +277,41 @@ def diffusion_cross_att_transformer(queries_act, queries_mask, gather_idxs, gath
     return act
 
 
+def msa_attention(msa, msa_mask, pair, params, num_head=8, prefix=""):
+    """MSAAttention.forward (xfold/nn/attention.py:125-144): softmax over keys
+    of the pair logits plus 1e9 (max over sequences of msa_mask - 1), shared by
+    every MSA row; per-head weighted average of v, sigmoid gate, output
+    projection."""
+    P = lambda n: _p(params, prefix, n)
+    x = layer_norm(msa, P("act_norm.weight"), P("act_norm.bias"))
+    p = layer_norm(pair, P("pair_norm.weight"), P("pair_norm.bias"))
+    logits = linear(p, P("pair_logits.weight")).permute(2, 0, 1)
+    logits = logits + 1e9 * (torch.max(msa_mask, dim=0).values - 1.0)
+    weights = torch.softmax(logits, dim=-1)
+    v = linear(x, P("v_projection.weight"))
+    v = v.reshape(v.shape[:-1] + (num_head, -1))
+    o = torch.einsum("hqk,bkhc->bqhc", weights, v)
+    o = o.reshape(o.shape[:-2] + (-1,))
+    o = o * torch.sigmoid(linear(x, P("gating_query.weight")))
+    return linear(o, P("output_projection.weight"))
+
+
+def outer_product_mean(msa, mask, params, prefix=""):
+    """OuterProductMean.forward (xfold/nn/primitives.py:62-75): the masked left /
+    right projections' outer product summed over sequences, contracted with
+    output_w [c, e, f] plus output_b, divided by (1e-3 + the mask overlap
+    count); returns the [N, N, f] pair update."""
+    P = lambda n: _p(params, prefix, n)
+    m = mask.unsqueeze(-1)
+    x = layer_norm(msa, P("layer_norm_input.weight"), P("layer_norm_input.bias"))
+    left = m * linear(x, P("left_projection.weight"))
+    right = m * linear(x, P("right_projection.weight"))
+    act = torch.einsum("aic,aje->icje", left, right)
+    act = torch.einsum("icje,cef->ijf", act, P("output_w")) + P("output_b")
+    norm = torch.einsum("ai,aj->ij", mask, mask)[..., None]
+    return act / (1e-3 + norm)
+
+
 def pairformer_block(pair, pair_mask, single, seq_mask, params, n_heads=16, n_heads_pair=4,
                      with_single=True, prefix=""):
     """PairformerBlock.forward (xfold/nn/pairformer.py:77-114): five in-place
@@ -300,6 +335,34 @@ def pairformer_block(pair, pair_mask, single, seq_mask, params, n_heads=16, n_he
                              prefix + "single_attention_.")
     single += transition(single, params, prefix + "single_transition.")
     return pair, single
+
+
+def evoformer_block(msa, pair, msa_mask, pair_mask, params, n_heads_pair=4, prefix=""):
+    """EvoformerBlock.forward (xfold/nn/pairformer.py:138-156): the outer
+    product mean into pair, MSA attention and transition into msa, then the
+    pair stack.  Returns new (msa, pair) tensors."""
+    msa, pair = msa.clone(), pair.clone()
+    pair += outer_product_mean(msa, msa_mask, params, prefix + "outer_product_mean.")
+    msa += msa_attention(msa, msa_mask, pair, params, 8, prefix + "msa_attention1.")
+    msa += transition(msa, params, prefix + "msa_transition.")
+    pair = pairformer_block(pair, pair_mask, None, None, params, n_heads_pair=n_heads_pair,
+                            with_single=False, prefix=prefix)
+    return msa, pair
+
+
+def evoformer_block_flops(s, n, c_msa=64, c_pair=128, heads_pair=4):
+    """Algorithmic FLOPs of one Evoformer block: outer product mean (both
+    contractions and the projections), MSA attention, MSA transition, and the
+    pair stack of a Pairformer block."""
+    sn = s * n
+    opm = 2 * sn * c_msa * 64 + 2 * s * (32 * n) ** 2 + 2 * n * n * 1024 * c_pair
+    msa_att = (2 * sn * c_msa * 128 + 2 * n * n * c_pair * 8 + 2 * 8 * n * n * s * 8
+               + 2 * sn * 64 * 64)
+    msa_tr = 2 * sn * c_msa * (8 * c_msa) + 2 * sn * (4 * c_msa) * c_msa
+    f = pairformer_block_flops(n, c_pair, 384, heads_pair, 16)
+    pair_stack = f["triangle_multiplication"] + f["triangle_attention"] + f["pair_transition"]
+    return {"outer_product_mean": opm, "msa_attention": msa_att, "msa_transition": msa_tr,
+            "pair": pair_stack, "total": opm + msa_att + msa_tr + pair_stack}
 
 
 # --------------------------------------------------------------------------- FLOP counts

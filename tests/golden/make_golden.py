@@ -225,6 +225,50 @@ def main() -> None:
            "queries_single_cond": qsc, "keys_single_cond": ksc, "pair_cond": pair_cond},
           {"queries_act": fp32, "bf16:queries_act": bf16})
 
+    # --- MSA stack (Evoformer): MSAAttention at its own widths, a token masked in
+    # every sequence (the key mask), OuterProductMean, and a whole EvoformerBlock
+    # with c_pair = 16
+    from xfold.nn.attention import MSAAttention
+    from xfold.nn.pairformer import EvoformerBlock
+    from xfold.nn.primitives import OuterProductMean
+
+    s_, n_ = 5, 6
+    mod = MSAAttention(c_msa=64, c_pair=128, num_head=8).eval()
+    _init(mod, 90)
+    msa = torch.randn(s_, n_, 64, generator=g)
+    msa_mask = (torch.rand(s_, n_, generator=g) > 0.25).float()
+    msa_mask[:, 2] = 0.0
+    pair = torch.randn(n_, n_, 128, generator=g)
+    fp32, bf16 = _both(lambda: mod(msa, msa_mask, pair))
+    _save("msa_attention", mod, {"msa": msa, "msa_mask": msa_mask, "pair": pair},
+          {"update": fp32, "bf16:update": bf16})
+
+    mod = OuterProductMean(c_msa=64, num_output_channel=16).eval()
+    _init(mod, 91)
+    with torch.no_grad():  # output_w / output_b are plain Parameters: small values
+        mod.output_w.mul_(0.1)
+        mod.output_b.mul_(0.1)
+    msa = torch.randn(s_, n_, 64, generator=g)
+    fp32, bf16 = _both(lambda: mod(msa, msa_mask))
+    _save("outer_product_mean", mod, {"msa": msa, "mask": msa_mask},
+          {"update": fp32, "bf16:update": bf16})
+
+    mod = EvoformerBlock(c_msa=64, c_pair=16, n_heads_pair=4).eval()
+    _init(mod, 92, std=0.1)
+    with torch.no_grad():
+        mod.outer_product_mean.output_w.mul_(0.1)
+    msa = torch.randn(s_, n_, 64, generator=g)
+    pair = torch.randn(n_, n_, 16, generator=g)
+    _, pmask = masks(n_, 1)
+
+    def evo():
+        m, p = msa.clone(), pair.clone()
+        return mod(m, p, msa_mask, pmask)
+
+    (m32, p32), (m16, p16) = _both(evo)
+    _save("evoformer_block", mod, {"msa": msa, "pair": pair, "msa_mask": msa_mask, "pair_mask": pmask},
+          {"msa": m32, "pair": p32, "bf16:msa": m16, "bf16:pair": p16})
+
 
 if __name__ == "__main__":
     ONLY.update(sys.argv[1:])

@@ -155,3 +155,45 @@ def test_cross_att_transformer_gather_is_pinned():
     rows = i["queries_act"].shape[0] * i["queries_act"].shape[1]
     wrong = _cross_transformer(p, i, (i["gather_idxs"].long() + 1) % rows)
     assert oracle.relative_error(wrong, o["queries_act"]) > 1e-3
+
+
+def test_msa_attention():
+    p, i, o = load("msa_attention")
+    got = oracle.msa_attention(i["msa"], i["msa_mask"], i["pair"], p, 8)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_msa_attention_key_mask_is_pinned():
+    """Planted mistake: without the key mask (token 2 is masked in every
+    sequence) the fixture catches the difference."""
+    p, i, o = load("msa_attention")
+    wrong = oracle.msa_attention(i["msa"], torch.ones_like(i["msa_mask"]), i["pair"], p, 8)
+    assert oracle.relative_error(wrong, o["update"]) > 1e-2
+
+
+def test_outer_product_mean():
+    p, i, o = load("outer_product_mean")
+    got = oracle.outer_product_mean(i["msa"], i["mask"], p)
+    check(got, o["update"], FP32_TOL)
+    check(o["bf16:update"], got, BF16_TOL)
+
+
+def test_outer_product_mean_orientation_is_pinned():
+    """Planted mistake: swapping the left and right projections transposes the
+    outer product (i <-> j) and must be caught."""
+    p, i, o = load("outer_product_mean")
+    q = dict(p)
+    q["left_projection.weight"], q["right_projection.weight"] = (p["right_projection.weight"],
+                                                                 p["left_projection.weight"])
+    wrong = oracle.outer_product_mean(i["msa"], i["mask"], q)
+    assert oracle.relative_error(wrong, o["update"]) > 1e-2
+
+
+def test_evoformer_block():
+    p, i, o = load("evoformer_block")
+    msa, pair = oracle.evoformer_block(i["msa"], i["pair"], i["msa_mask"], i["pair_mask"], p)
+    check(msa, o["msa"], 1e-5)
+    check(pair, o["pair"], 1e-5)
+    check(o["bf16:msa"] - i["msa"], msa - i["msa"], BF16_TOL)
+    check(o["bf16:pair"] - i["pair"], pair - i["pair"], BF16_TOL)

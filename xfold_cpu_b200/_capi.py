@@ -98,6 +98,14 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_cross_pair_logits": (_i, [_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _d, _p,
                                    _p, _p]),
     "xfb_cross_attention_workspace": (_i64, [_i64]),
+    "xfb_msa_attention_workspace": (_i64, [_i64, _i64]),
+    "xfb_pack_outer_product_weight_bytes": (_i64, [_i64]),
+    "xfb_pack_outer_product_weight": (_i, [_p, _i, _i64, _p, _p]),
+    "xfb_outer_product_mean_workspace": (_i64, [_i64, _i64]),
+    "xfb_outer_product_mean": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _d, _p, _p, _p, _p,
+                                    _i64, _p, _i, _p, _i64, _p]),
+    "xfb_msa_attention": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _i64, _p, _p, _p, _p,
+                               _d, _p, _p, _p, _p, _p, _i, _i, _p, _i64, _p]),
     "xfb_cross_attention": (_i, [_p, _i, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p,
                                  _p, _d, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _p, _i64,
                                  _p]),

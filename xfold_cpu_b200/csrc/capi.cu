@@ -19,6 +19,7 @@
 #include "gemm.cuh"
 #include "layer_norm.cuh"
 #include "window_attention.cuh"
+#include "msa.cuh"
 
 #ifndef XFB_NVCC_FLAGS
 #define XFB_NVCC_FLAGS "unknown"
@@ -296,7 +297,7 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
                    const bf16* mod_scale, const bf16* mod_shift, const bf16* wh, int heads,
                    bf16* head_out, int64_t head_ld, cudaStream_t st, float head_scale = 1.f,
                    const int64_t* gather_idx = nullptr, const uint8_t* gather_valid = nullptr,
-                   int64_t src_rows = 0) {
+                   int64_t src_rows = 0, int64_t perm_outer = 0, int64_t perm_inner = 0) {
   if (rows <= 0) return XFB_OK;
   XFB_REQUIRE(x_dtype == XFB_F32 || x_dtype == XFB_BF16, "LayerNorm input must be f32 or bf16");
   XFB_REQUIRE(heads >= 0 && heads <= 16, "head projection supports at most 16 heads");
@@ -320,7 +321,11 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
   a.gather_idx = gather_idx;
   a.gather_valid = gather_valid;
   a.src_rows = src_rows;
+  a.perm_outer = perm_outer;
+  a.perm_inner = perm_inner;
   XFB_REQUIRE(gather_idx == nullptr || heads == 0, "row gather excludes the head projection");
+  XFB_REQUIRE(perm_outer == 0 || (heads == 0 && perm_inner > 0 && perm_outer * perm_inner == rows),
+              "row permutation must cover the rows and excludes the head projection");
   int sms;
   XFB_TRY(sm_count(&sms));
   if (c == 128 && heads > 0 && mod_scale == nullptr && mod_shift == nullptr && ldx % 4 == 0 &&
@@ -1878,6 +1883,249 @@ XFB_API int xfb_cross_attention(
   return linear_core(w.o, mq, c, c, static_cast<const bf16*>(wo), c, nullptr,
                      static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32, accumulate,
                      c, st);
+}
+
+// ---------------------------------------------------------------- MSA attention
+
+namespace {
+struct MsaWs {
+  bf16 *x, *vt, *gt, *logits, *weights, *ot, *o, *wvg;
+  float* kmask;
+};
+void msa_layout(Carver& cv, int64_t s, int64_t n, MsaWs* w) {
+  const int64_t rows = s * n;
+  w->x = cv.take<bf16>(rows * 64);
+  w->vt = cv.take<bf16>(rows * 64);
+  w->gt = cv.take<bf16>(rows * 64);
+  w->logits = cv.take<bf16>(8 * n * n);
+  w->weights = cv.take<bf16>(8 * n * n);
+  w->ot = cv.take<bf16>(rows * 64);
+  w->o = cv.take<bf16>(rows * 64);
+  w->wvg = cv.take<bf16>(128 * 64);
+  w->kmask = cv.take<float>(n);
+}
+}  // namespace
+
+XFB_API int64_t xfb_msa_attention_workspace(int64_t s, int64_t n) {
+  if (s <= 0 || n <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  MsaWs w;
+  msa_layout(cv, s, n, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_msa_attention(const void* msa, int msa_dtype, int64_t s, int64_t n,
+                              int64_t c_msa, const float* msa_mask, const void* pair,
+                              int pair_dtype, int64_t c_pair, int64_t heads,
+                              const float* act_norm_w, const float* act_norm_b,
+                              const float* pair_norm_w, const float* pair_norm_b, double eps,
+                              const void* pair_logits_w, const void* v_w, const void* gate_w,
+                              const void* out_w, void* out, int out_dtype, int accumulate,
+                              void* workspace, int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(msa_dtype == XFB_F32 || msa_dtype == XFB_BF16, "msa must be f32 or bf16");
+  XFB_REQUIRE(pair_dtype == XFB_F32 || pair_dtype == XFB_BF16, "pair must be f32 or bf16");
+  XFB_REQUIRE(s >= 0 && n >= 0, "sizes must be non-negative");
+  XFB_REQUIRE(c_msa == 64 && heads == 8 && c_pair == 128,
+              "MSA attention takes c_msa = 64, 8 heads of 8, c_pair = 128");
+  XFB_REQUIRE(n % 8 == 0, "the token count must be a multiple of 8");
+  XFB_REQUIRE(out_dtype == XFB_F32 || out_dtype == XFB_BF16, "output must be f32 or bf16");
+  XFB_REQUIRE(!accumulate || out_dtype == XFB_F32, "accumulate requires an f32 output");
+  XFB_REQUIRE(pair_logits_w && v_w && gate_w && out_w, "MSA attention weights missing");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(aligned16(msa) && aligned16(pair) && aligned16(out) && aligned16(v_w) &&
+                  aligned16(gate_w) && aligned16(out_w),
+              "MSA attention buffers must be 16-byte aligned");
+  if (s == 0 || n == 0) return XFB_OK;
+  XFB_REQUIRE(s * n < (1ll << 31) - 256 && n <= 16384, "MSA too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  MsaWs w;
+  msa_layout(cv, s, n, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t rows = s * n;
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  // normalised MSA, rows reordered (token, sequence)
+  XFB_TRY(run_layer_norm(msa, msa_dtype, rows, 64, 64, act_norm_w, act_norm_b, eps, w.x, 64,
+                         nullptr, nullptr, nullptr, 0, nullptr, 0, st, 1.f, nullptr, nullptr, 0,
+                         s, n));
+  // v | gate projection, head-major outputs
+  XFB_CUDA(cudaMemcpyAsync(w.wvg, v_w, 64 * 64 * sizeof(bf16), cudaMemcpyDeviceToDevice, st));
+  XFB_CUDA(cudaMemcpyAsync(w.wvg + 64 * 64, gate_w, 64 * 64 * sizeof(bf16),
+                           cudaMemcpyDeviceToDevice, st));
+  {
+    xfb::EpiMsaVG epi;
+    epi.vt = w.vt;
+    epi.gt = w.gt;
+    epi.M = rows;
+    XFB_TRY((run_gemm<128, false, false>(w.x, 64, 0, w.wvg, 64, 0, rows, 128, 64, 1, epi, st)));
+  }
+  // pair logits [8][n][n] (LayerNorm of the pair and the head projection)
+  XFB_TRY(run_layer_norm(pair, pair_dtype, n * n, 128, 128, pair_norm_w, pair_norm_b, eps,
+                         nullptr, 0, nullptr, nullptr, static_cast<const bf16*>(pair_logits_w), 8,
+                         w.logits, n * n, st));
+  // key mask and the shared softmax weights
+  const float* kmask = nullptr;
+  if (msa_mask != nullptr) {
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, sms * 4));
+    xfb::msa_key_mask_kernel<<<grid, 256, 0, st>>>(msa_mask, s, n, w.kmask);
+    XFB_LAUNCHED();
+    kmask = w.kmask;
+  }
+  {
+    const int grid = static_cast<int>(std::min<int64_t>((8 * n + 7) / 8, sms * 8));
+    xfb::msa_softmax_kernel<<<grid, 256, 0, st>>>(w.logits, kmask, 8 * n, n, w.weights);
+    XFB_LAUNCHED();
+  }
+  // weighted average per head: ot[h] = (weights[h] @ vt[h]) * gt[h], [n][s*8]
+  {
+    xfb::EpiOutGated<128, false> epi;
+    XFB_TRY(make_out_map(&epi.out_map, w.ot, false, s * 8, n, 8, s * 8, n * s * 8));
+    const uint64_t dims[3] = {static_cast<uint64_t>(s * 8), static_cast<uint64_t>(n), 8};
+    const uint64_t strides[2] = {static_cast<uint64_t>(s * 16), static_cast<uint64_t>(n * s * 16)};
+    const uint32_t box[3] = {64, 128, 1};
+    XFB_TRY(make_map_nd(&epi.gate_map, false, 3, w.gt, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
+    epi.bias = nullptr;
+    epi.accumulate = 0;
+    XFB_TRY((run_gemm<128, false, true>(w.weights, n, n * n, w.vt, s * 8, n * s * 8, n, s * 8, n,
+                                        8, epi, st)));
+  }
+  {
+    const int grid = static_cast<int>(std::min<int64_t>((rows + 255) / 256, sms * 8));
+    xfb::msa_merge_heads_kernel<<<grid, 256, 0, st>>>(w.ot, s, n, w.o);
+    XFB_LAUNCHED();
+  }
+  return linear_core(w.o, rows, 64, 64, static_cast<const bf16*>(out_w), 64, nullptr, nullptr, 0,
+                     out, out_dtype == XFB_F32, accumulate, 64, st);
+}
+
+// ---------------------------------------------------------------- OuterProductMean
+
+namespace {
+constexpr int64_t kOpmChunkBytes = 64ll << 20;  // outer products of one chunk of rows i
+
+int64_t opm_chunk_rows(int64_t n) {
+  const int64_t r = kOpmChunkBytes / (n * 1024 * 2);
+  return std::max<int64_t>(1, std::min<int64_t>(n, r));
+}
+
+struct OpmWs {
+  bf16 *x, *wlr, *left, *right, *maskb, *outer;
+  float* norm;
+};
+void opm_layout(Carver& cv, int64_t s, int64_t n, OpmWs* w) {
+  const int64_t rows = s * n;
+  w->x = cv.take<bf16>(rows * 64);
+  w->wlr = cv.take<bf16>(64 * 64);
+  w->left = cv.take<bf16>(rows * 32);
+  w->right = cv.take<bf16>(rows * 32);
+  w->maskb = cv.take<bf16>(rows);
+  w->norm = cv.take<float>(n * n);
+  w->outer = cv.take<bf16>(opm_chunk_rows(n) * n * 1024);
+}
+}  // namespace
+
+XFB_API int64_t xfb_pack_outer_product_weight_bytes(int64_t c_out) { return c_out * 1024 * 2; }
+
+XFB_API int xfb_pack_outer_product_weight(const void* output_w, int w_dtype, int64_t c_out,
+                                          void* packed, void* stream) {
+  XFB_REQUIRE(w_dtype == XFB_F32 || w_dtype == XFB_BF16, "output_w must be f32 or bf16");
+  XFB_REQUIRE(c_out > 0 && output_w != nullptr && packed != nullptr, "bad outer-product weight");
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int grid = static_cast<int>(std::min<int64_t>((c_out * 1024 + 255) / 256, sms * 8));
+  xfb::pack_opm_weight_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      output_w, w_dtype == XFB_F32, c_out, static_cast<bf16*>(packed));
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+XFB_API int64_t xfb_outer_product_mean_workspace(int64_t s, int64_t n) {
+  if (s <= 0 || n <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  OpmWs w;
+  opm_layout(cv, s, n, &w);
+  return cv.used;
+}
+
+XFB_API int xfb_outer_product_mean(const void* msa, int msa_dtype, int64_t s, int64_t n,
+                                   int64_t c_msa, const float* mask, const float* norm_w,
+                                   const float* norm_b, double eps, const void* left_w,
+                                   const void* right_w, const void* packed_output_w,
+                                   const float* output_b, int64_t c_out, void* out,
+                                   int accumulate, void* workspace, int64_t workspace_bytes,
+                                   void* stream) {
+  XFB_REQUIRE(msa_dtype == XFB_F32 || msa_dtype == XFB_BF16, "msa must be f32 or bf16");
+  XFB_REQUIRE(s >= 0 && n >= 0, "sizes must be non-negative");
+  XFB_REQUIRE(c_msa == 64 && c_out == 128, "outer product mean takes c_msa = 64, 32 outer "
+                                           "channels and 128 outputs");
+  XFB_REQUIRE(n % 8 == 0, "the token count must be a multiple of 8");
+  XFB_REQUIRE(mask != nullptr && left_w && right_w && packed_output_w && output_b,
+              "outer product mean needs the mask and every weight");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  XFB_REQUIRE(aligned16(msa) && aligned16(out) && aligned16(packed_output_w) &&
+                  aligned16(left_w) && aligned16(right_w),
+              "outer product mean buffers must be 16-byte aligned");
+  if (s == 0 || n == 0) return XFB_OK;
+  XFB_REQUIRE(s * n < (1ll << 31) - 256 && n * 32 < (1 << 30), "MSA too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  OpmWs w;
+  opm_layout(cv, s, n, &w);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t rows = s * n;
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  XFB_TRY(run_layer_norm(msa, msa_dtype, rows, 64, 64, norm_w, norm_b, eps, w.x, 64, nullptr,
+                         nullptr, nullptr, 0, nullptr, 0, st));
+  XFB_CUDA(cudaMemcpyAsync(w.wlr, left_w, 32 * 64 * sizeof(bf16), cudaMemcpyDeviceToDevice, st));
+  XFB_CUDA(cudaMemcpyAsync(w.wlr + 32 * 64, right_w, 32 * 64 * sizeof(bf16),
+                           cudaMemcpyDeviceToDevice, st));
+  {
+    xfb::EpiOpmLR epi;
+    epi.left = w.left;
+    epi.right = w.right;
+    epi.mask = mask;
+    epi.M = rows;
+    XFB_TRY((run_gemm<128, false, false>(w.x, 64, 0, w.wlr, 64, 0, rows, 64, 64, 1, epi, st)));
+  }
+  // overlap counts norm[i][j] = sum_a mask[a][i] mask[a][j] (exact in f32)
+  {
+    const int grid = static_cast<int>(std::min<int64_t>((rows + 255) / 256, sms * 8));
+    xfb::f32_to_bf16_kernel<<<grid, 256, 0, st>>>(mask, rows, w.maskb);
+    XFB_LAUNCHED();
+    xfb::EpiOut<128, true> epi;
+    XFB_TRY(make_out_map(&epi.out_map, w.norm, true, n, n, 1, n, 0));
+    epi.bias = nullptr;
+    epi.accumulate = 0;
+    XFB_TRY((run_gemm<128, true, true>(w.maskb, n, 0, w.maskb, n, 0, n, n, s, 1, epi, st)));
+  }
+  const int64_t chunk = opm_chunk_rows(n);
+  for (int64_t i0 = 0; i0 < n; i0 += chunk) {
+    const int64_t ci = std::min(chunk, n - i0);
+    {
+      xfb::EpiOpmOuter epi;
+      epi.outer = w.outer;
+      epi.M = static_cast<int>(ci * 32);
+      epi.N = static_cast<int>(n);
+      XFB_TRY((run_gemm<256, true, true>(w.left + i0 * 32, n * 32, 0, w.right, n * 32, 0, ci * 32,
+                                         n * 32, s, 1, epi, st)));
+    }
+    {
+      xfb::EpiOpmOut epi;
+      float* dst = static_cast<float*>(out) + i0 * n * c_out;
+      XFB_TRY(make_out_map(&epi.out_map, dst, true, c_out, ci * n, 1, c_out, 0));
+      epi.bias = output_b;
+      epi.accumulate = accumulate;
+      epi.norm = w.norm + i0 * n;
+      epi.eps = 1e-3f;
+      epi.M = static_cast<int>(ci * n);
+      XFB_TRY((run_gemm<128, false, false>(w.outer, 1024, 0, packed_output_w, 1024, 0, ci * n,
+                                           c_out, 1024, 1, epi, st)));
+    }
+  }
+  return XFB_OK;
 }
 
 XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,

@@ -63,6 +63,7 @@ struct LnArgs {
   const int64_t* gather_idx;       // [rows] source row of each output row, or null
   const uint8_t* gather_valid;     // [rows] zero = the output row reads zeros; or null
   int64_t src_rows;                // rows of x that gather_idx may address
+  int64_t perm_outer, perm_inner;  // > 0: input row b*inner + k writes y row k*outer + b
 };
 
 // C = 32 * 4 * R channels: each lane holds R groups of 4 consecutive channels.
@@ -166,7 +167,9 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
       for (int e = 0; e < V; ++e) v[r][e] = bf16r(v[r][e]);
 
     if (a.y != nullptr) {
-      __nv_bfloat16* yr = a.y + row * a.ldy;
+      const int64_t yrow =
+          a.perm_outer > 0 ? (row % a.perm_inner) * a.perm_outer + row / a.perm_inner : row;
+      __nv_bfloat16* yr = a.y + yrow * a.ldy;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int ch = r * 32 * V + lane * V;

@@ -632,3 +632,71 @@ def cross_attention(x_q: torch.Tensor, keys, mask_q: torch.Tensor | None,
                _ptr(wo), _ptr(out_gate), _ptr(out), _code(out), 1 if accumulate else 0, _ptr(ws),
                ws.numel(), _stream(device))
     return out
+
+
+# ----------------------------------------------------------------------------- MSA stack
+
+def msa_attention(msa: torch.Tensor, msa_mask: torch.Tensor | None, pair: torch.Tensor,
+                  act_norm_w: torch.Tensor | None, act_norm_b: torch.Tensor | None,
+                  pair_norm_w: torch.Tensor | None, pair_norm_b: torch.Tensor | None, eps: float,
+                  pair_logits_w: torch.Tensor, v_w: torch.Tensor, gate_w: torch.Tensor,
+                  out_w: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False,
+                  out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """MSAAttention update (xfold/nn/attention.py:125-144): msa [S, N, 64],
+    msa_mask [S, N], pair [N, N, 128]; 8 heads of 8."""
+    device = _check_cuda(msa, pair, msa_mask, pair_logits_w, v_w, gate_w, out_w)
+    if msa.dim() != 3 or pair.dim() != 3:
+        raise ValueError("msa must be [S, N, c_msa] and pair [N, N, c_pair]")
+    s, n, c = msa.shape
+    msa, pair = _contig(msa), _contig(pair)
+    if msa_mask is not None:
+        msa_mask = _contig(msa_mask.expand(s, n), torch.float32)
+    if out is None:
+        out = torch.empty((s, n, c), dtype=out_dtype, device=device)
+    f32 = [_contig(t, torch.float32) for t in (act_norm_w, act_norm_b, pair_norm_w, pair_norm_b)]
+    ws_w = [prepare_weight(t) for t in (pair_logits_w, v_w, gate_w, out_w)]
+    ws = _workspace(_capi.load().xfb_msa_attention_workspace(s, n), device)
+    _capi.call("xfb_msa_attention", _ptr(msa), _code(msa), s, n, c, _ptr(msa_mask), _ptr(pair),
+               _code(pair), pair.shape[-1], pair_logits_w.shape[0], *(_ptr(t) for t in f32),
+               float(eps), *(_ptr(t) for t in ws_w), _ptr(out), _code(out),
+               1 if accumulate else 0, _ptr(ws), ws.numel(), _stream(device))
+    return out
+
+
+def pack_outer_product_weight(output_w: torch.Tensor) -> torch.Tensor:
+    """output_w [32, 32, f] -> [f, 1024] bf16 (the second contraction's operand)."""
+    device = _check_cuda(output_w)
+    if output_w.dim() != 3 or output_w.shape[:2] != (32, 32):
+        raise ValueError("output_w must be [32, 32, f]")
+    w = _contig(output_w)
+    f = w.shape[2]
+    packed = torch.empty((f, 1024), dtype=torch.bfloat16, device=device)
+    _capi.call("xfb_pack_outer_product_weight", _ptr(w), _code(w), f, _ptr(packed), _stream(device))
+    return packed
+
+
+def outer_product_mean(msa: torch.Tensor, mask: torch.Tensor, norm_w: torch.Tensor | None,
+                       norm_b: torch.Tensor | None, eps: float, left_w: torch.Tensor,
+                       right_w: torch.Tensor, packed_output_w: torch.Tensor,
+                       output_b: torch.Tensor, out: torch.Tensor | None = None,
+                       accumulate: bool = False) -> torch.Tensor:
+    """OuterProductMean update (xfold/nn/primitives.py:62-75): msa [S, N, 64],
+    mask [S, N] -> [N, N, 128] f32."""
+    device = _check_cuda(msa, mask, left_w, right_w, packed_output_w, output_b)
+    if msa.dim() != 3:
+        raise ValueError("msa must be [S, N, c_msa]")
+    s, n, c = msa.shape
+    msa = _contig(msa)
+    mask = _contig(mask.expand(s, n), torch.float32)
+    c_out = packed_output_w.shape[0]
+    if out is None:
+        out = torch.empty((n, n, c_out), dtype=torch.float32, device=device)
+    elif out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("outer product mean writes a contiguous f32 [N, N, c] tensor")
+    nw, nb, ob = (_contig(t, torch.float32) for t in (norm_w, norm_b, output_b))
+    lw, rw = prepare_weight(left_w), prepare_weight(right_w)
+    ws = _workspace(_capi.load().xfb_outer_product_mean_workspace(s, n), device)
+    _capi.call("xfb_outer_product_mean", _ptr(msa), _code(msa), s, n, c, _ptr(mask), _ptr(nw),
+               _ptr(nb), float(eps), _ptr(lw), _ptr(rw), _ptr(packed_output_w), _ptr(ob), c_out,
+               _ptr(out), 1 if accumulate else 0, _ptr(ws), ws.numel(), _stream(device))
+    return out

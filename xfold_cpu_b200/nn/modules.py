@@ -14,6 +14,9 @@ stream in place through the fused epilogue (the `x += op(x)` of the callers).
   DiffusionTransition      xfold/nn/diffusion_transformer.py:98-128
   SelfAttention            xfold/nn/diffusion_transformer.py:131-217
   DiffusionTransformer     xfold/nn/diffusion_transformer.py:220-272
+  MSAAttention             xfold/nn/attention.py:108-144
+  OuterProductMean         xfold/nn/primitives.py:40-75
+  EvoformerBlock           xfold/nn/pairformer.py:117-156
   CrossAttention           xfold/nn/diffusion_transformer.py:275-350
   DiffusionCrossAttTransformer  xfold/nn/diffusion_transformer.py:353-411
   PairformerBlock          xfold/nn/pairformer.py:26-114
@@ -680,6 +683,108 @@ class CrossAttStepGraph:
         self.ksc.copy_(keys_single_cond)
         self.graph.replay()
         return self.out
+
+
+class MSAAttention(nn.Module):
+    def __init__(self, c_msa: int = 64, c_pair: int = 128, num_head: int = 8) -> None:
+        super().__init__()
+        self.c_msa = c_msa
+        self.c_pair = c_pair
+        self.num_head = num_head
+        self.value_dim = c_msa // num_head
+        self.act_norm = LayerNorm(c_msa)
+        self.pair_norm = LayerNorm(c_pair)
+        self.pair_logits = nn.Linear(c_pair, num_head, bias=False)
+        self.v_projection = nn.Linear(c_msa, num_head * self.value_dim, bias=False)
+        self.gating_query = nn.Linear(c_msa, c_msa, bias=False)
+        self.output_projection = nn.Linear(c_msa, c_msa, bias=False)
+        self._w = [WeightCache() for _ in range(4)]
+
+    def _run(self, msa, msa_mask, pair, out, accumulate):
+        config.require_cuda("dot_product_attention_implementation")
+        if (self.c_msa, self.c_pair, self.num_head) != (64, 128, 8):
+            raise ValueError("the cuda backend's MSA attention takes c_msa = 64, c_pair = 128, "
+                             "8 heads")
+        w = [_bf16(c, t.weight) for c, t in zip(self._w, (self.pair_logits, self.v_projection,
+                                                           self.gating_query,
+                                                           self.output_projection))]
+        return native.msa_attention(msa, msa_mask, pair, self.act_norm.weight, self.act_norm.bias,
+                                    self.pair_norm.weight, self.pair_norm.bias, self.act_norm.eps,
+                                    *w, out=out, accumulate=accumulate)
+
+    def forward(self, msa: torch.Tensor, msa_mask: torch.Tensor, pair: torch.Tensor) -> torch.Tensor:
+        return self._run(msa, msa_mask, pair, None, False)
+
+    def accumulate_(self, msa, msa_mask, pair):
+        if _fused_target(msa):
+            return self._run(msa, msa_mask, pair, msa, True)
+        msa += self._run(msa, msa_mask, pair, None, False)
+        return msa
+
+
+class OuterProductMean(nn.Module):
+    def __init__(self, c_msa: int = 64, num_output_channel: int = 128,
+                 num_outer_channel: int = 32) -> None:
+        super().__init__()
+        self.c_msa = c_msa
+        self.num_outer_channel = num_outer_channel
+        self.num_output_channel = num_output_channel
+        self.epsilon = 1e-3
+        self.layer_norm_input = LayerNorm(c_msa)
+        self.left_projection = nn.Linear(c_msa, num_outer_channel, bias=False)
+        self.right_projection = nn.Linear(c_msa, num_outer_channel, bias=False)
+        self.output_w = nn.Parameter(torch.randn(num_outer_channel, num_outer_channel,
+                                                 num_output_channel))
+        self.output_b = nn.Parameter(torch.randn(num_output_channel))
+        self._lw, self._rw, self._ow = WeightCache(), WeightCache(), WeightCache()
+
+    def _run(self, msa, mask, out, accumulate):
+        config.require_cuda("triangle_multiplication_implementation")
+        if (self.c_msa, self.num_outer_channel, self.num_output_channel) != (64, 32, 128):
+            raise ValueError("the cuda backend's outer product mean takes c_msa = 64, 32 outer "
+                             "and 128 output channels")
+        ln = self.layer_norm_input
+        return native.outer_product_mean(
+            msa, mask, ln.weight, ln.bias, ln.eps, _bf16(self._lw, self.left_projection.weight),
+            _bf16(self._rw, self.right_projection.weight),
+            self._ow.get((self.output_w,), native.pack_outer_product_weight), self.output_b,
+            out=out, accumulate=accumulate)
+
+    def forward(self, msa: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        return self._run(msa, mask, None, False)
+
+    def accumulate_(self, pair, msa, mask):
+        """pair += forward(msa, mask), added by the kernel into an f32 pair."""
+        if _fused_target(pair):
+            return self._run(msa, mask, pair, True)
+        pair += self._run(msa, mask, None, False)
+        return pair
+
+
+class EvoformerBlock(nn.Module):
+    def __init__(self, c_msa: int = 64, c_pair: int = 128, n_heads_pair: int = 4) -> None:
+        super().__init__()
+        self.outer_product_mean = OuterProductMean(c_msa=c_msa, num_output_channel=c_pair)
+        self.msa_attention1 = MSAAttention(c_msa=c_msa, c_pair=c_pair)
+        self.msa_transition = Transition(c_x=c_msa)
+        self.triangle_multiplication_outgoing = TriangleMultiplication(c_pair=c_pair, _outgoing=True)
+        self.triangle_multiplication_incoming = TriangleMultiplication(c_pair=c_pair, _outgoing=False)
+        self.pair_attention1 = GridSelfAttention(c_pair=c_pair, num_head=n_heads_pair, transpose=False)
+        self.pair_attention2 = GridSelfAttention(c_pair=c_pair, num_head=n_heads_pair, transpose=True)
+        self.pair_transition = Transition(c_x=c_pair)
+
+    def forward(self, msa: torch.Tensor, pair: torch.Tensor, msa_mask: torch.Tensor,
+                pair_mask: torch.Tensor):
+        """Updates msa and pair in place and returns them, as the reference."""
+        self.outer_product_mean.accumulate_(pair, msa, msa_mask)
+        self.msa_attention1.accumulate_(msa, msa_mask, pair)
+        self.msa_transition.accumulate_(msa)
+        self.triangle_multiplication_outgoing.accumulate_(pair, pair_mask)
+        self.triangle_multiplication_incoming.accumulate_(pair, pair_mask)
+        self.pair_attention1.accumulate_(pair, pair_mask)
+        self.pair_attention2.accumulate_(pair, pair_mask)
+        self.pair_transition.accumulate_(pair)
+        return msa, pair
 
 
 class PairformerBlock(nn.Module):
