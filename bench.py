@@ -407,6 +407,110 @@ def _atom_c5(dev, steps: int) -> dict:
     return out
 
 
+EVO_N, EVO_S = 1024, 1024  # the reference's MSA stack: num_msa = 1024 at N_token = 1024
+
+
+def _evo_inputs(n: int, s: int, seed: int):
+    """Synthetic MSA-stack inputs: msa ~ N(0,1) [s, n, 64], pair ~ N(0,1)
+    [n, n, 128]; the last 5 % of tokens are padding (masked in every sequence
+    and in the pair mask) and 10 % of the other MSA entries are gaps."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    msa = torch.randn(s, n, 64, generator=g)
+    pair = torch.randn(n, n, 128, generator=g)
+    tail = max(1, n // 20)
+    msa_mask = (torch.rand(s, n, generator=g) > 0.1).float()
+    msa_mask[0] = 1.0
+    msa_mask[:, n - tail:] = 0.0
+    seq = torch.ones(n)
+    seq[n - tail:] = 0.0
+    return msa, pair, msa_mask, seq[:, None] * seq[None, :]
+
+
+def _evoformer(dev, steps: int) -> dict:
+    """One Evoformer block of the reference's MSA stack (N_token = 1024,
+    num_msa = 1024, c_msa = 64, c_pair = 128, random init N(0, 0.02), seed 5),
+    timed eager per block, with a per-operator split from one more pass."""
+    import torch
+
+    from xfold_cpu_b200 import _capi
+    from xfold_cpu_b200.nn import EvoformerBlock, init_params_
+
+    n, s = EVO_N, EVO_S
+    with torch.inference_mode(False):
+        blk = EvoformerBlock().eval()
+        init_params_(blk, seed=5)
+        blk = blk.to(dev)
+    msa_h, pair_h, mask_h, pmask_h = _evo_inputs(n, s, 5)
+    msa, pair = msa_h.to(dev), pair_h.to(dev)
+    mask, pmask = mask_h.to(dev), pmask_h.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {"n_token": n, "num_msa": s, "c_msa": 64, "c_pair": 128,
+           "data": "synthetic, random init, 5 % padded tokens, 10 % MSA gaps"}
+    with torch.inference_mode():
+        for _ in range(2):
+            blk(msa, pair, mask, pmask)
+        torch.cuda.synchronize(dev)
+        l0 = _capi.launch_count()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = max(steps, 3)
+        e0.record(stream)
+        for _ in range(reps):
+            blk(msa, pair, mask, pmask)
+        e1.record(stream)
+        e1.synchronize()
+        out["ms_per_block"] = round(e0.elapsed_time(e1) / reps, 3)
+        out["kernel_launches_per_block"] = int((_capi.launch_count() - l0) // reps)
+        parts = [("outer_product_mean", lambda: blk.outer_product_mean.accumulate_(pair, msa, mask)),
+                 ("msa_attention", lambda: blk.msa_attention1.accumulate_(msa, mask, pair)),
+                 ("msa_transition", lambda: blk.msa_transition.accumulate_(msa))]
+        for name, fn in parts:
+            fn()
+            torch.cuda.synchronize(dev)
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(reps):
+                fn()
+            a1.record(stream)
+            a1.synchronize()
+            out[f"{name}_ms"] = round(a0.elapsed_time(a1) / reps, 3)
+        if _capi.device_error(clear=True):
+            raise RuntimeError("a device wait expired in the Evoformer timing")
+    opm_flops = 2 * s * (32 * n) ** 2 + 2 * n * n * 1024 * 128
+    out["outer_product_mean_tflops"] = round(opm_flops / (out["outer_product_mean_ms"] * 1e-3) / 1e12, 1)
+    return out
+
+
+def cpu_baseline_evoformer(sample: int = 128, threads: int | None = None) -> dict:
+    """The CPU oracle of one Evoformer block at N = num_msa = `sample`,
+    float32, scaled to N = num_msa = 1024 by the FLOP ratio."""
+    import torch
+
+    import oracle
+    from xfold_cpu_b200.nn import EvoformerBlock, init_params_
+
+    if threads:
+        torch.set_num_threads(threads)
+    blk = EvoformerBlock()
+    init_params_(blk, seed=5)
+    params = {k: v.detach().clone() for k, v in blk.state_dict().items()}
+    msa, pair, mask, pmask = _evo_inputs(sample, sample, 5)
+    with torch.inference_mode():
+        oracle.evoformer_block(msa, pair, mask, pmask, params)  # warm-up
+        t0 = time.perf_counter()
+        oracle.evoformer_block(msa, pair, mask, pmask, params)
+        dt = time.perf_counter() - t0
+    scale = (oracle.evoformer_block_flops(EVO_S, EVO_N)["total"]
+             / oracle.evoformer_block_flops(sample, sample)["total"])
+    return {"value": round(dt * scale * 1e3, 1), "unit": "ms/block", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": (f"1 Evoformer block at N = num_msa = {sample} fp32 (torch CPU "
+                                       f"oracle of the reference torch path), {dt:.2f} s, scaled "
+                                       f"x{scale:.1f} by FLOPs to {EVO_N}")}
+
+
 def cpu_baseline_atom(threads: int | None = None) -> dict:
     """The CPU oracle (the reference's torch path restated, float32) of one
     C5 atom-transformer call at full size, on the host's cores."""
@@ -450,6 +554,21 @@ def run_only(args) -> None:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     native.check_device(dev)
+    if args.only == "evoformer":
+        from xfold_cpu_b200.nn import EvoformerBlock
+
+        blk = EvoformerBlock().eval()
+        init_params_(blk, seed=5)
+        blk = blk.to(dev)
+        msa, pair, mask, pmask = (t.to(dev) for t in _evo_inputs(EVO_N, EVO_S, 5))
+        with torch.inference_mode():
+            for _ in range(args.warmup + args.steps):
+                blk(msa, pair, mask, pmask)
+            torch.cuda.synchronize(dev)
+        print(json.dumps({"only": args.only, "calls": args.warmup + args.steps,
+                          "device_error": _capi.device_error(clear=True),
+                          "finite": bool(torch.isfinite(pair).all() and torch.isfinite(msa).all())}))
+        return
     if args.only == "atom":
         s = ATOM_SUBSETS
         mod = DiffusionCrossAttTransformer().eval()
@@ -589,12 +708,15 @@ def run_cuda(args) -> None:
         roof = _kernel_roofline(dev, args.steps, peaks) if rank == 0 else {}
         c5 = _diffusion_c5(dev, args.steps) if rank == 0 and world == 1 else None
         atom = _atom_c5(dev, args.steps) if rank == 0 and world == 1 else None
+        evo = _evoformer(dev, args.steps) if rank == 0 and world == 1 else None
 
     if rank != 0:
         return
     base = cpu_baseline(sample_n=256) if world == 1 else None
     if atom is not None:
         atom["cpu_port"] = cpu_baseline_atom()
+    if evo is not None:
+        evo["cpu_port"] = cpu_baseline_evoformer()
     dominant = max(roof.values(), key=lambda r: r["ms_per_launch"]) if roof else None
     line = {
         "metric": METRIC, "value": round(step_ms / n_blocks, 4), "unit": UNIT, "n_gpus": world,
@@ -627,7 +749,8 @@ def run_cuda(args) -> None:
         "clocks": clocks,
         "cpu_baseline": base,
         "finite": finite,
-        "extras": {"diffusion_transformer_c5": c5, "atom_transformer_c5": atom} if c5 else None,
+        "extras": ({"diffusion_transformer_c5": c5, "atom_transformer_c5": atom,
+                    "evoformer_block": evo} if c5 else None),
     }
     print(json.dumps(line), flush=True)
 
@@ -644,7 +767,7 @@ def main() -> None:
                     help="N_token (1024 for the metric; smaller only for profiling)")
     ap.add_argument("--skip-extras", action="store_true",
                     help="profiling mode: no e2e pass, kernel roofline or CPU baseline")
-    ap.add_argument("--only", choices=("atom", "diffusion"), default=None,
+    ap.add_argument("--only", choices=("atom", "diffusion", "evoformer"), default=None,
                     help="run only the C5 atom or token transformer: --warmup + --steps eager "
                          "calls, one JSON line (a profiling target)")
     args = ap.parse_args()

@@ -340,6 +340,18 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
     XFB_LAUNCHED();
     return XFB_OK;
   }
+  if (c == 64 && heads == 0 && ldx % 8 == 0 && (y == nullptr || ldy % 8 == 0) &&
+      aligned16(mod_scale) && aligned16(mod_shift)) {
+    // four rows per warp
+    const int blocks = static_cast<int>(std::min<int64_t>((rows + 31) / 32, int64_t(sms) * 16));
+    if (x_dtype == XFB_F32) {
+      xfb::ln_rows64_kernel<float><<<blocks, 256, 0, st>>>(a);
+    } else {
+      xfb::ln_rows64_kernel<bf16><<<blocks, 256, 0, st>>>(a);
+    }
+    XFB_LAUNCHED();
+    return XFB_OK;
+  }
   const int64_t warps = (rows + 0);
   const int blocks = static_cast<int>(std::min<int64_t>((warps + 7) / 8, int64_t(sms) * 16));
   const dim3 block(256);
@@ -1967,8 +1979,8 @@ XFB_API int xfb_msa_attention(const void* msa, int msa_dtype, int64_t s, int64_t
   // key mask and the shared softmax weights
   const float* kmask = nullptr;
   if (msa_mask != nullptr) {
-    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, sms * 4));
-    xfb::msa_key_mask_kernel<<<grid, 256, 0, st>>>(msa_mask, s, n, w.kmask);
+    xfb::msa_key_mask_kernel<<<static_cast<unsigned>((n + 31) / 32), 1024, 0, st>>>(msa_mask, s, n,
+                                                                                  w.kmask);
     XFB_LAUNCHED();
     kmask = w.kmask;
   }

@@ -344,6 +344,16 @@ __device__ __forceinline__ float bf16r(float x) {  // round-trip through bf16 (R
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// Eight bf16 (one 16-byte vector) to f32.
+__device__ __forceinline__ void unpack8_bf16(const uint4 w, float* v) {
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(ww[i] << 16);
+    v[2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u);
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -358,15 +358,6 @@ __device__ __forceinline__ void store16_bf16(__nv_bfloat16* dst, const float (&v
   reinterpret_cast<uint4*>(dst)[1] = b;
 }
 
-__device__ __forceinline__ void unpack8_bf16(const uint4 w, float* v) {
-  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = __uint_as_float(ww[i] << 16);
-    v[2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u);
-  }
-}
-
 // Address of 16-byte chunk `chunk` (0..7) of row `row` in a [rows][128 B] tile
 // written / read by TMA with the 128-byte swizzle (base 1024-byte aligned).
 __device__ __forceinline__ uint8_t* sw128_chunk(uint8_t* base, int row, int chunk) {

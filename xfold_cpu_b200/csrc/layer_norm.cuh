@@ -222,6 +222,89 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
   }
 }
 
+// LayerNorm of 64-wide rows without a head projection: four rows per warp at a
+// time (8 lanes per row, 8 channels per lane), so a warp keeps four rows'
+// loads in flight; statistics by 3-step shuffles within the 8 lanes.  Same
+// arithmetic and options (gather, modulation, output-row permutation) as
+// ln_rows_kernel.
+template <typename InT>
+__global__ void __launch_bounds__(256) ln_rows64_kernel(LnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 7;   // channels 8*sub .. 8*sub+7
+  const int grp = lane >> 3;  // which of the warp's four rows
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  float wv[8], bv[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    wv[e] = a.w ? a.w[sub * 8 + e] : 1.f;
+    bv[e] = a.b ? a.b[sub * 8 + e] : 0.f;
+  }
+  for (int64_t row0 = warp_id * 4; row0 < a.rows; row0 += warps_total * 4) {
+    const int64_t row = row0 + grp;
+    const bool live = row < a.rows;
+    int64_t src = row;
+    bool zero = !live;
+    if (live && a.gather_idx != nullptr) {
+      src = a.gather_idx[row];
+      zero = a.gather_valid != nullptr && a.gather_valid[row] == 0;
+      if (!zero && (src < 0 || src >= a.src_rows)) {
+        if (sub == 0) record_error(kErrIndex);
+        zero = true;
+      }
+    }
+    float v[8];
+    if (zero) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    } else {
+      const InT* xr = reinterpret_cast<const InT*>(a.x) + src * a.ldx + sub * 8;
+      float q[4];
+      load_vec4<InT>(xr, q);
+      v[0] = q[0], v[1] = q[1], v[2] = q[2], v[3] = q[3];
+      load_vec4<InT>(xr + 4, q);
+      v[4] = q[0], v[5] = q[1], v[6] = q[2], v[7] = q[3];
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += v[e];
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s * (1.f / 64);
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += (v[e] - mean) * (v[e] - mean);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rstd = rsqrtf(ss * (1.f / 64) + a.eps);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = (v[e] - mean) * rstd * wv[e] + bv[e];
+    if (!live) continue;
+    if (a.mod_scale != nullptr) {
+      float sc[8], sh[8];
+      unpack8_bf16(*reinterpret_cast<const uint4*>(a.mod_scale + row * 64 + sub * 8), sc);
+      if (a.mod_shift) {
+        unpack8_bf16(*reinterpret_cast<const uint4*>(a.mod_shift + row * 64 + sub * 8), sh);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sh[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = sc[e] * v[e] + sh[e];
+    }
+    if (a.y != nullptr) {
+      const int64_t yrow =
+          a.perm_outer > 0 ? (row % a.perm_inner) * a.perm_outer + row / a.perm_inner : row;
+      uint4 w;
+      w.x = pack_bf16x2(v[0], v[1]);
+      w.y = pack_bf16x2(v[2], v[3]);
+      w.z = pack_bf16x2(v[4], v[5]);
+      w.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(a.y + yrow * a.ldy + sub * 8) = w;
+    }
+  }
+}
+
 // Channel-major LayerNorm: x(ch, i, j) = in[ch*chan_stride + i*pitch + j].
 // ln_heads_tc_kernel: LayerNorm of 128-wide rows plus a projection onto up to
 // 16 heads (the attention pair bias, the single track's pair logits) on the

@@ -57,13 +57,24 @@ struct EpiMsaVG {
 };
 
 // kmask[k] = max over sequences s of mask[s][k] (the reference's
-// torch.max(msa_mask, dim=0)); one thread per token, coalesced along k.
-__global__ void msa_key_mask_kernel(const float* mask, int64_t s, int64_t n, float* kmask) {
-  for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
-       k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float m = -INFINITY;
-    for (int64_t r = 0; r < s; ++r) m = fmaxf(m, mask[r * n + k]);
-    kmask[k] = s > 0 ? m : 0.f;
+// torch.max(msa_mask, dim=0)).  A block of 1024 threads takes 32 tokens: lane
+// = token (a warp reads 128 contiguous bytes of a row), warp = one of 32 row
+// groups, then a shared-memory reduction over the groups.
+__global__ void __launch_bounds__(1024) msa_key_mask_kernel(const float* mask, int64_t s,
+                                                            int64_t n, float* kmask) {
+  __shared__ float part[32][33];
+  const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int64_t k = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  float m = -INFINITY;
+  if (k < n) {
+    for (int64_t r = grp; r < s; r += 32) m = fmaxf(m, mask[r * n + k]);
+  }
+  part[grp][lane] = m;
+  __syncthreads();
+  if (grp == 0) {
+#pragma unroll 8
+    for (int g = 1; g < 32; ++g) m = fmaxf(m, part[g][lane]);
+    if (k < n) kmask[k] = s > 0 ? m : 0.f;
   }
 }
 

@@ -1,7 +1,8 @@
 """Deterministic random initialisation used by the benchmarks and tests.
 
 The reference's benchmark configs use random-init weights: every Linear
-weight and bias ~ N(0, std) with std = 0.02, LayerNorm gamma = 1, beta = 0.
+weight and bias, and the other plain parameters (OuterProductMean's output_w
+and output_b), ~ N(0, std) with std = 0.02; LayerNorm gamma = 1, beta = 0.
 `perturb_layer_norm` draws gamma ~ 1 + 0.1 N(0,1), beta ~ 0.1 N(0,1) instead,
 so tests exercise the affine path.  Parameters are drawn on the CPU from one
 torch.Generator in named_parameters() order (reproducible on any machine).
@@ -12,6 +13,8 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
+from ..fastnn import LayerNorm
+
 
 @torch.no_grad()
 def init_params_(module: nn.Module, seed: int = 0, std: float = 0.02,
@@ -20,7 +23,7 @@ def init_params_(module: nn.Module, seed: int = 0, std: float = 0.02,
     for name, p in module.named_parameters():
         leaf = name.rsplit(".", 1)[-1]
         owner = module.get_submodule(name.rsplit(".", 1)[0]) if "." in name else module
-        is_norm = not isinstance(owner, nn.Linear)
+        is_norm = isinstance(owner, (LayerNorm, nn.LayerNorm))
         if is_norm:
             if perturb_layer_norm:
                 v = torch.randn(p.shape, generator=g) * 0.1
