@@ -115,6 +115,33 @@ def test_dot_product_attention(B, H, nq, nk, d, mask_kind, bias_kind):
     assert _rel(got, ref) < TOL
 
 
+@pytest.mark.parametrize("B,H,n,d", [(50, 4, 200, 32), (49, 8, 136, 16), (48, 4, 64, 32)])
+def test_dot_product_attention_three_slot_kernel(B, H, n, d):
+    """Shapes with >= 48 batch rows and one shared bias run on the three-slot
+    kernel: a batch not divisible by 3, ragged query / key tiles, a fully
+    masked row and tail-masked rows.  Checked against the oracle and against
+    the one-tile kernel (the same rows two at a time)."""
+    g = _g(9)
+    q = torch.randn(B, H, n, d, generator=g) * 0.5
+    k = torch.randn(B, H, n, d, generator=g) * 0.5
+    v = torch.randn(B, H, n, d, generator=g)
+    bias = torch.randn(H, n, n, generator=g)
+    mask = torch.ones(B, n)
+    mask[:, -max(1, n // 10):] = 0
+    mask[3] = 0  # every key of row 3 masked: a uniform average
+    mask[7, : n // 2] = 0
+    rb = lambda t: t.bfloat16().float()
+    ref = oracle.dot_product_attention(rb(q), rb(k), rb(v), mask, rb(bias)[None])
+    dq, dk, dv, dm = q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV)
+    db = bias.to(DEV).bfloat16()
+    got = native.dot_product_attention(dq, dk, dv, dm, db)
+    assert _rel(got, ref) < TOL
+    one_tile = torch.cat([native.dot_product_attention(dq[i:i + 2], dk[i:i + 2], dv[i:i + 2],
+                                                       dm[i:i + 2], db)
+                          for i in range(0, B, 2)])
+    assert _rel(got, one_tile.float().cpu()) < 8e-3  # two bf16 ulps of the largest output
+
+
 def _tri_params(g, c):
     lw, lb = _ln(g, c)
     cw, cb = _ln(g, c)

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -14,6 +15,7 @@
 
 #include "../../include/xfold_b200.h"
 #include "attention.cuh"
+#include "tri_attention.cuh"
 #include "exchange.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
@@ -517,6 +519,42 @@ int launch_flash(const bf16* q, const bf16* k, const bf16* v, xfb::AttnArgs args
   return XFB_OK;
 }
 
+// Three-query-tile triangle attention (tri_attention.cuh): head dim <= 32, one
+// TMA-streamed bias shared by all batch rows.
+template <bool PRE>
+int launch_flash_tri(const bf16* q, const bf16* k, const bf16* v, xfb::AttnArgs args,
+                     cudaStream_t st) {
+  CUtensorMap tq, tk, tv, tb;
+  const CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_64B;
+  const int64_t bh = static_cast<int64_t>(args.B) * args.H;
+  XFB_TRY(make_map(&tq, q, 32, args.nq, bh, 64, int64_t(args.nq) * 64, 32, 128, swz));
+  XFB_TRY(make_map(&tk, k, 32, args.nk, bh, 64, int64_t(args.nk) * 64, 32, xfb::kAttnBK, swz));
+  XFB_TRY(make_map(&tv, v, 32, args.nk, bh, 64, int64_t(args.nk) * 64, 32, xfb::kAttnBK, swz));
+  XFB_TRY(make_map(&tb, args.bias, args.nk, args.nq, args.H, args.bias_sq * 2, args.bias_sh * 2,
+                   xfb::kAttnBK, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+  args.q_tiles = (args.nq + 127) / 128;
+  auto kernel = xfb::flash_tri_kernel<PRE>;
+  XFB_TRY(set_smem(kernel, xfb::TriSmem::kLaunchBytes));
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int64_t groups = static_cast<int64_t>((args.B + xfb::kTriSlots - 1) / xfb::kTriSlots) *
+                         args.H * args.q_tiles;
+  const int grid = static_cast<int>(std::min<int64_t>(groups, sms));
+  kernel<<<grid, xfb::kTriThreads, xfb::TriSmem::kLaunchBytes, st>>>(tq, tk, tv, tb, args);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+// The three-slot kernel pays off once there are enough batch rows to fill the
+// slots; XFB_FLASH_TRI=0 selects the one-tile kernel for every shape.
+bool use_flash_tri(const xfb::AttnArgs& args) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("XFB_FLASH_TRI");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return enabled && args.bias != nullptr && !args.bias_batched && args.B >= 48;
+}
+
 // Picks the bias path: TMA-streamed bf16 tiles when the layout allows it
 // (row stride nk with nk % 8 == 0, contiguous heads, 16-byte aligned), else
 // per-thread global loads.  `pre`: q and the bias already carry log2(e)
@@ -537,9 +575,12 @@ int run_flash(int dp, int bias_dtype, bool pre, const bf16* q, const bf16* k, co
   }
   if (pre) {
     XFB_REQUIRE(mode == xfb::kBiasTma && dp == 32, "pre-scaled attention needs the TMA bias path");
+    if (use_flash_tri(args)) return launch_flash_tri<true>(q, k, v, args, st);
     return launch_flash<32, xfb::kBiasTma, true>(q, k, v, args, st);
   }
   if (dp == 32) {
+    if (mode == xfb::kBiasTma && use_flash_tri(args))
+      return launch_flash_tri<false>(q, k, v, args, st);
     if (mode == xfb::kBiasTma) return launch_flash<32, xfb::kBiasTma, false>(q, k, v, args, st);
     if (mode == xfb::kBiasGlobalF32)
       return launch_flash<32, xfb::kBiasGlobalF32, false>(q, k, v, args, st);

@@ -1,0 +1,471 @@
+// Triangle attention (head dim <= 32, one bias shared by every batch row) on
+// tcgen05 with three query tiles in flight per SM.
+//
+// The exponentials, not the MMAs, bound this attention: one score costs 4 d =
+// 128 MMA FLOP but one ex2 on the MUFU unit (16 per clock per SM).  The
+// one-tile-per-CTA kernel in attention.cuh keeps two softmax warps per SM
+// sub-partition busy and leaves the MUFU unit idle half of the time while
+// those warps wait on TMEM loads, stores and barriers.  This kernel runs one
+// persistent CTA per SM with three softmax warpgroups, each owning its own
+// query tile ("slot"), so three softmax warps share each sub-partition and
+// cover each other's latencies.
+//
+// Work group = (head h, 128-query tile qt, batch rows 3j, 3j+1, 3j+2): slot s
+// handles batch row 3j+s.  The bias tile bias[h, qt-rows, key-tile] is the
+// same for the three rows, so it is loaded once per key tile and read by all
+// three slots' S MMAs.  Per 64-key tile of a slot:
+//   S   = bias + Q K^T   four identity MMAs (the bf16 bias enters the f32
+//                        accumulator exactly) then the QK^T MMAs, into one of
+//                        the slot's two 64-column S buffers
+//   P   = 2^(S - m_ref)  softmax warps, one query row per thread; P (bf16
+//                        pairs) is written back over the first 32 columns of
+//                        the same S buffer, and the row sum of the f32
+//                        probabilities is kept in registers
+//   O  += P V            tcgen05.mma with A = P from TMEM, V MN-major
+// TMEM: slot s owns columns [160 s, 160 s + 160): S buffers at +0 and +64, O
+// (32 columns) at +128; 480 of the 512 columns.
+//
+// Semantics are those of flash_attn_kernel (attention.cuh): masked keys get
+// the logit -1e9, keys past the end probability 0, a NaN logit poisons its
+// row, and the reference max m_ref moves lazily (only when a tile exceeds it
+// by more than 2^8), rescaling O in TMEM and the row sum in registers.
+#pragma once
+
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace xfb {
+
+constexpr int kTriSlots = 3;
+// warpgroups 0-2: softmax (slot = warpgroup); warpgroup 3: TMA producer (warp
+// 12) and one MMA issuer per slot (warps 13-15; warp 13 owns TMEM).
+constexpr int kTriThreads = 512;
+constexpr int kTriRegsLaunch = 128, kTriRegsSoftmax = 152, kTriRegsOther = 56;
+static_assert(3 * 128 * kTriRegsSoftmax + 128 * kTriRegsOther == kTriThreads * kTriRegsLaunch,
+              "register split must add up to the launch allocation");
+constexpr int kTriKvStages = 3;    // per slot, freed by the slot's PV MMA
+constexpr int kTriBiasStages = 3;  // shared, freed once every slot's S MMA read it
+constexpr int kTriSlotCols = 160;
+
+struct TriSmem {
+  static constexpr int kQBytes = 128 * 32 * 2;       // 8 KB, 64-byte swizzle
+  static constexpr int kKVBytes = kAttnBK * 32 * 2;  // 4 KB
+  static constexpr int kBiasBytes = 128 * kAttnBK * 2;  // 16 KB, 128-byte swizzle
+  static constexpr int kQOff = 0;                                          // [slot][2]
+  static constexpr int kKOff = kQOff + kTriSlots * 2 * kQBytes;            // [slot][stage]
+  static constexpr int kVOff = kKOff + kTriSlots * kTriKvStages * kKVBytes;  // [slot][stage]
+  static constexpr int kBiasOff = kVOff + kTriSlots * kTriKvStages * kKVBytes;
+  static constexpr int kIdentOff = kBiasOff + kTriBiasStages * kBiasBytes;
+  static constexpr int kIdentBytes = 16 * 128;
+  static constexpr int kBarOff = kIdentOff + kIdentBytes;
+  // per slot: q_full[2], q_empty[2], kv_full[S], kv_empty[S], s_full[2],
+  // p_full[2], pv_done[2], o_free;  shared: b_full[SB], b_empty[SB]
+  static constexpr int kSlotBars = 4 + 2 * kTriKvStages + 7;
+  static constexpr int kNumBars = kTriSlots * kSlotBars + 2 * kTriBiasStages;
+  static constexpr int kTotal = kBarOff + kNumBars * 8 + 16;
+  static constexpr int kLaunchBytes = kTotal + 1024;
+  static_assert(kBiasOff % 1024 == 0 && kIdentOff % 1024 == 0, "128-byte swizzle alignment");
+  static_assert(kKOff % 512 == 0 && kVOff % 512 == 0, "64-byte swizzle alignment");
+  static_assert(kLaunchBytes <= 227 * 1024, "shared memory");
+};
+
+struct TriBars {
+  uint64_t* q_full;   // [2]
+  uint64_t* q_empty;  // [2]
+  uint64_t* kv_full;  // [kTriKvStages]
+  uint64_t* kv_empty;
+  uint64_t* s_full;   // [2]
+  uint64_t* p_full;   // [2]
+  uint64_t* pv_done;  // [2]
+  uint64_t* o_free;   // [1]
+};
+
+__device__ __forceinline__ TriBars tri_bars(uint64_t* base, int slot) {
+  uint64_t* p = base + slot * TriSmem::kSlotBars;
+  TriBars b;
+  b.q_full = p;
+  b.q_empty = p + 2;
+  b.kv_full = p + 4;
+  b.kv_empty = p + 4 + kTriKvStages;
+  b.s_full = p + 4 + 2 * kTriKvStages;
+  b.p_full = b.s_full + 2;
+  b.pv_done = b.p_full + 2;
+  b.o_free = b.pv_done + 2;
+  return b;
+}
+
+// Group index -> (head, query tile, first batch row); query tiles fastest so
+// the CTAs running at the same time read the same rows' K / V from L2.
+__device__ __forceinline__ void tri_group(const AttnArgs& a, int gi, int& h, int& qt, int& b0) {
+  qt = gi % a.q_tiles;
+  const int jh = gi / a.q_tiles;
+  h = jh % a.H;
+  b0 = (jh / a.H) * kTriSlots;
+}
+
+template <bool PRE>
+__global__ void __launch_bounds__(kTriThreads, 1)
+    flash_tri_kernel(const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmBias, AttnArgs args) {
+  using L = TriSmem;
+  constexpr uint32_t kIdescS = idesc_bf16(128, kAttnBK, false, false);
+  constexpr uint32_t kIdescO = idesc_bf16(128, 32, false, true);
+  constexpr uint32_t kIdescB = idesc_bf16(128, 16, false, false);  // bias identity MMAs
+  constexpr uint32_t kOCol = 128;  // within a slot
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem + L::kQOff;
+  uint8_t* sK = smem + L::kKOff;
+  uint8_t* sV = smem + L::kVOff;
+  uint8_t* sBias = smem + L::kBiasOff;
+  uint8_t* sIdent = smem + L::kIdentOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* b_full = bars + kTriSlots * L::kSlotBars;
+  uint64_t* b_empty = b_full + kTriBiasStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tiles = (args.nk + kAttnBK - 1) / kAttnBK;
+  const int row_groups = (args.B + kTriSlots - 1) / kTriSlots;
+  const int n_groups = row_groups * args.H * args.q_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTriSlots; ++s) {
+      const TriBars tb = tri_bars(bars, s);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&tb.q_full[i], 1);
+        mbar_init(&tb.q_empty[i], 1);
+        mbar_init(&tb.s_full[i], 1);
+        mbar_init(&tb.p_full[i], 128);
+        mbar_init(&tb.pv_done[i], 1);
+      }
+      for (int i = 0; i < kTriKvStages; ++i) {
+        mbar_init(&tb.kv_full[i], 1);
+        mbar_init(&tb.kv_empty[i], 1);
+      }
+      mbar_init(tb.o_free, 128);
+    }
+    for (int i = 0; i < kTriBiasStages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], kTriSlots);  // one commit per slot
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 13) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp < 4) {
+    // 16 x 16 identity in the 128-byte swizzle (chunk c of row n at c ^ (n % 8))
+    for (int i = threadIdx.x; i < L::kIdentBytes / 16; i += 128) {
+      const int n = i >> 3;
+      const int c = (i & 7) ^ (n & 7);
+      const uint32_t one = (n & 1) ? 0x3F800000u : 0x00003F80u;
+      const int word = c == (n >> 3) ? (n & 7) >> 1 : -1;
+      reinterpret_cast<uint4*>(sIdent)[i] =
+          make_uint4(word == 0 ? one : 0u, word == 1 ? one : 0u, word == 2 ? one : 0u,
+                     word == 3 ? one : 0u);
+    }
+    fence_async_smem();
+  }
+  if (warp == 12 && lane == 0) {
+    tma_prefetch(&tmQ);
+    tma_prefetch(&tmK);
+    tma_prefetch(&tmV);
+    tma_prefetch(&tmBias);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp >= 12) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kTriRegsOther));
+    if (warp == 12 && lane == 0) {
+      // ------------------------------------------------ TMA producer
+      // Per group: the three slots' Q tiles, then per key tile the shared bias
+      // tile and each slot's K / V.  Rows past B (only in the last row group)
+      // read as zeros (TMA fills boxes outside the tensor) and are not stored.
+      int it = 0, g = 0;
+      bool ok = true;
+      for (int gi = blockIdx.x; ok && gi < n_groups; gi += gridDim.x, ++it) {
+        int h, qt, b0;
+        tri_group(args, gi, h, qt, b0);
+        const int qb = it & 1;
+#pragma unroll
+        for (int s = 0; s < kTriSlots; ++s) {
+          const TriBars tb = tri_bars(bars, s);
+          if (!mbar_wait(&tb.q_empty[qb], ((it >> 1) & 1) ^ 1, kErrWaitProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&tb.q_full[qb], L::kQBytes);
+          tma_load_3d(sQ + (s * 2 + qb) * L::kQBytes, &tmQ, &tb.q_full[qb], 0, qt * 128,
+                      (b0 + s) * args.H + h);
+        }
+        for (int t = 0; ok && t < n_tiles; ++t, ++g) {
+          const int sb = g % kTriBiasStages;
+          if (!mbar_wait(&b_empty[sb], ((g / kTriBiasStages) & 1) ^ 1, kErrWaitProducer,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&b_full[sb], L::kBiasBytes);
+          tma_load_3d(sBias + sb * L::kBiasBytes, &tmBias, &b_full[sb], t * kAttnBK, qt * 128, h);
+          const int st = g % kTriKvStages;
+#pragma unroll
+          for (int s = 0; s < kTriSlots; ++s) {
+            const TriBars tb = tri_bars(bars, s);
+            if (!mbar_wait(&tb.kv_empty[st], ((g / kTriKvStages) & 1) ^ 1, kErrWaitProducer,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
+            const int bh = (b0 + s) * args.H + h;
+            mbar_arrive_expect_tx(&tb.kv_full[st], 2 * L::kKVBytes);
+            tma_load_3d(sK + (s * kTriKvStages + st) * L::kKVBytes, &tmK, &tb.kv_full[st], 0,
+                        t * kAttnBK, bh);
+            tma_load_3d(sV + (s * kTriKvStages + st) * L::kKVBytes, &tmV, &tb.kv_full[st], 0,
+                        t * kAttnBK, bh);
+          }
+        }
+      }
+    } else if (warp >= 13 && lane == 0) {
+      // ------------------------------------------------ MMA issuer of one slot
+      // Tile sequence g = item * n_tiles + t (the same for every slot, and the
+      // index of the shared bias tile).  One tile of lookahead:
+      //   S(g + 1) once PV(g - 1), which read P from the same TMEM buffer, is done;
+      //   PV(g)    once the softmax stored P(g).
+      const int s = warp - 13;
+      const TriBars tb = tri_bars(bars, s);
+      const uint32_t slot_tmem = tmem_base + s * kTriSlotCols;
+      const uint64_t ident_desc = sw128_desc(smem_u32(sIdent), 16, 1024);
+      const int my_groups =
+          static_cast<int>(blockIdx.x) < n_groups
+              ? (n_groups - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+              : 0;
+      const int total = my_groups * n_tiles;
+      // issues S(gs); false if a wait gave up
+      auto issue_s = [&](int gs) -> bool {
+        const int it = gs / n_tiles;
+        const int t = gs - it * n_tiles;
+        const int qb = it & 1;
+        const int st = gs % kTriKvStages;
+        const int sb = gs % kTriBiasStages;
+        const int buf = gs & 1;
+        if ((t == 0 && !mbar_wait(&tb.q_full[qb], (it >> 1) & 1, kErrWaitMma, abort_flag)) ||
+            !mbar_wait(&b_full[sb], (gs / kTriBiasStages) & 1, kErrWaitMma, abort_flag) ||
+            !mbar_wait(&tb.kv_full[st], (gs / kTriKvStages) & 1, kErrWaitMma, abort_flag) ||
+            (gs >= 2 &&
+             !mbar_wait(&tb.pv_done[buf], ((gs - 2) >> 1) & 1, kErrWaitMma, abort_flag)))
+          return false;
+        tc_fence_after();
+        const uint32_t d_tmem = slot_tmem + buf * kAttnBK;
+        const uint32_t b_addr = smem_u32(sBias + sb * L::kBiasBytes);
+        const uint32_t q_addr = smem_u32(sQ + (s * 2 + qb) * L::kQBytes);
+        const uint32_t k_addr = smem_u32(sK + (s * kTriKvStages + st) * L::kKVBytes);
+        // S[:, 16j + n] = sum_k bias[:, 16j + k] I[k][n]: exact in the f32 accumulator
+#pragma unroll
+        for (int j = 0; j < kAttnBK / 16; ++j)
+          umma_bf16(d_tmem + 16 * j, p_desc(b_addr, j), ident_desc, kIdescB, 0u);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          umma_bf16(d_tmem, qk_desc<32>(q_addr, k), qk_desc<32>(k_addr, k), kIdescS, 1u);
+        umma_commit(&tb.s_full[buf]);
+        umma_commit(&b_empty[sb]);  // one of the three slots done with this bias tile
+        if (t == n_tiles - 1) umma_commit(&tb.q_empty[qb]);
+        return true;
+      };
+      bool ok = total == 0 || issue_s(0);
+      for (int gp = 0; ok && gp < total; ++gp) {
+        if (gp + 1 < total && !issue_s(gp + 1)) break;
+        const int it = gp / n_tiles;
+        const int t = gp - it * n_tiles;
+        const int st = gp % kTriKvStages;
+        const int buf = gp & 1;
+        // the previous item must have read O before its first PV overwrites it
+        if ((t == 0 && it > 0 && !mbar_wait(tb.o_free, (it - 1) & 1, kErrWaitMma, abort_flag)) ||
+            !mbar_wait(&tb.p_full[buf], (gp >> 1) & 1, kErrWaitMma, abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (s * kTriKvStages + st) * L::kKVBytes);
+        const uint32_t p_tmem = slot_tmem + buf * kAttnBK;  // 8 columns per 16 keys
+#pragma unroll
+        for (int j = 0; j < kAttnBK / 16; ++j)
+          umma_bf16_ts(slot_tmem + kOCol, p_tmem + 8 * j, v_desc<32>(v_addr, j, L::kKVBytes),
+                       kIdescO, (t > 0 || j > 0) ? 1u : 0u);
+        umma_commit(&tb.pv_done[buf]);
+        umma_commit(&tb.kv_empty[st]);  // K (read by S) and V of this tile are done
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTriRegsSoftmax));
+    // ------------------------------------------------ softmax warpgroups
+    const int slot = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const TriBars tb = tri_bars(bars, slot);
+    const uint32_t t_row =
+        tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + slot * kTriSlotCols;
+    const int words = (args.nk + 31) / 32;
+    constexpr float kScale = PRE ? 1.f : kLog2e;
+    constexpr float kMasked = PRE ? -1e9f * kLog2e : -1e9f;
+    const float2 scale2 = make_float2(kScale, kScale);
+    int g = 0;
+    bool ok = true;
+    for (int gi = blockIdx.x; gi < n_groups; gi += gridDim.x) {
+      int h, qt, b0;
+      tri_group(args, gi, h, qt, b0);
+      const int b = b0 + slot;
+      const bool b_ok = b < args.B;  // rows past B (last row group) run on zeros, unstored
+      const int q = qt * 128 + row;
+      const uint32_t* mrow =
+          (args.mask_bits != nullptr && b_ok) ? args.mask_bits + b * args.mask_sb : nullptr;
+      float m_ref = -INFINITY;  // reference max, log2 units
+      float2 lsum[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
+      for (int t = 0; t < n_tiles; ++t, ++g) {
+        const int buf = g & 1;
+        const int key0 = t * kAttnBK;
+        uint32_t w0 = 0xFFFFFFFFu, w1 = 0xFFFFFFFFu;
+        if (mrow != nullptr) {
+          w0 = mrow[2 * t];
+          w1 = (2 * t + 1 < words) ? mrow[2 * t + 1] : 0u;
+        }
+        ok = mbar_wait(&tb.s_full[buf], (g >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
+        tc_fence_after();
+        float s[kAttnBK];
+        tmem_ld32_to(t_row + buf * kAttnBK, s);
+        tmem_ld32_to(t_row + buf * kAttnBK + 32, s + 32);
+        tmem_wait_ld();
+        float2* s2 = reinterpret_cast<float2*>(s);
+        // ---- key mask: masked -> -1e9, past the end -> -inf
+        if (key0 + kAttnBK > args.nk || (w0 & w1) != 0xFFFFFFFFu) {
+#pragma unroll
+          for (int j = 0; j < kAttnBK; ++j) {
+            const uint32_t bit = ((j < 32 ? w0 : w1) >> (j & 31)) & 1u;
+            if (key0 + j >= args.nk) {
+              s[j] = -INFINITY;
+            } else if (!bit) {
+              s[j] = kMasked;
+            }
+          }
+        }
+        // ---- tile max and lazy reference update (a NaN max always "grows")
+        const float mt = tile_max64(s) * kScale;
+        const bool grow = !(mt <= m_ref + 8.f);
+        float factor = 1.f;
+        if (grow) {
+          factor = ex2_approx(m_ref - mt);  // 0 when m_ref = -inf
+          m_ref = mt;
+        }
+        if (t > 0 && __any_sync(0xffffffffu, grow)) {
+          // O holds earlier tiles of this item: rescale it once PV(g - 1) is done
+          const int gp = g - 1;
+          ok = mbar_wait(&tb.pv_done[gp & 1], (gp >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
+          tc_fence_after();
+          float o[32];
+          tmem_ld32_to(t_row + kOCol, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= factor;
+          tmem_st32_from(t_row + kOCol, o);
+          tmem_wait_st();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            lsum[i].x *= factor;
+            lsum[i].y *= factor;
+          }
+        }
+        // ---- probabilities 2^(s * kScale - m_ref), row sum in f32, P as bf16 pairs
+        uint32_t pk[kAttnBK / 2];
+        {
+          const float2 neg = make_float2(-m_ref, -m_ref);
+#pragma unroll
+          for (int j = 0; j < kAttnBK / 2; ++j) {
+            float2 x = fma2(s2[j], scale2, neg);
+            x.x = ex2_approx(x.x);
+            x.y = ex2_approx(x.y);
+            lsum[j & 3] = add2(lsum[j & 3], x);
+            pk[j] = pack_bf16x2(x.x, x.y);
+          }
+        }
+        // P over the S columns this thread just read (the next S MMA into this
+        // buffer waits for the PV MMA that reads P)
+        tmem_st32_u(t_row + buf * kAttnBK, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&tb.p_full[buf]);
+      }
+      // ---- item epilogue: last PV, normalise, gate, store
+      const int gl = g - 1;
+      ok = mbar_wait(&tb.pv_done[gl & 1], (gl >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
+      tc_fence_after();
+      float o[32];
+      tmem_ld32_to(t_row + kOCol, o);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(tb.o_free);
+      if (b_ok && q < args.nq && ok) {
+        const float l = (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y) +
+                        ((lsum[2].x + lsum[2].y) + (lsum[3].x + lsum[3].y));
+        const float inv_l = 1.f / l;
+        __nv_bfloat16* orow =
+            args.out + b * args.out_sb + h * args.out_sh + static_cast<int64_t>(q) * args.out_sq;
+        const __nv_bfloat16* grow_p =
+            args.gate == nullptr ? nullptr
+                                 : args.gate + b * args.gate_sb + h * args.gate_sh +
+                                       static_cast<int64_t>(q) * args.gate_sq;
+        const bool vec = (args.d == 32) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
+                         (grow_p == nullptr || (reinterpret_cast<uintptr_t>(grow_p) & 15) == 0);
+        if (vec) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = o[c * 8 + e] * inv_l;
+            if (grow_p != nullptr) {
+              const uint4 gw = reinterpret_cast<const uint4*>(grow_p)[c];
+              const uint32_t gg[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[2 * e] = bf16r(v[2 * e]) * __uint_as_float(gg[e] << 16);
+                v[2 * e + 1] = bf16r(v[2 * e + 1]) * __uint_as_float(gg[e] & 0xFFFF0000u);
+              }
+            }
+            uint4 pkd;
+            pkd.x = pack_bf16x2(v[0], v[1]);
+            pkd.y = pack_bf16x2(v[2], v[3]);
+            pkd.z = pack_bf16x2(v[4], v[5]);
+            pkd.w = pack_bf16x2(v[6], v[7]);
+            reinterpret_cast<uint4*>(orow)[c] = pkd;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i < args.d) {
+              float v = bf16r(o[i] * inv_l);
+              if (grow_p != nullptr) v = v * __bfloat162float(grow_p[i]);
+              orow[i] = __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace xfb
