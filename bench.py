@@ -21,9 +21,10 @@ the trunk (48 blocks); the metric is ms per block = step time / 48.
 `--impl reference` times that CPU path alone on the same metric (the reference
 arm); under torchrun only rank 0 runs it.
 
-Multi-GPU (--gpus N under torchrun): replicas only in this version — every
-rank runs the full trunk on its own copy ("scaling": "weak" over independent
-trunks, one per GPU); value = the per-block time of the slowest rank.
+Multi-GPU (--gpus N under torchrun): one N = 1024 trunk with its pair
+row-sharded over the N GPUs (rank r holds rows [rN/G, (r+1)N/G)), exchanges
+by the peer-store kernel over NVLink ("scaling": "strong"); value = the
+per-block time of the slowest rank.
 """
 
 from __future__ import annotations
@@ -210,10 +211,10 @@ def run_reference(args) -> None:
 # ----------------------------------------------------------------------------- GPU arm
 
 # DRAM bytes (read + write) per launch from one ncu capture of the same kernel,
-# scaled to the bench shapes by the units processed (profiles/flash_attn_n512_full.md:
-# 323.5 MB at N = 512, every tensor of the launch scales with N^2).  None where no
+# scaled to the bench shapes by the units processed (profiles/flash_tri_n512_full.md:
+# 322.9 MB at N = 512, every tensor of the launch scales with N^2).  None where no
 # capture was taken.
-TRAFFIC_BYTES = {"flash_attn": 1.294e9, "triangle_contraction": None}
+TRAFFIC_BYTES = {"flash_attn": 1.292e9, "triangle_contraction": None}
 
 
 def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:

@@ -1,14 +1,15 @@
 // Triangle attention (head dim <= 32, one bias shared by every batch row) on
 // tcgen05 with three query tiles in flight per SM.
 //
-// The exponentials, not the MMAs, bound this attention: one score costs 4 d =
-// 128 MMA FLOP but one ex2 on the MUFU unit (16 per clock per SM).  The
-// one-tile-per-CTA kernel in attention.cuh keeps two softmax warps per SM
-// sub-partition busy and leaves the MUFU unit idle half of the time while
-// those warps wait on TMEM loads, stores and barriers.  This kernel runs one
-// persistent CTA per SM with three softmax warpgroups, each owning its own
-// query tile ("slot"), so three softmax warps share each sub-partition and
-// cover each other's latencies.
+// With head dim 32 one score costs 4 d = 128 MMA FLOP but one ex2 on the MUFU
+// unit (16 per clock per SM), and the MMAs are small (M = 128, N <= 64,
+// K = 16), so the softmax warps and the tensor pipe bound this attention
+// together, not the tensor FLOPs.  The one-tile-per-CTA kernel in attention.cuh
+// keeps two softmax warps per SM sub-partition and leaves the MUFU unit idle
+// half of the time while they wait on TMEM loads, stores and barriers.  This
+// kernel runs one persistent CTA per SM with three softmax warpgroups, each
+// owning its own query tile ("slot"), so three softmax warps share each
+// sub-partition and cover each other's latencies.
 //
 // Work group = (head h, 128-query tile qt, batch rows 3j, 3j+1, 3j+2): slot s
 // handles batch row 3j+s.  The bias tile bias[h, qt-rows, key-tile] is the
@@ -16,7 +17,8 @@
 // three slots' S MMAs.  Per 64-key tile of a slot:
 //   S   = bias + Q K^T   four identity MMAs (the bf16 bias enters the f32
 //                        accumulator exactly) then the QK^T MMAs, into one of
-//                        the slot's two 64-column S buffers
+//                        the slot's two 64-column S buffers (XFB_TRI_BIAS_MMA=0:
+//                        the softmax adds the bias from shared memory instead)
 //   P   = 2^(S - m_ref)  softmax warps, one query row per thread; P (bf16
 //                        pairs) is written back over the first 32 columns of
 //                        the same S buffer, and the row sum of the f32
@@ -44,8 +46,20 @@ constexpr int kTriRegsLaunch = 128, kTriRegsSoftmax = 152, kTriRegsOther = 56;
 static_assert(3 * 128 * kTriRegsSoftmax + 128 * kTriRegsOther == kTriThreads * kTriRegsLaunch,
               "register split must add up to the launch allocation");
 constexpr int kTriKvStages = 3;    // per slot, freed by the slot's PV MMA
-constexpr int kTriBiasStages = 3;  // shared, freed once every slot's S MMA read it
+constexpr int kTriBiasStages = 3;  // shared by the slots, freed once all of them read it
 constexpr int kTriSlotCols = 160;
+// 1: the bias tile enters S through identity MMAs (tensor pipe); 0: the
+// softmax warps add it from shared memory (ALU / FMA pipes).
+#ifndef XFB_TRI_BIAS_MMA
+#define XFB_TRI_BIAS_MMA 1
+#endif
+constexpr bool kTriBiasMma = XFB_TRI_BIAS_MMA != 0;
+// Of every 8 pairs of probabilities in a row tile, this many are computed by
+// exp2_poly2 on the FMA pipe instead of ex2.approx on the MUFU unit.
+#ifndef XFB_TRI_POLY_PAIRS
+#define XFB_TRI_POLY_PAIRS 0
+#endif
+constexpr int kTriPolyPairs = XFB_TRI_POLY_PAIRS;
 
 struct TriSmem {
   static constexpr int kQBytes = 128 * 32 * 2;       // 8 KB, 64-byte swizzle
@@ -153,7 +167,8 @@ __global__ void __launch_bounds__(kTriThreads, 1)
     }
     for (int i = 0; i < kTriBiasStages; ++i) {
       mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], kTriSlots);  // one commit per slot
+      // one MMA commit per slot, or one arrive per softmax warp
+      mbar_init(&b_empty[i], kTriBiasMma ? kTriSlots : kTriSlots * 4);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -261,25 +276,29 @@ __global__ void __launch_bounds__(kTriThreads, 1)
         const int sb = gs % kTriBiasStages;
         const int buf = gs & 1;
         if ((t == 0 && !mbar_wait(&tb.q_full[qb], (it >> 1) & 1, kErrWaitMma, abort_flag)) ||
-            !mbar_wait(&b_full[sb], (gs / kTriBiasStages) & 1, kErrWaitMma, abort_flag) ||
+            (kTriBiasMma &&
+             !mbar_wait(&b_full[sb], (gs / kTriBiasStages) & 1, kErrWaitMma, abort_flag)) ||
             !mbar_wait(&tb.kv_full[st], (gs / kTriKvStages) & 1, kErrWaitMma, abort_flag) ||
             (gs >= 2 &&
              !mbar_wait(&tb.pv_done[buf], ((gs - 2) >> 1) & 1, kErrWaitMma, abort_flag)))
           return false;
         tc_fence_after();
         const uint32_t d_tmem = slot_tmem + buf * kAttnBK;
-        const uint32_t b_addr = smem_u32(sBias + sb * L::kBiasBytes);
         const uint32_t q_addr = smem_u32(sQ + (s * 2 + qb) * L::kQBytes);
         const uint32_t k_addr = smem_u32(sK + (s * kTriKvStages + st) * L::kKVBytes);
-        // S[:, 16j + n] = sum_k bias[:, 16j + k] I[k][n]: exact in the f32 accumulator
+        if (kTriBiasMma) {
+          // S[:, 16j + n] = sum_k bias[:, 16j + k] I[k][n]: exact in the f32 accumulator
+          const uint32_t b_addr = smem_u32(sBias + sb * L::kBiasBytes);
 #pragma unroll
-        for (int j = 0; j < kAttnBK / 16; ++j)
-          umma_bf16(d_tmem + 16 * j, p_desc(b_addr, j), ident_desc, kIdescB, 0u);
+          for (int j = 0; j < kAttnBK / 16; ++j)
+            umma_bf16(d_tmem + 16 * j, p_desc(b_addr, j), ident_desc, kIdescB, 0u);
+        }
 #pragma unroll
         for (int k = 0; k < 2; ++k)
-          umma_bf16(d_tmem, qk_desc<32>(q_addr, k), qk_desc<32>(k_addr, k), kIdescS, 1u);
+          umma_bf16(d_tmem, qk_desc<32>(q_addr, k), qk_desc<32>(k_addr, k), kIdescS,
+                    (kTriBiasMma || k > 0) ? 1u : 0u);
         umma_commit(&tb.s_full[buf]);
-        umma_commit(&b_empty[sb]);  // one of the three slots done with this bias tile
+        if (kTriBiasMma) umma_commit(&b_empty[sb]);  // this slot is done with the bias tile
         if (t == n_tiles - 1) umma_commit(&tb.q_empty[qb]);
         return true;
       };
@@ -338,6 +357,20 @@ __global__ void __launch_bounds__(kTriThreads, 1)
           w0 = mrow[2 * t];
           w1 = (2 * t + 1 < words) ? mrow[2 * t + 1] : 0u;
         }
+        // this row of the shared bias tile (128-byte swizzle: 16-byte chunk c of
+        // row r sits at chunk c ^ (r % 8)), read before S is waited for
+        uint4 bw[kAttnBK / 8];
+        if (!kTriBiasMma) {
+          const int sbias = g % kTriBiasStages;
+          ok = mbar_wait(&b_full[sbias], (g / kTriBiasStages) & 1, kErrWaitSoftmax, abort_flag) &&
+               ok;
+          const uint8_t* brow = sBias + sbias * L::kBiasBytes + row * 128;
+#pragma unroll
+          for (int c = 0; c < kAttnBK / 8; ++c)
+            bw[c] = *reinterpret_cast<const uint4*>(brow + ((c ^ (row & 7)) << 4));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&b_empty[sbias]);  // the warp's values are in registers
+        }
         ok = mbar_wait(&tb.s_full[buf], (g >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
         tc_fence_after();
         float s[kAttnBK];
@@ -345,6 +378,16 @@ __global__ void __launch_bounds__(kTriThreads, 1)
         tmem_ld32_to(t_row + buf * kAttnBK + 32, s + 32);
         tmem_wait_ld();
         float2* s2 = reinterpret_cast<float2*>(s);
+        if (!kTriBiasMma) {
+#pragma unroll
+          for (int c = 0; c < kAttnBK / 8; ++c) {
+            const uint32_t ww[4] = {bw[c].x, bw[c].y, bw[c].z, bw[c].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              s2[c * 4 + e] = add2(s2[c * 4 + e], make_float2(__uint_as_float(ww[e] << 16),
+                                                              __uint_as_float(ww[e] & 0xFFFF0000u)));
+          }
+        }
         // ---- key mask: masked -> -1e9, past the end -> -inf
         if (key0 + kAttnBK > args.nk || (w0 & w1) != 0xFFFFFFFFu) {
 #pragma unroll
@@ -390,8 +433,12 @@ __global__ void __launch_bounds__(kTriThreads, 1)
 #pragma unroll
           for (int j = 0; j < kAttnBK / 2; ++j) {
             float2 x = fma2(s2[j], scale2, neg);
-            x.x = ex2_approx(x.x);
-            x.y = ex2_approx(x.y);
+            if ((j & 7) < kTriPolyPairs) {
+              x = exp2_poly2(x);
+            } else {
+              x.x = ex2_approx(x.x);
+              x.y = ex2_approx(x.y);
+            }
             lsum[j & 3] = add2(lsum[j & 3], x);
             pk[j] = pack_bf16x2(x.x, x.y);
           }
@@ -404,6 +451,15 @@ __global__ void __launch_bounds__(kTriThreads, 1)
         mbar_arrive(&tb.p_full[buf]);
       }
       // ---- item epilogue: last PV, normalise, gate, store
+      const bool store = b_ok && q < args.nq;
+      __nv_bfloat16* orow =
+          args.out + b * args.out_sb + h * args.out_sh + static_cast<int64_t>(q) * args.out_sq;
+      const __nv_bfloat16* grow_p =
+          args.gate == nullptr ? nullptr
+                               : args.gate + b * args.gate_sb + h * args.gate_sh +
+                                     static_cast<int64_t>(q) * args.gate_sq;
+      const bool vec = (args.d == 32) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
+                       (grow_p == nullptr || (reinterpret_cast<uintptr_t>(grow_p) & 15) == 0);
       const int gl = g - 1;
       ok = mbar_wait(&tb.pv_done[gl & 1], (gl >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
       tc_fence_after();
@@ -412,18 +468,10 @@ __global__ void __launch_bounds__(kTriThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(tb.o_free);
-      if (b_ok && q < args.nq && ok) {
+      if (store && ok) {
         const float l = (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y) +
                         ((lsum[2].x + lsum[2].y) + (lsum[3].x + lsum[3].y));
         const float inv_l = 1.f / l;
-        __nv_bfloat16* orow =
-            args.out + b * args.out_sb + h * args.out_sh + static_cast<int64_t>(q) * args.out_sq;
-        const __nv_bfloat16* grow_p =
-            args.gate == nullptr ? nullptr
-                                 : args.gate + b * args.gate_sb + h * args.gate_sh +
-                                       static_cast<int64_t>(q) * args.gate_sq;
-        const bool vec = (args.d == 32) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
-                         (grow_p == nullptr || (reinterpret_cast<uintptr_t>(grow_p) & 15) == 0);
         if (vec) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
