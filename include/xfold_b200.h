@@ -272,7 +272,9 @@ XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t ro
 
 /* TriMul stage 3 (triangle_multiplication.py:96-105 on a row block): z = the
  * contraction for these rows, channel-major [c][rows][n] bf16; update =
- * (LN_c(z) W_o^T) * g -> out [rows][n][c] (accumulate: out f32 += update). */
+ * (LN_c(z) W_o^T) * g -> out [rows][n][c] (accumulate: out f32 += update).  The
+ * centre LayerNorm is folded into the projection GEMM (per-position statistics,
+ * weights scaled by the LayerNorm weight); the workspace holds those statistics. */
 XFB_API int64_t xfb_triangle_output_workspace(int64_t rows, int64_t n, int64_t c);
 XFB_API int xfb_triangle_output(const void* z, int64_t rows, int64_t n, int64_t c, const void* g,
                                 const float* center_weight, const float* center_bias,

@@ -486,6 +486,104 @@ int check_workspace(const Carver& cv, const void* ws, int64_t ws_bytes) {
   return XFB_OK;
 }
 
+// ------------------------------------------------------------------ triangle output
+
+// W'[n][k] = bf16(gamma[k] W[n][k]), colsum[n] = sum_k W'[n][k] (the rounded
+// values the GEMM multiplies), colbias[n] = sum_k beta[k] W[n][k]; one block
+// of 128 threads per output channel n.
+__global__ void tri_center_fold_kernel(const float* gamma, const float* beta, const bf16* w, int c,
+                                       bf16* wf, float* colsum, float* colbias) {
+  __shared__ float red[2][4];
+  const int n = blockIdx.x;
+  float s = 0.f, sb = 0.f;
+  for (int k = threadIdx.x; k < c; k += blockDim.x) {
+    const float wv = __bfloat162float(w[static_cast<int64_t>(n) * c + k]);
+    const bf16 f = __float2bfloat16_rn((gamma ? gamma[k] : 1.f) * wv);
+    wf[static_cast<int64_t>(n) * c + k] = f;
+    s += __bfloat162float(f);
+    sb += (beta ? beta[k] : 0.f) * wv;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = s;
+    red[1][threadIdx.x >> 5] = sb;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    colsum[n] = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
+    colbias[n] = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+  }
+}
+
+struct TriCenterWs {
+  float2* stats;   // [count]
+  bf16* wf;        // [c][c]
+  float* colsum;   // [c]
+  float* colbias;  // [c]
+};
+
+void tri_center_layout(Carver& cv, int64_t count, int64_t c, TriCenterWs* w) {
+  w->stats = cv.take<float2>(count);
+  w->wf = cv.take<bf16>(c * c);
+  w->colsum = cv.take<float>(c);
+  w->colbias = cv.take<float>(c);
+}
+
+template <class EPI>
+int tri_center_gemm(const bf16* z, int64_t count, int64_t c, const bf16* g, void* out,
+                    int accumulate, const TriCenterWs& w, cudaStream_t st) {
+  constexpr bool kF32 = EPI::kColsPerBox == 32;
+  EPI epi;
+  XFB_TRY(make_out_map(&epi.out_map, out, kF32, c, count, 1, c, 0));
+  epi.bias = nullptr;
+  epi.accumulate = accumulate;
+  const uint64_t dims[3] = {static_cast<uint64_t>(c), static_cast<uint64_t>(count), 1};
+  const uint64_t strides[2] = {static_cast<uint64_t>(c * 2), static_cast<uint64_t>(count * c * 2)};
+  const uint32_t box[3] = {64, 128, 1};
+  XFB_TRY(make_map_nd(&epi.gate_map, false, 3, g, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  epi.stats = w.stats;
+  epi.colsum = w.colsum;
+  epi.colbias = w.colbias;
+  epi.rows = static_cast<int>(count);
+  // A = z read MN-major: element (position p, channel k) at z[k * count + p]
+  return run_gemm<128, true, false>(z, count, 0, w.wf, c, 0, count, c, c, 1, epi, st);
+}
+
+// Centre LayerNorm + output projection + output gate of a triangle
+// multiplication, for a channel-major contraction result with contiguous
+// positions, z[k * count + p]:  out (=|+=) bf16(bf16(LN_c(z) W^T) * g).  The
+// LayerNorm is folded into the GEMM (EpiOutLnGated): one read-only statistics
+// pass over z, and the GEMM reads z itself instead of a normalised copy.
+int tri_center_output(const bf16* z, int64_t count, int64_t c, const bf16* g, const float* gamma,
+                      const float* beta, double eps, const bf16* w, void* out, bool out_f32,
+                      int accumulate, const TriCenterWs& ws, cudaStream_t st) {
+  XFB_REQUIRE(count % 8 == 0 && aligned16(z) && aligned16(g) && aligned16(out),
+              "folded centre LayerNorm needs 16-byte aligned buffers and count % 8 == 0");
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int blocks =
+      static_cast<int>(std::min<int64_t>((count / 2 + 255) / 256, int64_t(sms) * 8));
+  if (c == 128) {
+    xfb::ln_stats_channel_major_kernel<128><<<blocks, 256, 0, st>>>(
+        z, count, count, static_cast<float>(eps), ws.stats);
+  } else {
+    xfb::ln_stats_channel_major_kernel<64><<<blocks, 256, 0, st>>>(
+        z, count, count, static_cast<float>(eps), ws.stats);
+  }
+  XFB_LAUNCHED();
+  tri_center_fold_kernel<<<static_cast<int>(c), 128, 0, st>>>(gamma, beta, w, static_cast<int>(c),
+                                                              ws.wf, ws.colsum, ws.colbias);
+  XFB_LAUNCHED();
+  return out_f32 ? tri_center_gemm<xfb::EpiOutLnGated<128, true>>(z, count, c, g, out, accumulate,
+                                                                  ws, st)
+                 : tri_center_gemm<xfb::EpiOutLnGated<128, false>>(z, count, c, g, out,
+                                                                   accumulate, ws, st);
+}
+
 // ------------------------------------------------------------------ attention launcher
 
 template <int DP, int BMODE, bool PRE>
@@ -866,6 +964,7 @@ XFB_API int xfb_pack_triangle_weights(const void* projection, const void* gate,
 namespace {
 struct TriWs {
   bf16 *x, *a, *b, *g, *z, *packed;
+  TriCenterWs center;  // folded centre LayerNorm (n % 8 == 0)
 };
 void tri_layout(Carver& cv, int64_t n, int64_t c, bool need_pack, TriWs* w) {
   const int64_t pitch = pad_pitch(n);
@@ -875,6 +974,7 @@ void tri_layout(Carver& cv, int64_t n, int64_t c, bool need_pack, TriWs* w) {
   w->z = cv.take<bf16>(c * n * pitch);
   w->g = cv.take<bf16>(n * n * c);
   w->packed = need_pack ? cv.take<bf16>(5 * c * c) : nullptr;
+  tri_center_layout(cv, n * n, c, &w->center);
 }
 }  // namespace
 
@@ -967,6 +1067,13 @@ XFB_API int xfb_triangle_multiplication(
       XFB_TRY((run_gemm<256, true, true>(w.b, pitch, n * pitch, w.a, pitch, n * pitch, n, n, n,
                                          c, epi, st)));
     }
+  }
+  // 4-5. centre LayerNorm folded into the output projection when the positions
+  //      of z are contiguous (pitch == n)
+  if (pitch == n) {
+    return tri_center_output(w.z, M, c, w.g, center_weight, center_bias, center_eps,
+                             static_cast<const bf16*>(output_weight), out, out_dtype == XFB_F32,
+                             accumulate, w.center, st);
   }
   // 4. centre LayerNorm over channels (channel-major in, row-major out; x is reused)
   {
@@ -1506,7 +1613,8 @@ XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t ro
 
 XFB_API int64_t xfb_triangle_output_workspace(int64_t rows, int64_t n, int64_t c) {
   Carver cv{nullptr, 0, 0};
-  cv.take<bf16>(rows * n * c);
+  TriCenterWs w;
+  tri_center_layout(cv, rows * n, c, &w);
   return cv.used;
 }
 
@@ -1527,24 +1635,13 @@ XFB_API int xfb_triangle_output(const void* z, int64_t rows, int64_t n, int64_t 
   XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
-  bf16* x = cv.take<bf16>(rows * n * c);
+  TriCenterWs w;
+  tri_center_layout(cv, rows * n, c, &w);
   XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
-  int sms;
-  XFB_TRY(sm_count(&sms));
-  const int blocks = static_cast<int>(std::min<int64_t>((rows * n + 127) / 128, int64_t(sms) * 8));
-  const bf16* zz = static_cast<const bf16*>(z);
-  if (c == 128) {
-    xfb::ln_channel_major_kernel<128><<<blocks, 128, 0, st>>>(
-        zz, static_cast<int>(rows), static_cast<int>(n), static_cast<int>(n), rows * n,
-        center_weight, center_bias, static_cast<float>(center_eps), x);
-  } else {
-    xfb::ln_channel_major_kernel<64><<<blocks, 128, 0, st>>>(
-        zz, static_cast<int>(rows), static_cast<int>(n), static_cast<int>(n), rows * n,
-        center_weight, center_bias, static_cast<float>(center_eps), x);
-  }
-  XFB_LAUNCHED();
-  return linear_core(x, rows * n, c, c, static_cast<const bf16*>(output_weight), c, nullptr,
-                     static_cast<const bf16*>(g), c, out, out_dtype == XFB_F32, accumulate, c, st);
+  return tri_center_output(static_cast<const bf16*>(z), rows * n, c, static_cast<const bf16*>(g),
+                           center_weight, center_bias, center_eps,
+                           static_cast<const bf16*>(output_weight), out, out_dtype == XFB_F32,
+                           accumulate, w, st);
 }
 
 XFB_API int xfb_grid_attention_prepare(const void* pair, int pair_dtype, int64_t rows, int64_t n,

@@ -489,6 +489,43 @@ struct EpiOutGated : EpiOut<BN, OUT_F32> {
   }
 };
 
+// EpiOutGated whose A operand is the un-normalised input of a LayerNorm over
+// the K dimension, folded into the GEMM: with per-row stats (mean, rstd) and a
+// weight W'[n][k] = gamma[k] W[n][k],
+//   LN(x) W^T = rstd (x W'^T - mean colsum) + colbias,
+//   colsum[n] = sum_k W'[n][k],  colbias[n] = sum_k beta[k] W[n][k],
+// then out = bf16(bf16(that) * gate).  The centring happens on the f32
+// accumulator, so no rounding of the normalised activations is involved.
+template <int BN, bool OUT_F32>
+struct EpiOutLnGated : EpiOutGated<BN, OUT_F32> {
+  const float2* stats;   // [rows] (mean, rstd)
+  const float* colsum;   // [N]
+  const float* colbias;  // [N]
+  int rows;
+
+  __device__ void compute(const EpiCtx& c) const {
+    constexpr int kHalf = BN / 2;
+    const float2 st = stats[min(c.m0 + c.row, rows - 1)];
+#pragma unroll 1
+    for (int c0 = 0; c0 < kHalf; c0 += 16) {
+      const int col = c.half * kHalf + c0;
+      float v[16], g[16];
+      tmem_ld16(c.tmem + col, v);
+      const uint8_t* gbox = c.aux + (col / 64) * 16384;
+      unpack8_bf16(*reinterpret_cast<const uint4*>(sw128_chunk(gbox, c.row, (col % 64) / 8)), g);
+      unpack8_bf16(*reinterpret_cast<const uint4*>(sw128_chunk(gbox, c.row, (col % 64) / 8 + 1)),
+                   g + 8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int n = c.n0 + col + i;
+        const float y = fmaf(st.y, fmaf(-st.x, colsum[n], v[i]), colbias[n]);
+        v[i] = bf16r(bf16r(y) * g[i]);
+      }
+      this->write(c, col, v);
+    }
+  }
+};
+
 // Direct per-thread stores (no staging): out [bat][m][ld] bf16 or f32.  Used by
 // the batched contraction (whose rows are 512-byte contiguous runs) and by odd
 // shapes the TMA layouts do not cover.

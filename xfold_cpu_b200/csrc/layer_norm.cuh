@@ -489,6 +489,41 @@ __global__ void __launch_bounds__(128) ln_channel_major_kernel(
   }
 }
 
+// LayerNorm statistics over the channels of a channel-major bf16 tensor with
+// contiguous positions: x[ch * chan_stride + p], p < count (count even).  Writes
+// stats[p] = (mean, 1 / sqrt(var + eps)).  Each thread takes two neighbouring
+// positions, so a warp reads one 128-byte line per channel plane; the sums
+// are shifted by the position's channel-0 value (a one-pass variance without
+// the cancellation of E[x^2] - E[x]^2 at large means).
+template <int C>
+__global__ void __launch_bounds__(256) ln_stats_channel_major_kernel(
+    const __nv_bfloat16* x, int64_t count, int64_t chan_stride, float eps, float2* stats) {
+  const int64_t pairs = count / 2;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < pairs;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(x) + t;
+    const int64_t stride_words = chan_stride / 2;
+    const uint32_t w0 = src[0];
+    const float k0 = __uint_as_float(w0 << 16), k1 = __uint_as_float(w0 & 0xFFFF0000u);
+    float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
+#pragma unroll 16
+    for (int ch = 1; ch < C; ++ch) {
+      const uint32_t w = src[ch * stride_words];
+      const float d0 = __uint_as_float(w << 16) - k0;
+      const float d1 = __uint_as_float(w & 0xFFFF0000u) - k1;
+      s0 += d0;
+      s1 += d1;
+      q0 = fmaf(d0, d0, q0);
+      q1 = fmaf(d1, d1, q1);
+    }
+    const float m0 = s0 * (1.f / C), m1 = s1 * (1.f / C);
+    const float v0 = fmaxf(q0 * (1.f / C) - m0 * m0, 0.f);
+    const float v1 = fmaxf(q1 * (1.f / C) - m1 * m1, 0.f);
+    reinterpret_cast<float4*>(stats)[t] =
+        make_float4(k0 + m0, rsqrtf(v0 + eps), k1 + m1, rsqrtf(v1 + eps));
+  }
+}
+
 // Row gather used to pack weights: dst[r][:] = src[map(r)][:] (bf16), zero rows
 // where map(r) < 0.  `src_is_f32` selects the source element type.
 __global__ void pack_rows_kernel(const void* src, int src_is_f32, const int* map, int rows,
