@@ -191,6 +191,11 @@ constexpr int gemm_stages() {
   constexpr int aux = ((Epi::kAuxBytes + 1023) / 1024) * 1024 * 2;
   constexpr int staging = ((Epi::kStagingBytes + 1023) / 1024) * 1024 * Epi::kStagingBufs;
   constexpr int budget = 200 * 1024 - aux - staging;
+  // Epilogues with large buffers (an f32 output plus an aux ring) would keep
+  // only two operand stages, i.e. no prefetch of the next tile when K = 128:
+  // those take a third stage out of the last 24 KB of shared memory.
+  constexpr int wide = 224 * 1024 - aux - staging;
+  if (budget / stage <= 2 && wide / stage >= 3) return 3;
   return budget / stage > 6 ? 6 : budget / stage;
 }
 
