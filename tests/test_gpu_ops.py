@@ -218,6 +218,30 @@ def test_transition(rows, c, factor):
     assert _rel(got, ref) < TOL
 
 
+@pytest.mark.parametrize("rows,factor,accumulate", [(300, 4, True), (1000, 2, False),
+                                                     (128, 4, False)])
+def test_fused_pair_transition(rows, factor, accumulate):
+    """c = 128 with an f32 output runs the fused GLU transition (hidden tile kept
+    on chip): a partial last row tile, hidden 256 / 512, residual add and store."""
+    g = _g(8)
+    c = 128
+    w, b = _ln(g, c)
+    p = {"input_layer_norm.weight": w, "input_layer_norm.bias": b,
+         "transition1.weight": _w(g, 2 * factor * c, c, std=0.1),
+         "transition2.weight": _w(g, c, factor * c, std=0.05)}
+    x = torch.randn(rows, c, generator=g)
+    base = torch.randn(rows, c, generator=g)
+    ref = oracle.transition(x, p)
+    d = {k: v.to(DEV) for k, v in p.items()}
+    w1 = native.pack_glu_weight(d["transition1.weight"])
+    out = base.to(DEV).clone() if accumulate else None
+    got = native.transition(x.to(DEV), d["input_layer_norm.weight"], d["input_layer_norm.bias"],
+                            1e-5, w1, d["transition2.weight"], factor, out=out,
+                            accumulate=accumulate, out_dtype=torch.float32)
+    update = got.cpu() - base if accumulate else got.cpu()
+    assert _rel(update, ref) < TOL
+
+
 @pytest.mark.parametrize("n,c,heads", [(200, 384, 16), (300, 768, 16)])
 def test_self_attention(n, c, heads):
     g = _g(8)

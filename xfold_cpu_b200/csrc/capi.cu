@@ -16,6 +16,7 @@
 #include "../../include/xfold_b200.h"
 #include "attention.cuh"
 #include "tri_attention.cuh"
+#include "transition.cuh"
 #include "exchange.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
@@ -1372,6 +1373,39 @@ XFB_API int64_t xfb_transition_workspace(int64_t rows, int64_t c, int64_t factor
   return cv.used;
 }
 
+namespace {
+// The fused GLU transition (transition.cuh) for c = 128 with an f32 output and
+// no output gate; XFB_FUSED_TRANSITION=0 selects the two-GEMM form.
+bool use_fused_transition() {
+  static const bool enabled = [] {
+    const char* e = std::getenv("XFB_FUSED_TRANSITION");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return enabled;
+}
+
+int launch_fused_transition(const bf16* x, int64_t rows, int64_t hid, const bf16* w1p,
+                            const bf16* w2, void* out, int accumulate, cudaStream_t st) {
+  XFB_REQUIRE(rows <= (1ll << 31) - 256, "transition has too many rows");
+  XFB_REQUIRE(aligned16(x) && aligned16(w1p) && aligned16(w2),
+              "transition buffers must be 16-byte aligned");
+  CUtensorMap tx, tw1, tw2, to;
+  XFB_TRY(make_map(&tx, x, 128, rows, 1, 256, 0, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+  XFB_TRY(make_map(&tw1, w1p, 128, 2 * hid, 1, 256, 0, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+  XFB_TRY(make_map(&tw2, w2, hid, 128, 1, hid * 2, 0, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+  XFB_TRY(make_out_map(&to, out, true, 128, rows, 1, 128, 0));
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int64_t m_tiles = (rows + 127) / 128;
+  const int grid = static_cast<int>(std::min<int64_t>(m_tiles, sms));
+  XFB_TRY(set_smem(xfb::fused_transition_kernel, xfb::FtSmem::kLaunchBytes));
+  xfb::fused_transition_kernel<<<grid, xfb::kFtThreads, xfb::FtSmem::kLaunchBytes, st>>>(
+      tx, tw1, tw2, to, static_cast<int>(rows), static_cast<int>(hid / 64), accumulate);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+}  // namespace
+
 XFB_API int xfb_transition(const void* x, int x_dtype, int64_t rows, int64_t c,
                            int64_t factor, const float* norm_weight, const float* norm_bias,
                            double eps, const void* mod_scale, const void* mod_shift,
@@ -1401,6 +1435,10 @@ XFB_API int xfb_transition(const void* x, int x_dtype, int64_t rows, int64_t c,
   XFB_TRY(run_layer_norm(x, x_dtype, rows, c, c, norm_weight, norm_bias, eps, w.x, c,
                          static_cast<const bf16*>(mod_scale), static_cast<const bf16*>(mod_shift),
                          nullptr, 0, nullptr, 0, st));
+  if (c == 128 && out_gate == nullptr && out_dtype == XFB_F32 && use_fused_transition()) {
+    return launch_fused_transition(w.x, rows, hid, w1p, static_cast<const bf16*>(w2), out,
+                                   accumulate, st);
+  }
   {
     xfb::EpiGLU epi;
     XFB_TRY(make_out_map(&epi.out_map, w.h, false, hid, rows, 1, hid, 0));
