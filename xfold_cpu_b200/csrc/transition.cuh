@@ -19,7 +19,10 @@
 //
 // TMEM (512 columns): acc1 x 2 at columns 0 / 128, acc2 x 2 at 256 / 384.
 // Warps 0-7: epilogue (warp w: TMEM lane quarter w % 4, column half w / 4);
-// warp 8: TMA producer; warp 9: TMEM owner and MMA issuer.
+// warp 8: TMA producer of x and W1; warp 9: TMEM owner and MMA issuer; warp 10:
+// TMA producer of W2.  The two weight rings have their own producers: W2(q)
+// waits for GEMM2(q - 2), and a single producer would hold W1(q + 1) behind that
+// wait (a clock64 trace showed GEMM1 issued ~1000 cycles late on every chunk).
 #pragma once
 
 #include "common.cuh"
@@ -27,7 +30,7 @@
 
 namespace xfb {
 
-constexpr int kFtThreads = 320;
+constexpr int kFtThreads = 352;
 constexpr int kFtEpiThreads = 256;
 
 struct FtSmem {
@@ -134,8 +137,7 @@ __global__ void __launch_bounds__(kFtThreads, 1)
         tma_load_3d(sx + 16384, &tmX, &x_full[xb], 64, tile * 128, 0);
         for (int j = 0; j < chunks; ++j, ++q) {
           const int s = q & 1;
-          const uint32_t ph = ((q >> 1) & 1) ^ 1;
-          if (!mbar_wait(&w1_empty[s], ph, kErrWaitProducer, abort_flag)) {
+          if (!mbar_wait(&w1_empty[s], ((q >> 1) & 1) ^ 1, kErrWaitProducer, abort_flag)) {
             ok = false;
             break;
           }
@@ -143,7 +145,18 @@ __global__ void __launch_bounds__(kFtThreads, 1)
           uint8_t* sw1 = smem + L::kW1Off + s * L::kW1Bytes;
           tma_load_3d(sw1, &tmW1, &w1_full[s], 0, 128 * j, 0);
           tma_load_3d(sw1 + 16384, &tmW1, &w1_full[s], 64, 128 * j, 0);
-          if (!mbar_wait(&w2_empty[s], ph, kErrWaitProducer, abort_flag)) {
+        }
+      }
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------ TMA producer of W2
+    if (lane == 0) {
+      int q = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < m_tiles; tile += gridDim.x) {
+        for (int j = 0; j < chunks; ++j, ++q) {
+          const int s = q & 1;
+          if (!mbar_wait(&w2_empty[s], ((q >> 1) & 1) ^ 1, kErrWaitProducer, abort_flag)) {
             ok = false;
             break;
           }
@@ -214,7 +227,7 @@ __global__ void __launch_bounds__(kFtThreads, 1)
       }
       if (ok && p_q >= 0) issue_g2();
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------ epilogue warps 0-7
     const int row = (warp & 3) * 32 + lane;
     const int half = warp >> 2;
