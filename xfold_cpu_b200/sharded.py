@@ -68,6 +68,10 @@ class CollectiveExchange:
         recv = self.all_to_all([t.view(g, c // g, rows, n) for t in blocks])
         return [t.transpose(0, 1).reshape(c // g, g * rows, n) for t in recv]
 
+    def rows_to_channels_pair(self, a_blocks, b_blocks):
+        """rows_to_channels of the TriMul operands a and b."""
+        return self.rows_to_channels(a_blocks), self.rows_to_channels(b_blocks)
+
     def channels_to_rows(self, blocks):
         g = self.world
         cs, n, _ = blocks[0].shape
@@ -221,18 +225,31 @@ class PeerExchange:
 
         return _capi.CopyBox(src_ptr, dst_ptr, d0, d1, d2_bytes, s0, s1, t0, t1)
 
-    def rows_to_channels(self, blocks):
-        (a,) = blocks
+    def _r2c_boxes(self, a, kind):
         g, r = self.world, self.rank
-        a = a.contiguous()
         c, rows, n = a.shape
         cs, e = c // g, a.element_size()
-        local, peers = self._recv("r2c", (cs, n, n), a.dtype, a.device)
+        local, peers = self._recv(kind, (cs, n, n), a.dtype, a.device)
         boxes = [self._box(a.data_ptr() + s * cs * rows * n * e, peers[s] + r * rows * n * e,
                            cs, rows, n * e, rows * n * e, n * e, n * n * e, n * e)
                  for s in range(g)]
+        return local, boxes
+
+    def rows_to_channels(self, blocks):
+        (a,) = blocks
+        a = a.contiguous()
+        local, boxes = self._r2c_boxes(a, "r2c")
         self._copy_and_sync(boxes, a.device)
         return [local]
+
+    def rows_to_channels_pair(self, a_blocks, b_blocks):
+        """rows_to_channels of a and b in one copy launch and one barrier."""
+        (a,), (b,) = a_blocks, b_blocks
+        a, b = a.contiguous(), b.contiguous()
+        la, boxes_a = self._r2c_boxes(a, "r2c")
+        lb, boxes_b = self._r2c_boxes(b, "r2c_b")
+        self._copy_and_sync(boxes_a + boxes_b, a.device)
+        return [la], [lb]
 
     def channels_to_rows(self, blocks):
         (z,) = blocks
@@ -381,8 +398,8 @@ def _triangle(mod, pairs, pair_mask, exchange, stages):
     rows, n, c = pairs[0].shape
     projected = [stages.trimul_project(mod, pair, pair_mask[shard_rows(n, g, r)])
                  for pair, r in zip(pairs, exchange.ranks)]
-    a_full = exchange.rows_to_channels([a for a, _, _ in projected])  # [c/G, n, n]
-    b_full = exchange.rows_to_channels([b for _, b, _ in projected])
+    a_full, b_full = exchange.rows_to_channels_pair([a for a, _, _ in projected],
+                                                    [b for _, b, _ in projected])  # [c/G, n, n]
     z = [stages.trimul_contract(mod, a, b) for a, b in zip(a_full, b_full)]
     del a_full, b_full
     z_rows = exchange.channels_to_rows(z)  # [c, rows, n]
