@@ -222,6 +222,63 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(LnArgs a) {
   }
 }
 
+// LayerNorm of 128-wide rows into bf16 y, without head projection, gather,
+// permutation or modulation (the pair LayerNorms before the triangle
+// multiplication and the transition): ln_rows_kernel's arithmetic, but each
+// warp takes K rows per step so K rows' loads are in flight.
+template <typename InT, int K>
+__global__ void __launch_bounds__(256) ln_rows128_multi_kernel(LnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  float wv[4], bv[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    wv[e] = a.w ? a.w[lane * 4 + e] : 1.f;
+    bv[e] = a.b ? a.b[lane * 4 + e] : 0.f;
+  }
+  for (int64_t r0 = K * warp_id; r0 < a.rows; r0 += K * warps_total) {
+    float v[K][4];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (r0 + k < a.rows) {
+        load_vec4<InT>(reinterpret_cast<const InT*>(a.x) + (r0 + k) * a.ldx + lane * 4, v[k]);
+      } else {
+        v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.f;
+      }
+    }
+    float mean[K], rstd[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s += v[k][e];
+      mean[k] = warp_sum(s) * (1.f / 128);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float dlt = v[k][e] - mean[k];
+        ss += dlt * dlt;
+      }
+      rstd[k] = rsqrtf(warp_sum(ss) * (1.f / 128) + a.eps);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (r0 + k >= a.rows) break;
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = bf16r((v[k][e] - mean[k]) * rstd[k] * wv[e] + bv[e]);
+      uint2 w;
+      w.x = pack_bf16x2(o[0], o[1]);
+      w.y = pack_bf16x2(o[2], o[3]);
+      *reinterpret_cast<uint2*>(a.y + (r0 + k) * a.ldy + lane * 4) = w;
+    }
+  }
+}
+
 // LayerNorm of 64-wide rows without a head projection: four rows per warp at a
 // time (8 lanes per row, 8 channels per lane), so a warp keeps four rows'
 // loads in flight; statistics by 3-step shuffles within the 8 lanes.  Same
