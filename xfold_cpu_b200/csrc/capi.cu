@@ -338,8 +338,10 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
   XFB_TRY(sm_count(&sms));
   if (c == 128 && heads > 0 && mod_scale == nullptr && mod_shift == nullptr && ldx % 4 == 0 &&
       (y == nullptr || ldy % 4 == 0)) {
-    // head projection on the tensor core, 128-row tiles
-    const int blocks = static_cast<int>(std::min<int64_t>((rows + 127) / 128, int64_t(sms) * 4));
+    // head projection on the tensor core, 128-row tiles; six CTAs per SM (40
+    // registers x 256 threads, 36 KB shared memory and 32 TMEM columns each):
+    // 184 -> 158 us for the 4-head bias at N = 1024 against four
+    const int blocks = static_cast<int>(std::min<int64_t>((rows + 127) / 128, int64_t(sms) * 6));
     if (x_dtype == XFB_F32) {
       xfb::ln_heads_tc_kernel<float><<<blocks, 256, 0, st>>>(a);
     } else {
