@@ -65,6 +65,19 @@ def test_layer_norm(rows, c):
     assert _rel(got, ref) < 8e-3
 
 
+@pytest.mark.parametrize("rows,dtype", [(1001, torch.float32), (6, torch.float32),
+                                        (4099, torch.bfloat16)])
+def test_layer_norm_multirow_tails(rows, dtype):
+    """The 128-wide LayerNorm takes four rows per warp: row counts that leave a
+    partial group, fewer rows than one group's warps, and bf16 input."""
+    g = _g(12)
+    x = (torch.randn(rows, 128, generator=g) * 2 - 0.5).to(dtype)
+    w, b = _ln(g, 128)
+    ref = oracle.layer_norm(x.float(), w, b)
+    got = native.layer_norm(x.to(DEV), w.to(DEV), b.to(DEV))
+    assert _rel(got, ref) < 8e-3
+
+
 @pytest.mark.parametrize("m,k,n", [(500, 128, 512), (129, 384, 1536)])
 def test_gated_linear_unit(m, k, n):
     g = _g(3)
