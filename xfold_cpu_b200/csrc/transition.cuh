@@ -13,14 +13,15 @@
 //   epilogue  h(j) = silu(gate) * value -> bf16, 128-byte-swizzled K-major tile
 //   GEMM2(j)  acc2 (+)= h(j) W2[:, chunk j]^T      M = 128, N = 128, K = 64
 // and only the final acc2 tile leaves the SM (TMA reduce-add into the f32
-// residual, or a store).  The MMA issuer runs GEMM1(j + 1) before GEMM2(j), so
-// the tensor pipe works while the epilogue warps compute h(j); the pending
-// GEMM2 carries over into the next tile.
+// residual, or a store).  GEMM1 and GEMM2 have their own issuing threads, so
+// GEMM1(j + 1) never waits behind GEMM2(j), whose h(j) the epilogue is still
+// writing (with one issuer a clock64 trace showed the MMAs of a chunk issued one
+// after another with the tensor pipe idle in between).
 //
 // TMEM (512 columns): acc1 x 2 at columns 0 / 128, acc2 x 2 at 256 / 384.
 // Warps 0-7: epilogue (warp w: TMEM lane quarter w % 4, column half w / 4);
-// warp 8: TMA producer of x and W1; warp 9: TMEM owner and MMA issuer; warp 10:
-// TMA producer of W2.  The two weight rings have their own producers: W2(q)
+// warp 8: TMA producer of x and W1; warp 9: TMEM owner and GEMM1 issuer; warp
+// 10: TMA producer of W2; warp 11: GEMM2 issuer.  The two weight rings have their own producers: W2(q)
 // waits for GEMM2(q - 2), and a single producer would hold W1(q + 1) behind that
 // wait (a clock64 trace showed GEMM1 issued ~1000 cycles late on every chunk).
 #pragma once
@@ -30,7 +31,7 @@
 
 namespace xfb {
 
-constexpr int kFtThreads = 352;
+constexpr int kFtThreads = 384;
 constexpr int kFtEpiThreads = 256;
 
 struct FtSmem {
@@ -168,32 +169,8 @@ __global__ void __launch_bounds__(kFtThreads, 1)
   } else if (warp == 9) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
+      // GEMM1 issuer: runs ahead of the epilogue as far as the two acc1 buffers allow
       bool ok = true;
-      // the GEMM2 that waits for the epilogue of its chunk: global chunk index,
-      // its tile's iteration and whether it opens / closes that tile
-      int p_q = -1, p_t = 0;
-      bool p_first = false, p_last = false;
-      auto issue_g2 = [&]() -> bool {
-        const int s = p_q & 1;
-        const int ab = p_t & 1;
-        if ((p_first &&
-             !mbar_wait(&a2_empty[ab], ((p_t >> 1) & 1) ^ 1, kErrWaitMma, abort_flag)) ||
-            !mbar_wait(&h_full[s], (p_q >> 1) & 1, kErrWaitMma, abort_flag) ||
-            !mbar_wait(&w2_full[s], (p_q >> 1) & 1, kErrWaitMma, abort_flag))
-          return false;
-        tc_fence_after();
-        const uint32_t h_addr = smem_u32(smem + L::kHOff + s * L::kHBytes);
-        const uint32_t w2_addr = smem_u32(smem + L::kW2Off + s * L::kW2Bytes);
-        const uint32_t d = tmem_base + 256 + ab * 128;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_bf16(d, ft_desc(h_addr, k), ft_desc(w2_addr, k), kIdesc,
-                    (!p_first || k > 0) ? 1u : 0u);
-        umma_commit(&h_empty[s]);
-        umma_commit(&w2_empty[s]);
-        if (p_last) umma_commit(&a2_full[ab]);
-        return true;
-      };
       int t_it = 0, q = 0;
       for (int tile = blockIdx.x; ok && tile < m_tiles; tile += gridDim.x, ++t_it) {
         const int xb = t_it & 1;
@@ -215,17 +192,39 @@ __global__ void __launch_bounds__(kFtThreads, 1)
           umma_commit(&a1_full[s]);
           umma_commit(&w1_empty[s]);
           if (j == chunks - 1) umma_commit(&x_empty[xb]);
-          if (p_q >= 0 && !issue_g2()) {
+        }
+      }
+    }
+  } else if (warp == 11) {
+    // ------------------------------------------------ GEMM2 issuer
+    // acc2[t % 2] (+)= h(q) W2[:, chunk q]^T as soon as the epilogue wrote h(q)
+    if (lane == 0) {
+      bool ok = true;
+      int t_it = 0, q = 0;
+      for (int tile = blockIdx.x; ok && tile < m_tiles; tile += gridDim.x, ++t_it) {
+        const int ab = t_it & 1;
+        for (int j = 0; j < chunks; ++j, ++q) {
+          const int s = q & 1;
+          if ((j == 0 &&
+               !mbar_wait(&a2_empty[ab], ((t_it >> 1) & 1) ^ 1, kErrWaitMma, abort_flag)) ||
+              !mbar_wait(&h_full[s], (q >> 1) & 1, kErrWaitMma, abort_flag) ||
+              !mbar_wait(&w2_full[s], (q >> 1) & 1, kErrWaitMma, abort_flag)) {
             ok = false;
             break;
           }
-          p_q = q;
-          p_t = t_it;
-          p_first = j == 0;
-          p_last = j == chunks - 1;
+          tc_fence_after();
+          const uint32_t h_addr = smem_u32(smem + L::kHOff + s * L::kHBytes);
+          const uint32_t w2_addr = smem_u32(smem + L::kW2Off + s * L::kW2Bytes);
+          const uint32_t d = tmem_base + 256 + ab * 128;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(d, ft_desc(h_addr, k), ft_desc(w2_addr, k), kIdesc,
+                      (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&h_empty[s]);
+          umma_commit(&w2_empty[s]);
+          if (j == chunks - 1) umma_commit(&a2_full[ab]);
         }
       }
-      if (ok && p_q >= 0) issue_g2();
     }
   } else if (warp < 8) {
     // ------------------------------------------------ epilogue warps 0-7
