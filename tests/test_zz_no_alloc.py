@@ -22,6 +22,7 @@ from xfold_cpu_b200 import _capi
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-2
+MAX_WEIGHT_ELEMS = 4 * 1024 * 1024  # XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS in include/xfold_b200.h
 
 
 def _glu_workspace(x, w, n):
@@ -64,8 +65,34 @@ def test_noalloc_glu_matches_the_workspace_entry_point_on_two_calls():
     assert _capi.device_error(clear=True) == 0
 
 
+def test_noalloc_glu_matches_the_oracle_at_the_scratch_limit_and_on_empty_input():
+    """Checked against the CPU oracle on its own (not only against the
+    workspace entry point, which shares the packing and GEMM kernels), with a
+    weight that fills the scratch exactly (2 n k = the maximum) followed by a
+    call with no rows."""
+    _capi.device_error(clear=True)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    m, k, n = 260, 1024, 2048
+    assert 2 * n * k == MAX_WEIGHT_ELEMS
+    x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(2 * n, k, device="cuda", generator=g) * 0.05).bfloat16()
+    got = _glu_noalloc(x, w, n)
+    torch.cuda.synchronize()
+    ref = oracle.gated_linear_unit(x.float().cpu(), w.float().cpu().T)
+    assert oracle.relative_error(got.float().cpu(), ref) <= TOL
+    empty = _glu_noalloc(torch.zeros(0, k, dtype=torch.bfloat16, device="cuda"), w, n)
+    torch.cuda.synchronize()
+    assert empty.shape == (0, n)
+    assert _capi.device_error(clear=True) == 0
+
+
 def test_noalloc_glu_rejects_weights_beyond_the_scratch():
     x = torch.zeros(128, 1024, dtype=torch.bfloat16, device="cuda")
     w = torch.zeros(2 * 4096, 1024, dtype=torch.bfloat16, device="cuda")  # 8M elements
     with pytest.raises(ValueError, match="exceeds the fixed scratch"):
         _glu_noalloc(x, w, 4096)
+    # sizes whose product 2 n k would overflow 64 bits are rejected by the same check
+    lib = _capi.load()
+    rc = lib.xfb_gated_linear_unit_noalloc(x.data_ptr(), 128, 1 << 40, w.data_ptr(), 1 << 40,
+                                           x.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 1  # XFB_ERR_INVALID

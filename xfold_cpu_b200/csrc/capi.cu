@@ -868,6 +868,7 @@ XFB_API int xfb_gated_linear_unit(const void* x, int64_t m, int64_t k, const voi
   XFB_REQUIRE(n > 0 && n % 64 == 0, "GLU hidden width must be a positive multiple of 64");
   XFB_REQUIRE(k % 8 == 0, "GLU input width must be a multiple of 8");
   XFB_REQUIRE(aligned16(y), "GLU output must be 16-byte aligned");
+  if (m == 0) return XFB_OK;  // empty input, empty output (no tensor map of zero rows)
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bf16* w = static_cast<const bf16*>(weight);
   if (!weights_packed) {
@@ -892,23 +893,26 @@ namespace {
 static __device__ __align__(256) bf16 g_glu_noalloc_scratch[XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS];
 
 bf16* g_glu_noalloc_ptr[kMaxDevices];
-cudaError_t g_glu_noalloc_status[kMaxDevices];
-std::once_flag g_glu_noalloc_once[kMaxDevices];
+std::mutex g_glu_noalloc_mutex;
 
 // Device address of the scratch on the current device.  The host symbol is
-// only a stand-in for the device array, so the address is asked for once per
-// device (on the first call made with that device current) and kept.
+// only a stand-in for the device array, so the address is asked for on the
+// first call made with that device current and kept once the lookup has
+// succeeded.  A failed lookup (for example one made while a stream was being
+// captured) is not remembered: the next call asks again.
 int glu_noalloc_scratch(bf16** out) {
   int dev;
   XFB_TRY(current_device(&dev));
-  std::call_once(g_glu_noalloc_once[dev], [dev]() {
+  std::lock_guard<std::mutex> lock(g_glu_noalloc_mutex);
+  if (g_glu_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
-    g_glu_noalloc_status[dev] = cudaGetSymbolAddress(&p, g_glu_noalloc_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_glu_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      if (e != cudaSuccess) cudaGetLastError();  // do not leave the error for the next launch check
+      return fail(XFB_ERR_CUDA, std::string("cudaGetSymbolAddress(GLU scratch): ") +
+                                    cudaGetErrorString(e));
+    }
     g_glu_noalloc_ptr[dev] = static_cast<bf16*>(p);
-  });
-  if (g_glu_noalloc_status[dev] != cudaSuccess || g_glu_noalloc_ptr[dev] == nullptr) {
-    return fail(XFB_ERR_CUDA, std::string("cudaGetSymbolAddress(GLU scratch): ") +
-                                  cudaGetErrorString(g_glu_noalloc_status[dev]));
   }
   *out = g_glu_noalloc_ptr[dev];
   return XFB_OK;
@@ -925,14 +929,18 @@ XFB_API int xfb_gated_linear_unit_noalloc(const void* x, int64_t m, int64_t k, c
   XFB_REQUIRE(k % 8 == 0, "GLU input width must be a multiple of 8");
   XFB_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(y),
               "GLU pointers must be 16-byte aligned");
-  if (2 * n * k > XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS) {
-    char buf[200];
+  // Compared by division, so caller values near INT64_MAX cannot wrap 2*n*k
+  // into range.
+  if (k > XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS / 2 || n > XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS / (2 * k)) {
+    char buf[240];
     snprintf(buf, sizeof(buf),
-             "xfb_gated_linear_unit_noalloc: weight of 2n*k = %lld elements exceeds the fixed "
-             "scratch of %lld elements; use xfb_gated_linear_unit with a workspace",
-             (long long)(2 * n * k), (long long)XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS);
+             "xfb_gated_linear_unit_noalloc: weight of 2n*k elements (n = %lld, k = %lld) "
+             "exceeds the fixed scratch of %lld elements; use xfb_gated_linear_unit with a "
+             "workspace",
+             (long long)n, (long long)k, (long long)XFB_GLU_NOALLOC_MAX_WEIGHT_ELEMS);
     return fail(XFB_ERR_INVALID, buf);
   }
+  if (m == 0) return XFB_OK;  // nothing to write; no tensor map of zero rows
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   bf16* packed = nullptr;
   XFB_TRY(glu_noalloc_scratch(&packed));
