@@ -153,57 +153,249 @@ def _barrier(world: int):
 
 # ----------------------------------------------------------------------------- CPU baseline
 
-def cpu_baseline(sample_n: int = 256, threads: int | None = None) -> dict:
-    """Times the CPU oracle (reference torch path restated) on one block at
-    sample_n in float32 and scales it to N_TOKEN by the FLOP ratio."""
+REF_DIR = ROOT / "baseline" / "_ref"
+# The seven sub-modules of one Pairformer block, in the order of
+# xfold/nn/pairformer.py:96-112; one reference step runs one of them.
+BLOCK_PARTS = ("triangle_multiplication_outgoing", "triangle_multiplication_incoming",
+               "pair_attention1", "pair_attention2", "pair_transition", "single_attention",
+               "single_transition")
+
+
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def _reference_parts(n: int):
+    """The block's seven sub-module calls on the reference's CPU path, with
+    the C4 weights (block 0: init seed 3000) and inputs (seed 3).
+
+    Preferred: the reference's own torch modules (xfold.nn.pairformer
+    PairformerBlock, installed unmodified in baseline/_ref) under CPU bf16
+    autocast, as its ModelRunner runs them (run_alphafold.py:466-472); the
+    weights are copied in with load_state_dict (same parameter names).  If
+    baseline/_ref is absent: the CPU oracle (a restatement of the same torch
+    path) under the same autocast.  Returns (kind, callables, inputs)."""
+    import torch
+
+    from xfold_cpu_b200.nn import PairformerBlock, init_params_
+
+    ours = PairformerBlock(c_pair=C_PAIR, c_single=C_SINGLE)
+    init_params_(ours, seed=SEED * 1000)
+    pair, pair_mask, single, seq_mask = _inputs(n, SEED)
+    if (REF_DIR / "xfold").is_dir():
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        from xfold.nn.pairformer import PairformerBlock as RefBlock
+
+        ref = RefBlock(c_pair=C_PAIR, c_single=C_SINGLE).eval()
+        ref.load_state_dict(ours.state_dict(), strict=True)
+
+        def single_attention():
+            logits = ref.single_pair_logits_projection(ref.single_pair_logits_norm(pair))
+            single.add_(ref.single_attention_(single, seq_mask, pair_logits=logits.permute(2, 0, 1)))
+
+        parts = {
+            "triangle_multiplication_outgoing":
+                lambda: pair.add_(ref.triangle_multiplication_outgoing(pair, mask=pair_mask)),
+            "triangle_multiplication_incoming":
+                lambda: pair.add_(ref.triangle_multiplication_incoming(pair, mask=pair_mask)),
+            "pair_attention1": lambda: pair.add_(ref.pair_attention1(pair, mask=pair_mask)),
+            "pair_attention2": lambda: pair.add_(ref.pair_attention2(pair, mask=pair_mask)),
+            "pair_transition": lambda: pair.add_(ref.pair_transition(pair)),
+            "single_attention": single_attention,
+            "single_transition": lambda: single.add_(ref.single_transition(single)),
+        }
+        return "reference", parts
+    import oracle
+
+    params = {k: v.detach().clone() for k, v in ours.state_dict().items()}
+    parts = {
+        "triangle_multiplication_outgoing": lambda: pair.add_(oracle.triangle_multiplication(
+            pair, pair_mask, params, True, "triangle_multiplication_outgoing.")),
+        "triangle_multiplication_incoming": lambda: pair.add_(oracle.triangle_multiplication(
+            pair, pair_mask, params, False, "triangle_multiplication_incoming.")),
+        "pair_attention1": lambda: pair.add_(oracle.grid_self_attention(
+            pair, pair_mask, params, False, 4, "pair_attention1.")),
+        "pair_attention2": lambda: pair.add_(oracle.grid_self_attention(
+            pair, pair_mask, params, True, 4, "pair_attention2.")),
+        "pair_transition": lambda: pair.add_(oracle.transition(pair, params, "pair_transition.")),
+        "single_attention": lambda: single.add_(oracle.self_attention(
+            single, seq_mask, oracle.pair_logits(pair, params), params, None, 16, False,
+            "single_attention_.")),
+        "single_transition": lambda: single.add_(oracle.transition(single, params,
+                                                                   "single_transition.")),
+    }
+    return "port", parts
+
+
+def _time_parts(parts: dict, order: list[str]) -> dict:
+    """Runs the named sub-modules in order under CPU bf16 autocast; returns
+    {name: [seconds, ...]}."""
+    import torch
+
+    times: dict[str, list[float]] = {}
+    with torch.inference_mode(), torch.amp.autocast("cpu", dtype=torch.bfloat16):
+        for name in order:
+            t0 = time.perf_counter()
+            parts[name]()
+            times.setdefault(name, []).append(time.perf_counter() - t0)
+    return times
+
+
+def cpu_baseline(threads: int | None = None) -> dict:
+    """One Pairformer block at N = 1024 (C4, bf16 autocast) on the reference's
+    CPU path, timed sub-module by sub-module on this host's cores (about
+    10-30 s of CPU work): ms per block = the sum of the seven calls."""
+    import torch
+
+    torch.set_num_threads(threads or _host_threads())
+    kind, parts = _reference_parts(N_TOKEN)
+    times = _time_parts(parts, list(BLOCK_PARTS))
+    per = {k: round(v[0] * 1e3, 1) for k, v in times.items()}
+    total = sum(v[0] for v in times.values())
+    who = ("the reference's own torch modules (xfold.nn.pairformer, baseline/_ref)"
+           if kind == "reference" else "the CPU oracle (restated reference torch path)")
+    return {"value": round(total * 1e3, 1), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": kind, "per_part_ms": per,
+            "sample": (f"1 Pairformer block at N={N_TOKEN} (C4 weights and inputs) under CPU bf16 "
+                       f"autocast, {who}, its 7 sub-modules timed once each ({total:.1f} s); "
+                       f"measured, not extrapolated")}
+
+
+PARITY_TOL = 1e-2
+
+
+def block_parity(dev, blk) -> dict:
+    """Sampled-row parity of one C4 block at N = 1024 against the CPU oracle:
+    each pair update (both triangle multiplications, both triangle attentions,
+    the transition) is compared on seven sampled rows with the oracle applied
+    to the same input, the single track in full; max |got - ref| / max |ref|
+    per update (the bf16 bar is 1e-2).  Checker only: runs after the timed
+    regions."""
     import torch
 
     import oracle
-    from xfold_cpu_b200.nn import PairformerBlock, init_params_
 
-    if threads:
-        torch.set_num_threads(threads)
-    cores = torch.get_num_threads()
-    block = PairformerBlock(c_pair=C_PAIR, c_single=C_SINGLE)
-    init_params_(block, seed=SEED)
-    params = {k: v.detach().clone() for k, v in block.state_dict().items()}
-    pair, pair_mask, single, seq_mask = _inputs(sample_n, SEED)
+    n = N_TOKEN
+    pair_h, pair_mask_h, single_h, seq_h = _inputs(n, SEED)
+    params = {k: v.detach().float().cpu() for k, v in blk.state_dict().items()}
+    rows = sorted({0, 1, n // 3, n // 2 + 7, n - 65, n - 64, n - 1})
+    pair, pair_mask = pair_h.to(dev), pair_mask_h.to(dev)
+    single, seq_mask = single_h.to(dev), seq_h.to(dev)
+    err = {}
+    ref_bf16 = None
+    if (REF_DIR / "xfold").is_dir():
+        # the reference's own bf16 autocast path on the same first input, for scale
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        from xfold.nn.pairformer import PairformerBlock as RefBlock
+        ref_blk = RefBlock(c_pair=C_PAIR, c_single=C_SINGLE).eval()
+        ref_blk.load_state_dict({k: v.float().cpu() for k, v in blk.state_dict().items()},
+                                strict=True)
+        with torch.inference_mode():
+            want = oracle.triangle_multiplication_rows(pair_h, pair_mask_h, params, True, rows,
+                                                       "triangle_multiplication_outgoing.")
+            with torch.amp.autocast("cpu", dtype=torch.bfloat16):
+                got_ref = ref_blk.triangle_multiplication_outgoing(pair_h, mask=pair_mask_h)
+            ref_bf16 = {"triangle_multiplication_outgoing":
+                        round(oracle.relative_error(got_ref[rows].float(), want), 5)}
+        del ref_blk, got_ref
     with torch.inference_mode():
-        oracle.pairformer_block(pair, pair_mask, single, seq_mask, params)  # warm-up
-        t0 = time.perf_counter()
-        oracle.pairformer_block(pair, pair_mask, single, seq_mask, params)
-        dt = time.perf_counter() - t0
-    scale = (oracle.pairformer_block_flops(N_TOKEN)["total"]
-             / oracle.pairformer_block_flops(sample_n)["total"])
-    return {"value": dt * scale * 1e3, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": (f"1 Pairformer block at N={sample_n} fp32 (torch CPU oracle of the "
-                       f"reference torch path), {dt:.2f} s, scaled x{scale:.1f} by FLOPs to N={N_TOKEN}")}
+        for name, transpose, ref_fn in (
+            ("triangle_multiplication_outgoing", False, lambda x: oracle.triangle_multiplication_rows(
+                x, pair_mask_h, params, True, rows, "triangle_multiplication_outgoing.")),
+            ("triangle_multiplication_incoming", False, lambda x: oracle.triangle_multiplication_rows(
+                x, pair_mask_h, params, False, rows, "triangle_multiplication_incoming.")),
+            ("pair_attention1", False, lambda x: oracle.grid_self_attention_rows(
+                x, pair_mask_h, params, False, rows, 4, "pair_attention1.")),
+            ("pair_attention2", True, lambda x: oracle.grid_self_attention_rows(
+                x, pair_mask_h, params, True, rows, 4, "pair_attention2.")),
+            ("pair_transition", False, lambda x: oracle.transition(x[rows], params,
+                                                                   "pair_transition.")),
+        ):
+            before = pair.clone()
+            mod = getattr(blk, name)
+            if name == "pair_transition":
+                mod.accumulate_(pair)
+            else:
+                mod.accumulate_(pair, pair_mask)
+            upd = pair - before
+            got = (upd[:, rows].permute(1, 0, 2) if transpose else upd[rows]).float().cpu()
+            del upd
+            err[name] = oracle.relative_error(got, ref_fn(before.cpu()))
+            del before
+        norm = blk.single_pair_logits_norm
+        from xfold_cpu_b200 import native
+
+        logits = native.pair_logits(pair, norm.weight, norm.bias, norm.eps,
+                                     blk.single_pair_logits_projection.weight.bfloat16())
+        s0 = single.clone()
+        blk.single_attention_.accumulate_(single, seq_mask, logits)
+        ref_logits = oracle.pair_logits(pair.cpu(), params)
+        err["single_attention"] = oracle.relative_error(
+            (single - s0).cpu(), oracle.self_attention(s0.cpu(), seq_h, ref_logits, params, None,
+                                                       16, False, "single_attention_."))
+        s1 = single.clone()
+        blk.single_transition.accumulate_(single)
+        err["single_transition"] = oracle.relative_error(
+            (single - s1).cpu(), oracle.transition(s1.cpu(), params, "single_transition."))
+    worst = max(err.values())
+    return {"max_rel_err": round(worst, 5), "tolerance": PARITY_TOL, "ok": worst <= PARITY_TOL,
+            "per_update": {k: round(v, 5) for k, v in err.items()}, "rows": rows,
+            "reference_bf16_per_update": ref_bf16,
+            "what": "block 0 at N=1024 (C4), each update vs the CPU oracle on the same input, "
+                    "sampled pair rows, single track in full"}
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's CPU path on C4's workload.  One step
+    is one of the block's seven sub-modules at full size (N = 1024), taken in
+    rotation, so a run of K steps covers K / 7 blocks; the value (ms per block)
+    is the sum over the seven sub-modules of each one's mean time over the
+    timed steps, plus the warm-up steps for any sub-module the timed steps did
+    not reach (K < 7)."""
     world, rank, _ = _dist()
     if rank != 0:
         return
     import torch
 
-    threads = os.cpu_count() or 1
+    threads = _host_threads()
     torch.set_num_threads(threads)
-    samples = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(sample_n=256, threads=threads)
-        if i >= args.warmup:
-            samples.append(r["value"])
-    value = sum(samples) / len(samples)
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value * N_BLOCKS,
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": "48-block Pairformer trunk, N_token=1024 (sampled)",
+    kind, parts = _reference_parts(N_TOKEN)
+    order = [BLOCK_PARTS[i % len(BLOCK_PARTS)] for i in range(args.warmup + args.steps)]
+    warm = _time_parts(parts, order[:args.warmup])
+    t0 = time.perf_counter()
+    timed = _time_parts(parts, order[args.warmup:])
+    wall = time.perf_counter() - t0
+    per = {}
+    for name in BLOCK_PARTS:
+        src = timed.get(name) or warm.get(name)
+        per[name] = sum(src) / len(src) if src else None
+    if any(v is None for v in per.values()):  # K + W < 7: time the rest once
+        rest = [k for k, v in per.items() if v is None]
+        for k, v in _time_parts(parts, rest).items():
+            per[k] = v[0]
+    value = sum(per.values()) * 1e3
+    who = ("the reference's own torch modules (xfold.nn.pairformer from baseline/_ref)"
+           if kind == "reference" else "the CPU oracle (restated reference torch path)")
+    sample = (f"one step = one of the block's 7 sub-modules at N={N_TOKEN} in rotation under CPU "
+              f"bf16 autocast, {who}; value = sum of the sub-modules' mean times")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(wall / max(args.steps, 1) * 1e3, 1),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) pair/single, random-init N(0,0.02) weights)",
+            "config": {"workload": "48-block Pairformer trunk, N_token=1024 (BASELINE config C4)",
                        "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR,
-                       "c_single": C_SINGLE, "seed": SEED},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": r["sample"]},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                       "c_single": C_SINGLE, "heads_pair": 4, "heads_single": 16, "seed": SEED,
+                       "mask": "64-token padded tail", "parallelism": "host CPU"},
+            "per_part_ms": {k: round(v * 1e3, 1) for k, v in per.items()},
+            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads,
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -226,11 +418,16 @@ def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
     from xfold_cpu_b200 import native
 
     n, c, heads, d = N_TOKEN, C_PAIR, 4, 32
+    log2e = 1.4426950408889634
     g = torch.Generator(device=dev).manual_seed(11)
-    q = (torch.randn(n, heads, n, d, device=dev, generator=g) * 0.2).bfloat16()
-    k = (torch.randn(n, heads, n, d, device=dev, generator=g) * 0.2).bfloat16()
+    # the operands of the block's triangle attention: q carries log2(e)/sqrt(d),
+    # the bias log2(e) (scores in base-2 units), the gate is already squashed
+    q = (torch.randn(n, heads, n, d, device=dev, generator=g) * (log2e / d ** 0.5)).bfloat16()
+    k = torch.randn(n, heads, n, d, device=dev, generator=g).bfloat16()
     v = torch.randn(n, heads, n, d, device=dev, generator=g).bfloat16()
-    bias = torch.randn(heads, n, n, device=dev, generator=g).bfloat16()
+    bias = (torch.randn(heads, n, n, device=dev, generator=g) * log2e).bfloat16()
+    gate = torch.rand(n, n, c, device=dev, generator=g).bfloat16()
+    att_out = torch.empty(n, n, c, device=dev, dtype=torch.bfloat16)
     seq = torch.ones(n, device=dev)
     seq[-64:] = 0
     mask = seq[:, None] * seq[None, :]
@@ -239,7 +436,7 @@ def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
     stream = torch.cuda.current_stream(dev)
     results = {}
     for name, fn, flops in (
-        ("flash_attn", lambda: native.dot_product_attention(q, k, v, mask, bias, q_pre_scaled=True),
+        ("flash_attn", lambda: native.grid_attention_core(q, k, v, mask, bias, gate, att_out),
          4.0 * heads * n ** 3 * d),
         ("triangle_contraction", lambda: native.gemm(a, b, out_dtype=torch.bfloat16),
          2.0 * c * n ** 3),
@@ -264,7 +461,7 @@ def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:
                          "traffic": TRAFFIC_BYTES[name],
                          "ms_per_launch": round(t * 1e3, 4),
                          "flops_per_launch": flops}
-    del q, k, v, bias, a, b
+    del q, k, v, bias, gate, att_out, a, b
     return results
 
 
@@ -713,7 +910,8 @@ def run_cuda(args) -> None:
 
     if rank != 0:
         return
-    base = cpu_baseline(sample_n=256) if world == 1 else None
+    base = cpu_baseline() if world == 1 else None
+    parity = block_parity(dev, blocks[0]) if world == 1 and n_tok == N_TOKEN else None
     if atom is not None:
         atom["cpu_port"] = cpu_baseline_atom()
     if evo is not None:
@@ -750,6 +948,7 @@ def run_cuda(args) -> None:
         "clocks": clocks,
         "cpu_baseline": base,
         "finite": finite,
+        "parity": parity,
         "extras": ({"diffusion_transformer_c5": c5, "atom_transformer_c5": atom,
                     "evoformer_block": evo} if c5 else None),
     }

@@ -304,6 +304,24 @@ XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int6
                                     int out_dtype, int accumulate, void* workspace,
                                     int64_t workspace_bytes, void* stream);
 
+/* Grid attention core (the softmax(q k^T + bias, mask) v, gated, of
+ * xfold/nn/attention.py:61-78 for head dim 32), the kernel between the input
+ * projections and the output projection of stage 2, for callers that hold the
+ * projected operands:
+ *   q, k, v [rows][heads][n][32] bf16, q already multiplied by
+ *     log2(e) / sqrt(32) (scores in base-2 units); bias [heads][n][n] bf16 in
+ *     base-2 units (multiplied by log2(e)), shared by every row;
+ *   mask [rows][n] f32 key mask (0 = masked: logit -1e9) or null;
+ *   gate [rows][n][heads*32] bf16 (already passed through sigmoid) or null;
+ *   out [rows][n][heads*32] bf16 = gate * attention output.
+ * n % 8 == 0.  No counterpart in the reference (it is one of this library's
+ * row-block stages). */
+XFB_API int64_t xfb_grid_attention_core_workspace(int64_t rows, int64_t n);
+XFB_API int xfb_grid_attention_core(const void* q, const void* k, const void* v, int64_t rows,
+                                    int64_t heads, int64_t n, const float* mask, const void* bias,
+                                    const void* gate, void* out, void* workspace,
+                                    int64_t workspace_bytes, void* stream);
+
 /* Pair-logit projection (pairformer.py:103-106) of a row block:
  * logits [heads][rows][n] bf16. */
 XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows, int64_t n,

@@ -142,6 +142,92 @@ def grid_self_attention(pair, mask, params, transpose, num_head=4, prefix="", ba
     return out
 
 
+def _projected_channels(pair, mask, params, prefix, row_slice):
+    """Rows `row_slice` of the masked, gated projection of
+    triangle_multiplication (xfold/nn/triangle_multiplication.py:81-95):
+    returns (a, b) as [c, rows, N] with a = channel 2c', b = channel 2c'+1."""
+    P = lambda n: _p(params, prefix, n)
+    x = layer_norm(pair[row_slice], P("left_norm_input.weight"), P("left_norm_input.bias"))
+    proj = linear(x, P("projection.weight")).permute(2, 0, 1)
+    if mask is not None:
+        proj = proj * mask[row_slice][None, ...]
+    proj = proj * torch.sigmoid(linear(x, P("gate.weight")).permute(2, 0, 1))
+    c = pair.shape[-1]
+    proj = proj.reshape(c, 2, *proj.shape[1:])
+    return proj[:, 0], proj[:, 1]
+
+
+def triangle_multiplication_rows(pair, mask, params, outgoing, rows, prefix="", chunk=128):
+    """triangle_multiplication (above; xfold/nn/triangle_multiplication.py:71-105)
+    evaluated only for the output rows `rows` (a list of indices i): returns
+    update[rows] as [len(rows), N, c].  The projection of the whole pair is
+    needed (all of b for outgoing, all of a for incoming) and is formed in
+    slices of `chunk` pair rows; the contraction, centre LayerNorm, output
+    projection and gate run for the selected rows only.  Same operations in
+    the same order as the full function, so large pairs can be checked on a
+    sample of rows."""
+    P = lambda n: _p(params, prefix, n)
+    n, _, c = pair.shape
+    rows = list(rows)
+    full = torch.empty(c, n, n, dtype=torch.float32)  # b (outgoing) or a (incoming)
+    # outgoing: rows i of a, a[c, i, k]; incoming: columns i of b, b[c, k, i]
+    sel = torch.empty(c, len(rows), n) if outgoing else torch.empty(c, n, len(rows))
+    for r0 in range(0, n, chunk):
+        r1 = min(n, r0 + chunk)
+        a, b = _projected_channels(pair, mask, params, prefix, slice(r0, r1))
+        full[:, r0:r1] = b if outgoing else a
+        if outgoing:
+            for s, i in enumerate(rows):
+                if r0 <= i < r1:
+                    sel[:, s] = a[:, i - r0]
+        else:
+            sel[:, r0:r1] = b[:, :, rows]
+    if outgoing:
+        z = torch.einsum("cik,cjk->cij", sel, full)
+    else:
+        z = torch.einsum("ckj,cki->cij", full, sel)
+    z = z.permute(1, 2, 0)  # [R, N, c]
+    z = layer_norm(z, P("center_norm.weight"), P("center_norm.bias"))
+    z = linear(z, P("output_projection.weight"))
+    x_rows = layer_norm(pair[rows], P("left_norm_input.weight"), P("left_norm_input.bias"))
+    return z * torch.sigmoid(linear(x_rows, P("gating_linear.weight")))
+
+
+def grid_self_attention_rows(pair, mask, params, transpose, rows, num_head=4, prefix="",
+                             chunk=128):
+    """grid_self_attention (above; xfold/nn/attention.py:61-105) evaluated only
+    for the batch rows `rows`: pair rows i for the starting node (returns
+    update[rows] as [R, N, c]) or pair columns j for the ending node (returns
+    update[:, rows] transposed, i.e. [R, N, c] with element [r, i] = update[i,
+    rows[r]]).  The bias of the whole pair (projected before the transpose,
+    :87-98) is formed in slices of `chunk` rows; the key mask of batch row b is
+    pair_mask[b] in both directions (:100)."""
+    P = lambda n: _p(params, prefix, n)
+    n, _, c = pair.shape
+    d = c // num_head
+    bias = torch.empty(num_head, n, n, dtype=torch.float32)
+    for r0 in range(0, n, chunk):
+        xs = layer_norm(pair[r0:r0 + chunk], P("act_norm.weight"), P("act_norm.bias"))
+        bias[:, r0:r0 + xs.shape[0]] = linear(xs, P("pair_bias_projection.weight")).permute(2, 0, 1)
+    outs = []
+    for r in rows:
+        src = pair[:, r] if transpose else pair[r]  # [N tokens, c]
+        x = layer_norm(src, P("act_norm.weight"), P("act_norm.bias"))
+
+        def heads(t):
+            return t.reshape(1, n, num_head, d).permute(0, 2, 1, 3)
+
+        q = heads(linear(x, P("q_projection.weight")))
+        k = heads(linear(x, P("k_projection.weight")))
+        v = heads(linear(x, P("v_projection.weight")))
+        m = None if mask is None else mask[r:r + 1]
+        o = dot_product_attention(q, k, v, mask=m, bias=bias)
+        o = o.permute(0, 2, 1, 3).reshape(n, c)
+        o = o * torch.sigmoid(linear(x, P("gating_query.weight")))
+        outs.append(linear(o, P("output_projection.weight")))
+    return torch.stack(outs, dim=0)
+
+
 def transition(x, params, prefix=""):
     """Transition.forward (xfold/nn/primitives.py:33-37): LN -> GLU with
     transition1.weight.T -> transition2."""

@@ -197,3 +197,33 @@ def test_evoformer_block():
     check(pair, o["pair"], 1e-5)
     check(o["bf16:msa"] - i["msa"], msa - i["msa"], BF16_TOL)
     check(o["bf16:pair"] - i["pair"], pair - i["pair"], BF16_TOL)
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_sampled_row_triangle_multiplication_equals_the_full_restatement(outgoing):
+    """oracle.triangle_multiplication_rows (used by the large-N GPU parity
+    tests) gives the rows of oracle.triangle_multiplication, which the golden
+    fixtures pin, up to float32 summation order (matrix products of other
+    shapes); checked on the fixture's inputs."""
+    name = "triangle_outgoing" if outgoing else "triangle_incoming"
+    p, i, o = load(name)
+    n = i["pair"].shape[0]
+    rows = sorted({0, n // 2, n - 1})
+    got = oracle.triangle_multiplication_rows(i["pair"], i["mask"], p, outgoing, rows, chunk=5)
+    full = oracle.triangle_multiplication(i["pair"], i["mask"], p, outgoing)
+    assert oracle.relative_error(got, full[rows]) < 1e-6
+    check(got, o["update"][rows], FP32_TOL)
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+def test_sampled_row_grid_attention_equals_the_full_restatement(transpose):
+    name = "grid_attention_ending" if transpose else "grid_attention_starting"
+    p, i, o = load(name)
+    n = i["pair"].shape[0]
+    rows = sorted({0, n // 2, n - 1})
+    got = oracle.grid_self_attention_rows(i["pair"], i["mask"], p, transpose, rows, 4, chunk=7)
+    full = oracle.grid_self_attention(i["pair"], i["mask"], p, transpose, 4)
+    want = full[:, rows].permute(1, 0, 2) if transpose else full[rows]
+    assert oracle.relative_error(got, want) < 1e-6
+    ref = o["update"][:, rows].permute(1, 0, 2) if transpose else o["update"][rows]
+    check(got, ref, FP32_TOL)

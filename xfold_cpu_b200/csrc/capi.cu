@@ -681,15 +681,21 @@ bool use_flash_tri(const xfb::AttnArgs& args) {
 // (row stride nk with nk % 8 == 0, contiguous heads, 16-byte aligned), else
 // per-thread global loads.  `pre`: q and the bias already carry log2(e)
 // (only the TMA bias path takes pre-scaled inputs).
+//
+// `exact_bias`: the bias is the caller's (any values, -inf and NaN included) and
+// is added in f32 by the softmax warps.  The TMA path lets the bias enter the
+// accumulator through MMAs against an identity tile, where a non-finite bias
+// value times the identity's zeros would turn its 15 neighbouring scores into
+// NaN; it is used for biases this library computes (finite projections).
 int run_flash(int dp, int bias_dtype, bool pre, const bf16* q, const bf16* k, const bf16* v,
-              const xfb::AttnArgs& args, cudaStream_t st) {
+              const xfb::AttnArgs& args, cudaStream_t st, bool exact_bias = false) {
   XFB_REQUIRE(static_cast<int64_t>(args.B) * args.H * ((args.nq + 127) / 128) < (1ll << 31),
               "attention has too many work items");
   int mode = xfb::kBiasGlobalBf16;
   if (args.bias != nullptr) {
     if (bias_dtype == XFB_F32) {
       mode = xfb::kBiasGlobalF32;
-    } else if (args.bias_sq == args.nk && args.nk % 8 == 0 && aligned16(args.bias) &&
+    } else if (!exact_bias && args.bias_sq == args.nk && args.nk % 8 == 0 && aligned16(args.bias) &&
                (args.bias_sh * 2) % 16 == 0 &&
                (!args.bias_batched || args.bias_sb == args.H * args.bias_sh)) {
       mode = xfb::kBiasTma;
@@ -1209,7 +1215,7 @@ XFB_API int xfb_dot_product_attention(const void* q, const void* k, const void* 
   a.gate = nullptr;
   a.gate_sb = a.gate_sh = a.gate_sq = 0;
   a.bias_batched = bias_batched;
-  return run_flash(dp, bias_dtype, false, qq, kk, vv, a, st);
+  return run_flash(dp, bias_dtype, false, qq, kk, vv, a, st, /*exact_bias=*/true);
 }
 
 XFB_API int64_t xfb_pack_attention_weights_bytes(int64_t c) { return 4 * c * c * 2; }
@@ -1836,6 +1842,55 @@ XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int6
   XFB_TRY(run_flash(dp, XFB_BF16, pre, w.q, w.k, w.v, a, st));
   return linear_core(w.o, rows * n, c, c, static_cast<const bf16*>(output_w), c, nullptr, nullptr,
                      0, out, out_dtype == XFB_F32, accumulate, c, st);
+}
+
+XFB_API int64_t xfb_grid_attention_core_workspace(int64_t rows, int64_t n) {
+  Carver cv{nullptr, 0, 0};
+  cv.take<uint32_t>(rows * mask_words(n));
+  return cv.used;
+}
+
+XFB_API int xfb_grid_attention_core(const void* q, const void* k, const void* v, int64_t rows,
+                                    int64_t heads, int64_t n, const float* mask, const void* bias,
+                                    const void* gate, void* out, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
+  XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "the attention core needs n % 8 == 0 tokens");
+  XFB_REQUIRE(heads > 0 && heads <= 16, "heads must be in 1..16");
+  XFB_REQUIRE(q && k && v && bias && out, "q, k, v, bias and out are required");
+  if (rows == 0 || n == 0) return XFB_OK;
+  XFB_REQUIRE(n <= 16384 && rows * n <= (1ll << 31) - 256, "row block too large");
+  XFB_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(bias) && aligned16(out) &&
+                  aligned16(gate),
+              "attention core tensors must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  uint32_t* bits = mask ? cv.take<uint32_t>(rows * mask_words(n)) : nullptr;
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  const int64_t c = heads * 32;
+  xfb::AttnArgs a;
+  a.B = static_cast<int>(rows);
+  a.H = static_cast<int>(heads);
+  a.nq = static_cast<int>(n);
+  a.nk = static_cast<int>(n);
+  a.d = 32;
+  if (mask != nullptr) XFB_TRY(launch_mask_bits(mask, true, rows, n, n, bits, st));
+  a.mask_bits = bits;
+  a.mask_sb = mask_words(n);
+  a.bias = bias;
+  a.bias_sb = 0;
+  a.bias_sh = n * n;
+  a.bias_sq = n;
+  a.bias_batched = 0;
+  a.out = static_cast<bf16*>(out);
+  a.out_sb = n * c;
+  a.out_sh = 32;
+  a.out_sq = c;
+  a.gate = static_cast<const bf16*>(gate);
+  a.gate_sb = a.out_sb;
+  a.gate_sh = a.out_sh;
+  a.gate_sq = a.out_sq;
+  return run_flash(32, XFB_BF16, true, static_cast<const bf16*>(q), static_cast<const bf16*>(k),
+                   static_cast<const bf16*>(v), a, st);
 }
 
 XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows, int64_t n,

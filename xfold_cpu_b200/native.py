@@ -511,6 +511,33 @@ def grid_attention_rows(x: torch.Tensor, mask: torch.Tensor | None, bias: torch.
     return out
 
 
+def grid_attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                        mask: torch.Tensor | None, bias: torch.Tensor,
+                        gate: torch.Tensor | None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The attention kernel of grid attention stage 2 alone (attention.py:61-78):
+    q, k, v [rows, heads, n, 32] bf16 with q carrying log2(e)/sqrt(32), bias
+    [heads, n, n] bf16 in base-2 units, mask [rows, n] key mask or None, gate
+    [rows, n, heads*32] bf16 (sigmoid applied) or None; returns out [rows, n,
+    heads*32] bf16."""
+    device = _check_cuda(q, k, v, mask, bias, gate, out)
+    rows, heads, n, d = q.shape
+    if d != 32 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("the attention core takes q, k, v [rows, heads, n, 32]")
+    if bias.shape != (heads, n, n):
+        raise ValueError("bias must be [heads, n, n]")
+    q, k, v, bias = (_contig(t, torch.bfloat16) for t in (q, k, v, bias))
+    if mask is not None:
+        mask = _contig(mask.expand(rows, n), torch.float32)
+    if gate is not None:
+        gate = _contig(gate, torch.bfloat16)
+    if out is None:
+        out = torch.empty((rows, n, heads * 32), dtype=torch.bfloat16, device=device)
+    ws = _workspace(_capi.load().xfb_grid_attention_core_workspace(rows, n), device)
+    _capi.call("xfb_grid_attention_core", _ptr(q), _ptr(k), _ptr(v), rows, heads, n, _ptr(mask),
+               _ptr(bias), _ptr(gate), _ptr(out), _ptr(ws), ws.numel(), _stream(device))
+    return out
+
+
 def pair_logits_rows(pair: torch.Tensor, norm_weight: torch.Tensor | None,
                      norm_bias: torch.Tensor | None, eps: float,
                      weight: torch.Tensor) -> torch.Tensor:
