@@ -374,42 +374,59 @@ __global__ void __launch_bounds__(kTriThreads, 1)
         ok = mbar_wait(&tb.s_full[buf], (g >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
         tc_fence_after();
         float s[kAttnBK];
-        tmem_ld32_to(t_row + buf * kAttnBK, s);
-        tmem_ld32_to(t_row + buf * kAttnBK + 32, s + 32);
-        tmem_wait_ld();
         float2* s2 = reinterpret_cast<float2*>(s);
-        if (!kTriBiasMma) {
+        // S of this tile from TMEM, with the bias (softmax-side variant) and the
+        // key mask applied: masked -> -1e9, past the end -> -inf
+        auto load_scores = [&]() {
+          tmem_ld32_to(t_row + buf * kAttnBK, s);
+          tmem_ld32_to(t_row + buf * kAttnBK + 32, s + 32);
+          tmem_wait_ld();
+          if (!kTriBiasMma) {
 #pragma unroll
-          for (int c = 0; c < kAttnBK / 8; ++c) {
-            const uint32_t ww[4] = {bw[c].x, bw[c].y, bw[c].z, bw[c].w};
+            for (int c = 0; c < kAttnBK / 8; ++c) {
+              const uint32_t ww[4] = {bw[c].x, bw[c].y, bw[c].z, bw[c].w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              s2[c * 4 + e] = add2(s2[c * 4 + e], make_float2(__uint_as_float(ww[e] << 16),
-                                                              __uint_as_float(ww[e] & 0xFFFF0000u)));
-          }
-        }
-        // ---- key mask: masked -> -1e9, past the end -> -inf
-        if (key0 + kAttnBK > args.nk || (w0 & w1) != 0xFFFFFFFFu) {
-#pragma unroll
-          for (int j = 0; j < kAttnBK; ++j) {
-            const uint32_t bit = ((j < 32 ? w0 : w1) >> (j & 31)) & 1u;
-            if (key0 + j >= args.nk) {
-              s[j] = -INFINITY;
-            } else if (!bit) {
-              s[j] = kMasked;
+              for (int e = 0; e < 4; ++e)
+                s2[c * 4 + e] = add2(s2[c * 4 + e],
+                                     make_float2(__uint_as_float(ww[e] << 16),
+                                                 __uint_as_float(ww[e] & 0xFFFF0000u)));
             }
           }
-        }
-        // ---- tile max and lazy reference update (a NaN max always "grows")
-        const float mt = tile_max64(s) * kScale;
-        const bool grow = !(mt <= m_ref + 8.f);
-        float factor = 1.f;
-        if (grow) {
-          factor = ex2_approx(m_ref - mt);  // 0 when m_ref = -inf
-          m_ref = mt;
-        }
-        if (t > 0 && __any_sync(0xffffffffu, grow)) {
-          // O holds earlier tiles of this item: rescale it once PV(g - 1) is done
+          if (key0 + kAttnBK > args.nk || (w0 & w1) != 0xFFFFFFFFu) {
+#pragma unroll
+            for (int j = 0; j < kAttnBK; ++j) {
+              const uint32_t bit = ((j < 32 ? w0 : w1) >> (j & 31)) & 1u;
+              if (key0 + j >= args.nk) {
+                s[j] = -INFINITY;
+              } else if (!bit) {
+                s[j] = kMasked;
+              }
+            }
+          }
+        };
+        load_scores();
+        uint32_t pk[kAttnBK / 2];
+        // probabilities 2^(s * kScale - m) of this tile into pk, their f32 sum into ts
+        float2 ts[4];
+        auto exponentiate = [&](float m) {
+          const float2 neg = make_float2(-m, -m);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ts[i] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int j = 0; j < kAttnBK / 2; ++j) {
+            float2 x = fma2(s2[j], scale2, neg);
+            if ((j & 7) < kTriPolyPairs) {
+              x = exp2_poly2(x);
+            } else {
+              x.x = ex2_approx(x.x);
+              x.y = ex2_approx(x.y);
+            }
+            ts[j & 3] = add2(ts[j & 3], x);
+            pk[j] = pack_bf16x2(x.x, x.y);
+          }
+        };
+        // rescales O (earlier tiles of this item) by `factor` once PV(g - 1) is done
+        auto rescale_o = [&](float factor) {
           const int gp = g - 1;
           ok = mbar_wait(&tb.pv_done[gp & 1], (gp >> 1) & 1, kErrWaitSoftmax, abort_flag) && ok;
           tc_fence_after();
@@ -425,24 +442,21 @@ __global__ void __launch_bounds__(kTriThreads, 1)
             lsum[i].x *= factor;
             lsum[i].y *= factor;
           }
-        }
-        // ---- probabilities 2^(s * kScale - m_ref), row sum in f32, P as bf16 pairs
-        uint32_t pk[kAttnBK / 2];
+        };
+        // ---- tile max and lazy reference update (a NaN max always "grows")
         {
-          const float2 neg = make_float2(-m_ref, -m_ref);
-#pragma unroll
-          for (int j = 0; j < kAttnBK / 2; ++j) {
-            float2 x = fma2(s2[j], scale2, neg);
-            if ((j & 7) < kTriPolyPairs) {
-              x = exp2_poly2(x);
-            } else {
-              x.x = ex2_approx(x.x);
-              x.y = ex2_approx(x.y);
-            }
-            lsum[j & 3] = add2(lsum[j & 3], x);
-            pk[j] = pack_bf16x2(x.x, x.y);
+          const float mt = tile_max64(s) * kScale;
+          const bool grow = !(mt <= m_ref + 8.f);
+          float factor = 1.f;
+          if (grow) {
+            factor = ex2_approx(m_ref - mt);  // 0 when m_ref = -inf
+            m_ref = mt;
           }
+          if (t > 0 && __any_sync(0xffffffffu, grow)) rescale_o(factor);
+          exponentiate(m_ref);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) lsum[i] = add2(lsum[i], ts[i]);
         // P over the S columns this thread just read (the next S MMA into this
         // buffer waits for the PV MMA that reads P)
         tmem_st32_u(t_row + buf * kAttnBK, pk);
