@@ -471,6 +471,58 @@ XFB_API int xfb_outer_product_mean(const void* msa, int msa_dtype, int64_t s, in
                                    int accumulate, void* workspace, int64_t workspace_bytes,
                                    void* stream);
 
+/* ---- af3_kernels-compatible entry points.  The argument lists of the
+ * reference's native extension (af3_kernels/src/csrc/bindings.cpp:26-49) with
+ * plain pointers: weights are the transposed nn.Linear weights [in][out] that
+ * its bridges pass (xfold/fastnn/native.py:61, xfold/nn/triangle_multiplication.py:58-60),
+ * f32 or bf16 (w_dtype); the CPU tile sizes (block_size, M_BLK, N_BLK,
+ * query_block) must be positive 32-bit sizes, as xsmm_size requires
+ * (af3_kernels/src/csrc/tools.cpp:30-34), and do not change results;
+ * weights_packed = 1 (the CPU's VNNI2 layout) is rejected with
+ * XFB_ERR_INVALID.  Computation is bf16 with f32 accumulation, as the other
+ * entry points; each call packs its weights into the workspace. */
+
+/* linear (matrix.cpp:119-129): y[m][n] = x[m][k] (bf16) @ weight[k][n] + bias,
+ * bias f32 [n] or NULL, y f32 or bf16.  k, n multiples of 8. */
+XFB_API int64_t xfb_af3_linear_workspace(int64_t k, int64_t n);
+XFB_API int xfb_af3_linear(const void* x, int64_t m, int64_t k, const void* weight, int w_dtype,
+                           int64_t n, const float* bias, int weight_packed, void* y, int y_dtype,
+                           void* workspace, int64_t workspace_bytes, void* stream);
+
+/* gated_linear_unit (gated_linear_unit.cpp:78-121): y[m][n] (bf16) =
+ * silu(x @ weight[:, :n]) * (x @ weight[:, n:]) for x [m][k] bf16 and weight
+ * [k][2n].  n a multiple of 64, k a multiple of 8. */
+XFB_API int64_t xfb_af3_gated_linear_unit_workspace(int64_t k, int64_t n);
+XFB_API int xfb_af3_gated_linear_unit(const void* x, int64_t m, int64_t k, const void* weight,
+                                      int w_dtype, int64_t n, int64_t m_block, int64_t n_block,
+                                      int weight_packed, void* y, void* workspace,
+                                      int64_t workspace_bytes, void* stream);
+
+/* triangle_multiplication (triangle_multiplication.cpp:6-73): the update for
+ * pair [n][n][c] (f32 or bf16) with projection, gate [c][2c] and
+ * output_weight, gating_weight [c][c]; mask f32 [n][n] (the reference's
+ * broadcast to [N, N] done by the caller) or NULL.  out [n][n][c], f32 or bf16. */
+XFB_API int64_t xfb_af3_triangle_multiplication_workspace(int64_t n, int64_t c);
+XFB_API int xfb_af3_triangle_multiplication(
+    const void* pair, int pair_dtype, int64_t n, int64_t c, const float* mask, int outgoing,
+    const float* left_weight, const float* left_bias, const void* projection, const void* gate,
+    const float* center_weight, const float* center_bias, const void* output_weight,
+    const void* gating_weight, int w_dtype, double left_eps, double center_eps,
+    int64_t block_size, int weights_packed, void* out, int out_dtype, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
+/* dot_product_attention (dot_product_attention.cpp:110-174): xfb_dot_product_attention
+ * with the reference's query_block argument. */
+XFB_API int64_t xfb_af3_dot_product_attention_workspace(int64_t B, int64_t H, int64_t nq,
+                                                        int64_t nk, int64_t d);
+XFB_API int xfb_af3_dot_product_attention(const void* q, const void* k, const void* v, int64_t B,
+                                          int64_t H, int64_t nq, int64_t nk, int64_t d,
+                                          const void* mask, int mask_dtype, int mask_batched,
+                                          const void* bias, int bias_dtype, int bias_batched,
+                                          int64_t query_block, int q_pre_scaled, void* out,
+                                          void* workspace, int64_t workspace_bytes,
+                                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -95,3 +95,23 @@ def test_init_params_is_deterministic_and_follows_the_recipe():
     w = a.triangle_multiplication_outgoing.projection.weight
     assert abs(w.std().item() - 0.02) < 0.003
     assert torch.equal(a.triangle_multiplication_outgoing.left_norm_input.weight, torch.ones(16))
+
+
+def test_af3_compat_mirrors_the_reference_argument_checks():
+    """xfold_cpu_b200.af3_compat (the af3_kernels._C stand-in) refuses what the
+    reference's native extension refuses, before any device work: non-device
+    tensors, VNNI2-packed weights, non-positive tile sizes."""
+    import pytest
+    import torch
+
+    from xfold_cpu_b200 import af3_compat
+
+    x = torch.zeros(4, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        af3_compat.linear(x, torch.zeros(8, 8))
+    with pytest.raises(RuntimeError, match="VNNI2"):
+        af3_compat.gated_linear_unit(x, torch.zeros(8, 16), weight_packed=True)
+    with pytest.raises(RuntimeError, match="VNNI2"):
+        af3_compat.triangle_multiplication(*([None] * 11), weights_packed=True)
+    assert af3_compat.packed_weight_api == 0
+    assert af3_compat.load_extension() is af3_compat

@@ -111,6 +111,23 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_cross_attention": (_i, [_p, _i, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p,
                                  _p, _d, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _p, _i64,
                                  _p]),
+    "xfb_af3_linear_workspace": (_i64, [_i64, _i64]),
+    "xfb_af3_linear": (_i, [_p, _i64, _i64, _p, _i, _i64, _p, _i, _p, _i, _p, _i64, _p]),
+    "xfb_af3_gated_linear_unit_workspace": (_i64, [_i64, _i64]),
+    "xfb_af3_gated_linear_unit": (
+        _i, [_p, _i64, _i64, _p, _i, _i64, _i64, _i64, _i, _p, _p, _i64, _p]),
+    "xfb_af3_triangle_multiplication_workspace": (_i64, [_i64, _i64]),
+    "xfb_af3_triangle_multiplication": (
+        _i,
+        [_p, _i, _i64, _i64, _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _i, _d, _d, _i64, _i, _p,
+         _i, _p, _i64, _p],
+    ),
+    "xfb_af3_dot_product_attention_workspace": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "xfb_af3_dot_product_attention": (
+        _i,
+        [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _i, _p, _i, _i, _i64, _i, _p, _p,
+         _i64, _p],
+    ),
 }
 
 

@@ -417,9 +417,13 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
 // mode 0: triangle (proj/gate interleaved by 64 rows, then gating_linear)
 // mode 1: GLU (gate/value interleaved by 64 rows)
 // mode 2: concatenation of four [c][c] matrices
+// mode 3: one [rows][k] matrix (a plain copy, or the transpose of [k][rows])
+// transposed: the sources are the transposed nn.Linear weights [in][out] the
+// reference's native extension takes; element (row, col) is read at
+// col * out_features + row instead of row * k + col.
 __global__ void pack_weights_kernel(const void* s0, const void* s1, const void* s2,
                                     const void* s3, int src_f32, int mode, int64_t c_or_n,
-                                    int64_t k, int64_t rows, bf16* dst) {
+                                    int64_t k, int64_t rows, int transposed, bf16* dst) {
   const int64_t total = rows * k;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -427,28 +431,37 @@ __global__ void pack_weights_kernel(const void* s0, const void* s1, const void* 
     const int64_t col = idx - r * k;
     const void* src = nullptr;
     int64_t srow = 0;
+    int64_t out_features = 0;  // rows of the source matrix (its width when transposed)
     if (mode == 0) {
       const int64_t c = c_or_n;
       if (r < 4 * c) {
         const int64_t t = r / 128, w = r % 128;
         src = (w < 64) ? s0 : s1;
         srow = 64 * t + (w % 64);
+        out_features = 2 * c;
       } else {
         src = s2;
         srow = r - 4 * c;
+        out_features = c;
       }
     } else if (mode == 1) {
       const int64_t n = c_or_n;
       const int64_t t = r / 128, w = r % 128;
       src = s0;
       srow = (w < 64) ? 64 * t + w : n + 64 * t + (w - 64);
-    } else {
+      out_features = 2 * n;
+    } else if (mode == 2) {
       const int64_t c = c_or_n;
       const int64_t which = r / c;
       src = which == 0 ? s0 : which == 1 ? s1 : which == 2 ? s2 : s3;
       srow = r - which * c;
+      out_features = c;
+    } else {
+      src = s0;
+      srow = r;
+      out_features = rows;
     }
-    const int64_t off = srow * k + col;
+    const int64_t off = transposed ? col * out_features + srow : srow * k + col;
     const float v = src_f32 ? reinterpret_cast<const float*>(src)[off]
                             : __bfloat162float(reinterpret_cast<const bf16*>(src)[off]);
     dst[idx] = __float2bfloat16_rn(v);
@@ -456,12 +469,13 @@ __global__ void pack_weights_kernel(const void* s0, const void* s1, const void* 
 }
 
 int launch_pack(const void* s0, const void* s1, const void* s2, const void* s3, int w_dtype,
-                int mode, int64_t c_or_n, int64_t k, int64_t rows, void* dst, cudaStream_t st) {
+                int mode, int64_t c_or_n, int64_t k, int64_t rows, void* dst, cudaStream_t st,
+                int transposed = 0) {
   XFB_REQUIRE(w_dtype == XFB_F32 || w_dtype == XFB_BF16, "weights must be f32 or bf16");
   const int64_t total = rows * k;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
   pack_weights_kernel<<<blocks, 256, 0, st>>>(s0, s1, s2, s3, w_dtype == XFB_F32, mode, c_or_n,
-                                              k, rows, static_cast<bf16*>(dst));
+                                              k, rows, transposed, static_cast<bf16*>(dst));
   XFB_LAUNCHED();
   return XFB_OK;
 }
@@ -2430,6 +2444,140 @@ XFB_API int xfb_exchange_wait(const void* flags, int world, uint32_t epoch, void
       static_cast<const uint32_t*>(flags), world, epoch);
   XFB_LAUNCHED();
   return XFB_OK;
+}
+
+}  // extern "C"
+
+// ====================================================================== af3_kernels-compatible ABI
+
+namespace {
+
+// The CPU tile sizes of the reference's native extension (block_size, M_BLK,
+// N_BLK, query_block): validated like xsmm_size (positive, 32-bit), otherwise
+// without effect -- the tile shapes of these kernels are fixed.
+int check_cpu_block(int64_t b, const char* name) {
+  if (b <= 0 || b > 0x7fffffff)
+    return fail(XFB_ERR_INVALID, std::string(name) + " must be a positive 32-bit size");
+  return XFB_OK;
+}
+
+int reject_vnni(int packed) {
+  if (packed)
+    return fail(XFB_ERR_INVALID,
+                "VNNI2-packed weights are a CPU layout; pass the [in, out] weights "
+                "(weights_packed = false)");
+  return XFB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+XFB_API int64_t xfb_af3_linear_workspace(int64_t k, int64_t n) {
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(n * k);
+  return cv.used;
+}
+
+XFB_API int xfb_af3_linear(const void* x, int64_t m, int64_t k, const void* weight, int w_dtype,
+                           int64_t n, const float* bias, int weight_packed, void* y, int y_dtype,
+                           void* workspace, int64_t workspace_bytes, void* stream) {
+  XFB_TRY(reject_vnni(weight_packed));
+  XFB_REQUIRE(m >= 0 && k > 0 && n > 0, "linear expects m >= 0, k > 0, n > 0");
+  XFB_REQUIRE(k % 8 == 0 && n % 8 == 0, "linear requires k and n to be multiples of 8");
+  XFB_REQUIRE(y_dtype == XFB_F32 || y_dtype == XFB_BF16, "linear output must be f32 or bf16");
+  XFB_REQUIRE(aligned16(x) && aligned16(y), "linear input and output must be 16-byte aligned");
+  if (m == 0) return XFB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  bf16* w = cv.take<bf16>(n * k);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  XFB_TRY(launch_pack(weight, nullptr, nullptr, nullptr, w_dtype, 3, n, k, n, w, st, 1));
+  return linear_core(static_cast<const bf16*>(x), m, k, k, w, n, bias, nullptr, 0, y,
+                     y_dtype == XFB_F32, 0, n, st);
+}
+
+XFB_API int64_t xfb_af3_gated_linear_unit_workspace(int64_t k, int64_t n) {
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(2 * n * k);
+  return cv.used;
+}
+
+XFB_API int xfb_af3_gated_linear_unit(const void* x, int64_t m, int64_t k, const void* weight,
+                                      int w_dtype, int64_t n, int64_t m_block, int64_t n_block,
+                                      int weight_packed, void* y, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
+  XFB_TRY(reject_vnni(weight_packed));
+  XFB_TRY(check_cpu_block(m_block, "M_BLK"));
+  XFB_TRY(check_cpu_block(n_block, "N_BLK"));
+  XFB_REQUIRE(m >= 0 && k > 0, "GLU expects m >= 0 and k > 0");
+  XFB_REQUIRE(n > 0 && n % 64 == 0, "GLU hidden width must be a positive multiple of 64");
+  XFB_REQUIRE(k % 8 == 0, "GLU input width must be a multiple of 8");
+  XFB_REQUIRE(aligned16(x) && aligned16(y), "GLU input and output must be 16-byte aligned");
+  if (m == 0) return XFB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  bf16* pk = cv.take<bf16>(2 * n * k);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  XFB_TRY(launch_pack(weight, nullptr, nullptr, nullptr, w_dtype, 1, n, k, 2 * n, pk, st, 1));
+  xfb::EpiGLU epi;
+  XFB_TRY(make_out_map(&epi.out_map, y, false, n, m, 1, n, 0));
+  return run_gemm<128, false, false>(x, k, 0, pk, k, 0, m, 2 * n, k, 1, epi, st);
+}
+
+XFB_API int64_t xfb_af3_triangle_multiplication_workspace(int64_t n, int64_t c) {
+  Carver cv{nullptr, 0, 0};
+  cv.take<bf16>(5 * c * c);  // packed projection | gate | gating_linear
+  cv.take<bf16>(c * c);      // output_projection in [out][in]
+  cv.take<uint8_t>(xfb_triangle_multiplication_workspace(n, c));
+  return cv.used;
+}
+
+XFB_API int xfb_af3_triangle_multiplication(
+    const void* pair, int pair_dtype, int64_t n, int64_t c, const float* mask, int outgoing,
+    const float* left_weight, const float* left_bias, const void* projection, const void* gate,
+    const float* center_weight, const float* center_bias, const void* output_weight,
+    const void* gating_weight, int w_dtype, double left_eps, double center_eps,
+    int64_t block_size, int weights_packed, void* out, int out_dtype, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  XFB_TRY(reject_vnni(weights_packed));
+  XFB_TRY(check_cpu_block(block_size, "block_size"));
+  XFB_REQUIRE(c == 64 || c == 128, "triangle multiplication supports c in {64, 128}");
+  XFB_REQUIRE(projection && gate && output_weight && gating_weight, "triangle weights missing");
+  XFB_REQUIRE(n >= 0, "pair side must be non-negative");
+  if (n == 0) return XFB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
+  bf16* packed = cv.take<bf16>(5 * c * c);
+  bf16* wo = cv.take<bf16>(c * c);
+  const int64_t inner = xfb_triangle_multiplication_workspace(n, c);
+  uint8_t* ws = cv.take<uint8_t>(inner);
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
+  XFB_TRY(launch_pack(projection, gate, gating_weight, nullptr, w_dtype, 0, c, c, 5 * c, packed,
+                      st, 1));
+  XFB_TRY(launch_pack(output_weight, nullptr, nullptr, nullptr, w_dtype, 3, c, c, c, wo, st, 1));
+  return xfb_triangle_multiplication(pair, pair_dtype, n, c, mask, outgoing, left_weight,
+                                     left_bias, nullptr, nullptr, center_weight, center_bias, wo,
+                                     nullptr, left_eps, center_eps, 1, packed, out, out_dtype, 0,
+                                     ws, inner, stream);
+}
+
+XFB_API int64_t xfb_af3_dot_product_attention_workspace(int64_t B, int64_t H, int64_t nq,
+                                                        int64_t nk, int64_t d) {
+  return xfb_dot_product_attention_workspace(B, H, nq, nk, d);
+}
+
+XFB_API int xfb_af3_dot_product_attention(const void* q, const void* k, const void* v, int64_t B,
+                                          int64_t H, int64_t nq, int64_t nk, int64_t d,
+                                          const void* mask, int mask_dtype, int mask_batched,
+                                          const void* bias, int bias_dtype, int bias_batched,
+                                          int64_t query_block, int q_pre_scaled, void* out,
+                                          void* workspace, int64_t workspace_bytes,
+                                          void* stream) {
+  XFB_TRY(check_cpu_block(query_block, "query_block"));
+  return xfb_dot_product_attention(q, k, v, B, H, nq, nk, d, mask, mask_dtype, mask_batched,
+                                   bias, bias_dtype, bias_batched, q_pre_scaled, out, workspace,
+                                   workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -654,17 +654,23 @@ struct EpiTriProj {
 
   __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
 
+  // mask value of a row (1 when there is no mask or the row is past the end)
+  __device__ __forceinline__ float row_mask(int bat, int j) const {
+    return (mask != nullptr && j < n) ? __ldg(mask + static_cast<int64_t>(bat) * n + j) : 1.f;
+  }
+
   __device__ void compute(const EpiCtx& c) const {
     const int tile = c.n0 / 128;
     const int j = c.m0 + c.row;
     if (tile < n_proj_tiles) {
-      float mval = 1.f;
-      if (mask != nullptr && j < n) mval = mask[static_cast<int64_t>(c.bat) * n + j];
-      float pv[32], gv[32];
-      tmem_ld32(c.tmem + c.half * 32, pv);
-      tmem_ld32(c.tmem + 64 + c.half * 32, gv);
+      const float mval = row_mask(c.bat, j);
       __nv_bfloat16* sa = reinterpret_cast<__nv_bfloat16*>(c.staging);
       __nv_bfloat16* sb = sa + 32 * 128;
+      // projection and gate columns with one TMEM round trip
+      float pv[32], gv[32];
+      tmem_ld32_nowait(c.tmem + c.half * 32, pv);
+      tmem_ld32_nowait(c.tmem + 64 + c.half * 32, gv);
+      tmem_ld_wait();
 #pragma unroll
       for (int q = 0; q < 32; q += 2) {
         const int ch = c.half * 16 + q / 2;  // local a / b channel
@@ -672,14 +678,14 @@ struct EpiTriProj {
         sb[ch * 128 + c.row] = __float2bfloat16_rn(pv[q + 1] * mval * sigmoid_fast(gv[q + 1]));
       }
     } else {
-      float v[32];
+      float v[64];
+      tmem_ld32_nowait(c.tmem + c.half * 64, v);
+      tmem_ld32_nowait(c.tmem + c.half * 64 + 32, v + 32);
+      tmem_ld_wait();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        tmem_ld32(c.tmem + c.half * 64 + h * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = sigmoid_fast(v[i]);
-        stage32_bf16_sw128(c.staging + c.half * 16384, c.row, h * 4, v);
-      }
+      for (int i = 0; i < 64; ++i) v[i] = sigmoid_fast(v[i]);
+      stage32_bf16_sw128(c.staging + c.half * 16384, c.row, 0, v);
+      stage32_bf16_sw128(c.staging + c.half * 16384, c.row, 4, v + 32);
     }
   }
 

@@ -239,13 +239,16 @@ def triangle_multiplication(pair: torch.Tensor, mask: torch.Tensor | None, outgo
 
 def dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                           mask: torch.Tensor | None = None, bias: torch.Tensor | None = None,
-                          q_pre_scaled: bool = False) -> torch.Tensor:
+                          q_pre_scaled: bool = False,
+                          query_block: int | None = None) -> torch.Tensor:
     """softmax(q k^T / sqrt(d) + bias, mask) v for q, k, v [B, H, Q/K, D] (af3_kernels
     dot_product_attention, dot_product_attention.cpp:110-174).
 
     mask: rank 1 [K] or rank 2 [B, K] (any dtype, nonzero = keep), or a bool
     tensor broadcastable to [B, 1, 1, K].  bias: broadcastable to [B, H, Q, K]
-    with the B dimension either B or 1."""
+    with the B dimension either B or 1.  query_block: the reference's CPU tile
+    size, passed through the af3_kernels-compatible entry point (validated,
+    no effect on results)."""
     device = _check_cuda(q, k, v, mask, bias)
     for t in (q, k, v):
         if t.dim() != 4:
@@ -283,10 +286,16 @@ def dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         bias_t = _contig(b4, torch.bfloat16 if b4.dtype == torch.bfloat16 else torch.float32)
     out = torch.empty((B, H, nq, d), dtype=torch.bfloat16, device=device)
     ws = _workspace(_capi.load().xfb_dot_product_attention_workspace(B, H, nq, nk, d), device)
-    _capi.call("xfb_dot_product_attention", _ptr(q), _ptr(k), _ptr(v), B, H, nq, nk, d,
-               _ptr(mask_t), mask_code, mask_batched, _ptr(bias_t),
-               _code(bias_t) if bias_t is not None else _capi.BF16, bias_batched,
-               1 if q_pre_scaled else 0, _ptr(out), _ptr(ws), ws.numel(), _stream(device))
+    bias_code = _code(bias_t) if bias_t is not None else _capi.BF16
+    if query_block is None:
+        _capi.call("xfb_dot_product_attention", _ptr(q), _ptr(k), _ptr(v), B, H, nq, nk, d,
+                   _ptr(mask_t), mask_code, mask_batched, _ptr(bias_t), bias_code, bias_batched,
+                   1 if q_pre_scaled else 0, _ptr(out), _ptr(ws), ws.numel(), _stream(device))
+    else:
+        _capi.call("xfb_af3_dot_product_attention", _ptr(q), _ptr(k), _ptr(v), B, H, nq, nk, d,
+                   _ptr(mask_t), mask_code, mask_batched, _ptr(bias_t), bias_code, bias_batched,
+                   int(query_block), 1 if q_pre_scaled else 0, _ptr(out), _ptr(ws), ws.numel(),
+                   _stream(device))
     return out
 
 
