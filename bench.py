@@ -605,6 +605,79 @@ def _atom_c5(dev, steps: int) -> dict:
     return out
 
 
+C5_SAMPLES, C5_STEPS = 5, 200
+
+
+def _c5_sampling(dev, world: int, rank: int) -> dict:
+    """BASELINE config C5 end to end on the in-scope modules: 5 samples x 200
+    denoising steps, each step = the atom encoder's transformer, the 24-block
+    token transformer and the atom decoder's transformer, every one a replayed
+    CUDA graph (sizes and init of _diffusion_c5 / _atom_c5; the two atom
+    transformers have their own weights).  Samples are spread over the ranks
+    by the reference's cyclic schedule (xfold/distributed.py:14-37, samples.py
+    work_indices); each step feeds its outputs to the next.  The time is this
+    rank's wall on the device; the caller takes the max over ranks."""
+    import torch
+
+    from xfold_cpu_b200 import samples
+    from xfold_cpu_b200.nn import DiffusionCrossAttTransformer, DiffusionTransformer, init_params_
+
+    n, c, s = 768, 768, ATOM_SUBSETS
+    with torch.inference_mode(False):
+        tok = DiffusionTransformer(c_act=c).eval()
+        init_params_(tok, seed=4)
+        enc = DiffusionCrossAttTransformer().eval()
+        init_params_(enc, seed=5)
+        dec = DiffusionCrossAttTransformer().eval()
+        init_params_(dec, seed=6)
+        tok, enc, dec = tok.to(dev), enc.to(dev), dec.to(dev)
+    g = torch.Generator(device=dev).manual_seed(4)
+    act = torch.randn(n, c, device=dev, generator=g)
+    cond = torch.randn(n, 384, device=dev, generator=g)
+    pair_cond = torch.randn(n, n, 128, device=dev, generator=g)
+    mask = torch.ones(n, device=dev)
+    info, qmask, kmask = _atom_windows(s, (s * 32) // 20)
+    atom_act, qsc, atom_pair = (t.to(dev) for t in _atom_inputs(s, 4))
+    qmask, kmask = qmask.to(dev), kmask.to(dev)
+    mine = list(samples.work_indices(C5_SAMPLES, rank, world))
+    stream = torch.cuda.current_stream(dev)
+    with torch.inference_mode():
+        from xfold_cpu_b200.nn import atom_layout
+
+        ksc = atom_layout.convert(info, qsc, layout_axes=(-3, -2))
+        enc_step = enc.capture(atom_act, qmask, info, kmask, qsc, ksc, atom_pair)
+        dec_step = dec.capture(atom_act, qmask, info, kmask, qsc, ksc, atom_pair)
+        tok_step = tok.capture(act, mask, cond, pair_cond)
+
+        def one_step(a_atom, a_tok):
+            a_atom = enc_step(a_atom, qsc, ksc)
+            a_tok = tok_step(a_tok, cond)
+            a_atom = dec_step(a_atom, qsc, ksc)
+            return a_atom, a_tok
+
+        for _ in range(3):  # warm-up
+            one_step(atom_act, act)
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in mine:
+            a_atom, a_tok = atom_act, act
+            for _ in range(C5_STEPS):
+                a_atom, a_tok = one_step(a_atom, a_tok)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        finite = bool(torch.isfinite(a_tok).all()) if mine else True
+        del enc_step, dec_step, tok_step
+    return {"samples": C5_SAMPLES, "steps_per_sample": C5_STEPS, "samples_this_rank": len(mine),
+            "ms": ms, "finite": finite,
+            "step": "atom encoder transformer + 24-block token transformer + atom decoder "
+                    "transformer, each a replayed CUDA graph",
+            "scope": "the in-scope modules of a denoising step (the diffusion head's "
+                     "featurisation, atom layout conversions and EDM update are out of scope)"}
+
+
 EVO_N, EVO_S = 1024, 1024  # the reference's MSA stack: num_msa = 1024 at N_token = 1024
 
 
@@ -804,6 +877,44 @@ def run_only(args) -> None:
                       "finite": bool(torch.isfinite(work).all())}))
 
 
+def _sharded_parity(dev, blk, pair_h, pair_mask_h, single_h, seq_mask_h, rows, world,
+                    exchange) -> dict:
+    """Block 0 of the trunk run twice on this rank before the timing: row-sharded
+    over the N GPUs (this rank's rows, the exchanges of the timed run) and whole
+    on this GPU alone; max |sharded - whole| / max |whole| of the pair update on
+    this rank's rows and of the single update, maximum over ranks.  Both
+    computations are the CUDA path (no oracle): the check is that sharding
+    changes nothing beyond bf16 rounding."""
+    import torch
+    import torch.distributed as dist
+
+    from xfold_cpu_b200 import sharded
+
+    with torch.inference_mode():
+        pm, sm = pair_mask_h.to(dev), seq_mask_h.to(dev)
+        whole = pair_h.to(dev)
+        s_whole = single_h.to(dev)
+        blk(whole, pm, s_whole, sm)
+        part0 = pair_h[rows].to(dev)
+        part = part0.clone()
+        s_part = single_h.to(dev)
+        sharded.pairformer_block(blk, [part], pm, s_part, sm, exchange)
+        want = whole[rows] - part0
+        single0 = single_h.to(dev)
+        stats = torch.tensor([(part - part0 - want).abs().max().item(), want.abs().max().item(),
+                              (s_part - s_whole).abs().max().item(),
+                              (s_whole - single0).abs().max().item()],
+                             dtype=torch.float64, device=dev)
+        del whole, part, part0, want
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    pair_err = stats[0].item() / max(stats[1].item(), 1e-30)
+    single_err = stats[2].item() / max(stats[3].item(), 1e-30)
+    return {"pair_update_rel_err": round(pair_err, 6), "single_update_rel_err": round(single_err, 6),
+            "tolerance": PARITY_TOL, "ok": max(pair_err, single_err) <= PARITY_TOL,
+            "what": f"block 0 row-sharded over {world} GPUs vs the same block on one GPU, "
+                    "all rows, max over ranks"}
+
+
 def run_cuda(args) -> None:
     import torch
 
@@ -822,16 +933,20 @@ def run_cuda(args) -> None:
         init_params_(blk, seed=SEED * 1000 + i)
         blocks.append(blk.to(dev))
     pair_h, pair_mask_h, single_h, seq_mask_h = _inputs(n_tok, SEED)
+    sharded_parity = None
     if world > 1:
         # row-sharded pair: this rank holds rows R_rank of the one N x N trunk
         from xfold_cpu_b200 import sharded
 
         sharded.check_sharding(n_tok, C_PAIR, world)
-        pair_h = pair_h[sharded.shard_rows(n_tok, world, rank)].contiguous()
+        rows = sharded.shard_rows(n_tok, world, rank)
         # peer stores over NVLink by default; XFB_EXCHANGE=collective uses NCCL all-to-all
         exchange = (sharded.ProcessGroupExchange()
                     if os.environ.get("XFB_EXCHANGE", "peer") == "collective"
                     else sharded.PeerExchange())
+        sharded_parity = _sharded_parity(dev, blocks[0], pair_h, pair_mask_h, single_h,
+                                          seq_mask_h, rows, world, exchange)
+        pair_h = pair_h[rows].contiguous()
     pair_h, pair_mask_h = pair_h.pin_memory(), pair_mask_h.pin_memory()
     single_h, seq_mask_h = single_h.pin_memory(), seq_mask_h.pin_memory()
     pair = pair_h.to(dev)
@@ -904,6 +1019,8 @@ def run_cuda(args) -> None:
         finite = bool(torch.isfinite(out_pair).all() and torch.isfinite(out_single).all())
 
         roof = _kernel_roofline(dev, args.steps, peaks) if rank == 0 else {}
+        c5_run = _c5_sampling(dev, world, rank)
+        c5_ms = _max_over_ranks(c5_run["ms"], world)
         c5 = _diffusion_c5(dev, args.steps) if rank == 0 and world == 1 else None
         atom = _atom_c5(dev, args.steps) if rank == 0 and world == 1 else None
         evo = _evoformer(dev, args.steps) if rank == 0 and world == 1 else None
@@ -949,8 +1066,11 @@ def run_cuda(args) -> None:
         "cpu_baseline": base,
         "finite": finite,
         "parity": parity,
-        "extras": ({"diffusion_transformer_c5": c5, "atom_transformer_c5": atom,
-                    "evoformer_block": evo} if c5 else None),
+        "sharded_parity": sharded_parity,
+        "extras": {"diffusion_c5_5x200": {**c5_run, "ms": round(c5_ms, 1), "gpus": world,
+                                          "ms_note": "max over ranks of each rank's samples"},
+                   **({"diffusion_transformer_c5": c5, "atom_transformer_c5": atom,
+                       "evoformer_block": evo} if c5 else {})},
     }
     print(json.dumps(line), flush=True)
 

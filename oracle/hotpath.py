@@ -287,6 +287,30 @@ def diffusion_transition(x, single_cond, params, use_single_cond=True, prefix=""
     return ada_ln_zero(h, single_cond, params, use_single_cond, prefix + "adaptive_zero_init.")
 
 
+def diffusion_transformer(act, mask, single_cond, pair_cond, params, num_blocks=24,
+                          super_block_size=4, num_head=16, prefix=""):
+    """DiffusionTransformer.forward (xfold/nn/diffusion_transformer.py:250-272):
+    LN(pair_cond) once; per super-block the pair-logit projection rearranged
+    'n s (b h) -> b h n s' (:262-265); then per block act += SelfAttention(act,
+    mask, logits[j], single_cond) and act += DiffusionTransition(act,
+    single_cond), both conditioned.  Returns a new tensor."""
+    P = lambda n: _p(params, prefix, n)
+    act = act.clone()
+    pair_act = layer_norm(pair_cond, P("pair_input_layer_norm.weight"),
+                          P("pair_input_layer_norm.bias"))
+    n, s = pair_act.shape[:2]
+    for sb in range(num_blocks // super_block_size):
+        logits = linear(pair_act, P(f"pair_logits_projection.{sb}.weight"))
+        logits = logits.reshape(n, s, super_block_size, num_head).permute(2, 3, 0, 1)
+        for j in range(super_block_size):
+            i = sb * super_block_size + j
+            act += self_attention(act, mask, logits[j], params, single_cond, num_head, True,
+                                  prefix + f"self_attention.{i}.")
+            act += diffusion_transition(act, single_cond, params, True,
+                                        prefix + f"transition_block.{i}.")
+    return act
+
+
 def pair_logits(pair, params, prefix=""):
     """Single-track pair logits (xfold/nn/pairformer.py:103-106): LN then a
     bias-free projection to heads, permuted to [H, N, N]."""

@@ -270,6 +270,31 @@ def main() -> None:
           {"msa": m32, "pair": p32, "bf16:msa": m16, "bf16:pair": p16})
 
 
+def diffusion_transformer_fixture() -> None:
+    """DiffusionTransformer.forward (diffusion_transformer.py:250-272): 4 blocks in
+    2 super-blocks, c_act 64, single cond 32, pair cond 8, masked tail; 16
+    heads (of 4), since the reference builds its SelfAttention with the default
+    head count (:243-244); its own random stream so the other fixtures are
+    unchanged."""
+    from xfold.nn.diffusion_transformer import DiffusionTransformer
+
+    g = torch.Generator().manual_seed(4321)
+    n = 16
+    mod = DiffusionTransformer(c_act=64, c_single_cond=32, c_pair_cond=8, num_head=16,
+                               num_blocks=4, super_block_size=2).eval()
+    _init(mod, 95, std=0.1)
+    act = torch.randn(n, 64, generator=g)
+    sc = torch.randn(n, 32, generator=g)
+    pc = torch.randn(n, n, 8, generator=g)
+    mask = torch.ones(n)
+    mask[-3:] = 0
+    fp32, bf16 = _both(lambda: mod(act.clone(), mask, sc, pc))
+    _save("diffusion_transformer", mod,
+          {"act": act, "mask": mask, "single_cond": sc, "pair_cond": pc},
+          {"act": fp32, "bf16:act": bf16})
+
+
 if __name__ == "__main__":
     ONLY.update(sys.argv[1:])
-    sys.exit(main())
+    main()
+    diffusion_transformer_fixture()

@@ -273,3 +273,34 @@ def test_empty_key_set_returns_zeros():
     torch.cuda.synchronize()
     assert out.shape == (2, 3, 40, 32)
     assert torch.count_nonzero(out.float()) == 0
+
+
+# ----------------------------------------------------------------------------- C5
+
+def test_c5_diffusion_transformer_24_blocks():
+    """C5's token transformer at full size: 24 blocks in 6 super-blocks, N = 768,
+    c = 768, 16 heads of 48, single cond 384, pair cond [768, 768, 128], random
+    init N(0, 0.02) with LayerNorm gamma 1 / beta 0, seed 4, 32 padded tokens;
+    the update of one forward against the oracle of DiffusionTransformer.forward
+    (xfold/nn/diffusion_transformer.py:250-272)."""
+    from xfold_cpu_b200.nn import DiffusionTransformer, init_params_
+
+    n, c = 768, 768
+    mod = DiffusionTransformer(c_act=c).eval()
+    init_params_(mod, seed=4)
+    params = {k: v.detach().clone() for k, v in mod.state_dict().items()}
+    g = torch.Generator().manual_seed(4)
+    act = torch.randn(n, c, generator=g)
+    cond = torch.randn(n, 384, generator=g)
+    pair_cond = torch.randn(n, n, 128, generator=g)
+    mask = torch.ones(n)
+    mask[-32:] = 0
+    mod = mod.to(DEV)
+    got = act.to(DEV)
+    with torch.inference_mode():
+        mod(got, mask.to(DEV), cond.to(DEV), pair_cond.to(DEV))
+    got = got.cpu()
+    assert torch.isfinite(got).all()
+    with torch.inference_mode():
+        ref = oracle.diffusion_transformer(act, mask, cond, pair_cond, params)
+    assert oracle.relative_error(got - act, ref - act) < TOL

@@ -227,3 +227,27 @@ def test_sampled_row_grid_attention_equals_the_full_restatement(transpose):
     assert oracle.relative_error(got, want) < 1e-6
     ref = o["update"][:, rows].permute(1, 0, 2) if transpose else o["update"][rows]
     check(got, ref, FP32_TOL)
+
+
+def test_diffusion_transformer():
+    """The 24-block composition of DiffusionTransformer.forward (:250-272): the
+    super-block pair-logit rearrangement and the residual order, on the
+    reference's own output (4 blocks, 2 super-blocks)."""
+    p, i, o = load("diffusion_transformer")
+    got = oracle.diffusion_transformer(i["act"], i["mask"], i["single_cond"], i["pair_cond"], p,
+                                       num_blocks=4, super_block_size=2, num_head=16)
+    check(got, o["act"], 1e-5)
+    check(o["bf16:act"] - i["act"], got - i["act"], BF16_TOL)
+
+
+def test_diffusion_transformer_logit_layout_is_pinned():
+    """Planted mistake: the super-block logits split as '(h b)' instead of
+    '(b h)' must be caught."""
+    p, i, o = load("diffusion_transformer")
+    q = dict(p)
+    for sb in range(2):
+        w = p[f"pair_logits_projection.{sb}.weight"]  # rows (b h)
+        q[f"pair_logits_projection.{sb}.weight"] = w.reshape(2, 16, -1).transpose(0, 1).reshape(w.shape)
+    wrong = oracle.diffusion_transformer(i["act"], i["mask"], i["single_cond"], i["pair_cond"], q,
+                                         num_blocks=4, super_block_size=2, num_head=16)
+    assert oracle.relative_error(wrong - i["act"], o["act"] - i["act"]) > 1e-2

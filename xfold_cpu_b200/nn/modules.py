@@ -28,7 +28,6 @@ from typing import Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from .. import native
 from . import atom_layout
@@ -164,19 +163,18 @@ class AdaptiveLayerNorm(nn.Module):
             self.single_cond_layer_norm = LayerNorm(c_single_cond, bias=False)
             self.single_cond_scale = nn.Linear(c_single_cond, c_x, bias=True)
             self.single_cond_bias = nn.Linear(c_single_cond, c_x, bias=False)
+            self._cond_w = WeightCache()
         else:
             self.layer_norm = LayerNorm(c_x)
 
     def modulation(self, single_cond: torch.Tensor):
-        """(sigmoid(scale), shift) of the conditioned path as bf16 [N, c_x], the
-        rounding of the reference under bf16 autocast (:57-62)."""
-        sc = F.layer_norm(single_cond.float(), (self.c_single_cond,),
-                          self.single_cond_layer_norm.weight, None,
-                          self.single_cond_layer_norm.eps).bfloat16()
-        scale = F.linear(sc, self.single_cond_scale.weight.bfloat16(),
-                         self.single_cond_scale.bias.bfloat16())
-        shift = F.linear(sc, self.single_cond_bias.weight.bfloat16())
-        return torch.sigmoid(scale), shift
+        """(sigmoid(scale), shift) of the conditioned path as bf16 [N, c_x]
+        (:57-62): the library's LayerNorm and one conditioning GEMM against the
+        stacked scale / shift weights, as DiffusionTransformer does for all of
+        its blocks at once.  c_x must be a multiple of 64."""
+        mod = _modulations(self._cond_w, [self], single_cond.reshape(-1, self.c_single_cond),
+                           self.c_x)
+        return mod[0], mod[1]
 
     def forward(self, x: torch.Tensor, single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
         assert (single_cond is None) == (self.use_single_cond is False)
@@ -197,12 +195,13 @@ class AdaLNZero(nn.Module):
         self.transition2 = nn.Linear(c_in, c_out, bias=False)
         if use_single_cond:
             self.adaptive_zero_cond = nn.Linear(c_single_cond, c_out, bias=True)
+            self._gate_w = WeightCache()
 
     def out_gate(self, single_cond: torch.Tensor) -> torch.Tensor:
-        """sigmoid(adaptive_zero_cond(single_cond)) as bf16 (:91-94)."""
-        cond = F.linear(single_cond.bfloat16(), self.adaptive_zero_cond.weight.bfloat16(),
-                        self.adaptive_zero_cond.bias.bfloat16())
-        return torch.sigmoid(cond)
+        """sigmoid(adaptive_zero_cond(single_cond)) as bf16 [N, c_out] (:91-94),
+        one conditioning GEMM of the library.  c_out must be a multiple of 64."""
+        return _gates(self._gate_w, [self], single_cond.reshape(-1, self.c_single_cond),
+                      self.c_out)[0]
 
     def forward(self, x: torch.Tensor, single_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
         assert (single_cond is None) == (self.use_single_cond is False)
