@@ -910,6 +910,8 @@ def _sharded_parity(dev, blk, pair_h, pair_mask_h, single_h, seq_mask_h, rows, w
     pair_err = stats[0].item() / max(stats[1].item(), 1e-30)
     single_err = stats[2].item() / max(stats[3].item(), 1e-30)
     return {"pair_update_rel_err": round(pair_err, 6), "single_update_rel_err": round(single_err, 6),
+            "pair_update_max_abs": round(stats[1].item(), 6),
+            "single_update_max_abs": round(stats[3].item(), 6),
             "tolerance": PARITY_TOL, "ok": max(pair_err, single_err) <= PARITY_TOL,
             "what": f"block 0 row-sharded over {world} GPUs vs the same block on one GPU, "
                     "all rows, max over ranks"}
