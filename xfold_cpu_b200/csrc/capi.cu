@@ -12,6 +12,7 @@
 #include <atomic>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "../../include/xfold_b200.h"
 #include "attention.cuh"
@@ -657,26 +658,39 @@ int launch_flash(const bf16* q, const bf16* k, const bf16* v, xfb::AttnArgs args
 
 // Three-query-tile triangle attention (tri_attention.cuh): head dim <= 32, one
 // TMA-streamed bias shared by all batch rows.
+// Triangle-attention kernel shape: XFB_TRI_CFG 0 = three slots of 64-key
+// tiles, 1 = four slots of 32-key tiles (tri_attention.cuh: TriCfg).  Measured
+// at N = 1024: 1.83 ms and 2.34 ms per launch -- per-tile costs (barrier
+// handoffs, MMA issue, TMEM round trips) outweigh the fourth softmax warp per
+// sub-partition.
+#ifndef XFB_TRI_CFG
+#define XFB_TRI_CFG 0
+#endif
+using TriShape = std::conditional_t<XFB_TRI_CFG == 0, xfb::TriCfg<3, 64>, xfb::TriCfg<4, 32>>;
+
 template <bool PRE>
 int launch_flash_tri(const bf16* q, const bf16* k, const bf16* v, xfb::AttnArgs args,
                      cudaStream_t st) {
+  using C = TriShape;
+  using L = xfb::TriSmem<C>;
   CUtensorMap tq, tk, tv, tb;
   const CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_64B;
   const int64_t bh = static_cast<int64_t>(args.B) * args.H;
   XFB_TRY(make_map(&tq, q, 32, args.nq, bh, 64, int64_t(args.nq) * 64, 32, 128, swz));
-  XFB_TRY(make_map(&tk, k, 32, args.nk, bh, 64, int64_t(args.nk) * 64, 32, xfb::kAttnBK, swz));
-  XFB_TRY(make_map(&tv, v, 32, args.nk, bh, 64, int64_t(args.nk) * 64, 32, xfb::kAttnBK, swz));
+  XFB_TRY(make_map(&tk, k, 32, args.nk, bh, 64, int64_t(args.nk) * 64, 32, C::kBK, swz));
+  XFB_TRY(make_map(&tv, v, 32, args.nk, bh, 64, int64_t(args.nk) * 64, 32, C::kBK, swz));
   XFB_TRY(make_map(&tb, args.bias, args.nk, args.nq, args.H, args.bias_sq * 2, args.bias_sh * 2,
-                   xfb::kAttnBK, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+                   C::kBK, 128,
+                   C::kBK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
   args.q_tiles = (args.nq + 127) / 128;
-  auto kernel = xfb::flash_tri_kernel<PRE>;
-  XFB_TRY(set_smem(kernel, xfb::TriSmem::kLaunchBytes));
+  auto kernel = xfb::flash_tri_kernel<PRE, C>;
+  XFB_TRY(set_smem(kernel, L::kLaunchBytes));
   int sms;
   XFB_TRY(sm_count(&sms));
-  const int64_t groups = static_cast<int64_t>((args.B + xfb::kTriSlots - 1) / xfb::kTriSlots) *
-                         args.H * args.q_tiles;
+  const int64_t groups = static_cast<int64_t>((args.B + C::kSlots - 1) / C::kSlots) * args.H *
+                         args.q_tiles;
   const int grid = static_cast<int>(std::min<int64_t>(groups, sms));
-  kernel<<<grid, xfb::kTriThreads, xfb::TriSmem::kLaunchBytes, st>>>(tq, tk, tv, tb, args);
+  kernel<<<grid, C::kThreads, L::kLaunchBytes, st>>>(tq, tk, tv, tb, args);
   XFB_LAUNCHED();
   return XFB_OK;
 }
