@@ -402,11 +402,14 @@ def run_reference(args) -> None:
 
 # ----------------------------------------------------------------------------- GPU arm
 
-# DRAM bytes (read + write) per launch from one ncu capture of the same kernel,
-# scaled to the bench shapes by the units processed (profiles/flash_tri_n512_full.md:
-# 322.9 MB at N = 512, every tensor of the launch scales with N^2).  None where no
-# capture was taken.
-TRAFFIC_BYTES = {"flash_attn": 1.292e9, "triangle_contraction": None}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch, from one
+# ncu capture of the block's own launches of the same kernels on the same shapes
+# (N = 1024: the outgoing contraction and the starting-node triangle attention).
+# flash_tri_kernel: 1.0838e9 read + 0.2540e9 written (q, k, v, gate and bias in,
+# the gated output out); outgoing contraction gemm_bf16_kernel<256, 4, 0, 0,
+# EpiDirect<256>>: 0.5370e9 read + 0.2337e9 written (a and b in, z out): both at
+# their algorithmic bytes, no re-reads.
+TRAFFIC_BYTES = {"flash_attn": 1.3378e9, "triangle_contraction": 0.7708e9}
 
 
 def _kernel_roofline(dev, steps: int, peaks: dict) -> dict:

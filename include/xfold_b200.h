@@ -329,6 +329,79 @@ XFB_API int xfb_pair_logits_rows(const void* pair, int pair_dtype, int64_t rows,
                                  const float* norm_bias, double eps, const void* w, void* logits,
                                  void* stream);
 
+/* Routed stages: the same arithmetic as the stages above, with the exchange
+ * that follows each one done by the producer.  Instead of a local output the
+ * kernel stores every row straight into the receive buffer of the rank that
+ * needs it: dst[s] is rank s's buffer as mapped into this process (dst[rank]
+ * is this GPU's own; a CUDA IPC mapping for the others), world <= 16 ranks,
+ * this block = pair rows [rank * rows, (rank + 1) * rows) with rows * world =
+ * n.  Stores are plain 16-byte stores (no TMA, no multicast) and the kernel
+ * ends with a system-scope fence, so the caller's exchange barrier after it
+ * (xfb_exchange_signal / xfb_exchange_wait) publishes them.  No counterpart in
+ * the reference (it has no multi-GPU pair).
+ *
+ * xfb_triangle_projection_routed: as xfb_triangle_projection, but a and b
+ * channel ch of pair row i go to rank s = ch / (c / world) as
+ * a_dst[s] / b_dst[s] [c / world][n][n] at [ch % (c / world)][i][j] (the rows
+ * -> channels exchange); g stays local. */
+XFB_API int xfb_triangle_projection_routed(const void* pair, int pair_dtype, int64_t rows,
+                                           int64_t n, int64_t c, const float* mask,
+                                           const float* left_weight, const float* left_bias,
+                                           double left_eps, const void* packed,
+                                           void* const* a_dst, void* const* b_dst, int world,
+                                           int rank, void* g, void* workspace,
+                                           int64_t workspace_bytes, void* stream);
+
+/* The TriMul contraction of this rank's channel shard a, b [cs][n][n] bf16
+ * (outgoing z[c,i,j] = sum_k a[c,i,k] b[c,j,k]; incoming sum_k a[c,k,j]
+ * b[c,k,i]; triangle_multiplication.py:34-36), row i of channel ch stored as
+ * bf16 into rank s = i / (n / world) as z_dst[s] [world * cs][n / world][n] at
+ * [rank * cs + ch][i % (n / world)] (the channels -> rows exchange). */
+XFB_API int xfb_triangle_contraction_routed(const void* a, const void* b, int64_t cs, int64_t n,
+                                            int outgoing, void* const* z_dst, int world, int rank,
+                                            void* stream);
+
+/* xfb_grid_attention_prepare with the ending node's transpose: the LayerNorm'd
+ * row (i, j) goes to rank s = j / rows as x_dst[s] [rows][n][c] at
+ * [j % rows][rank * rows + i] (attention.py:97-98); the bias rows stay local.
+ * c = 128. */
+XFB_API int xfb_grid_attention_prepare_routed(const void* pair, int pair_dtype, int64_t rows,
+                                              int64_t n, int64_t c, int64_t heads,
+                                              const float* norm_weight, const float* norm_bias,
+                                              double eps, const void* bias_weight,
+                                              void* const* x_dst, int world, int rank, void* bias,
+                                              void* stream);
+
+/* xfb_grid_attention_rows for the ending node with the transpose back: the bf16
+ * update of column jj (this rank's rows of the transposed pair), pair row i,
+ * goes to rank s = i / rows as out_dst[s] [rows][n][c] at [i % rows][rank *
+ * rows + jj]; the owner adds it to its pair rows.  Workspace as
+ * xfb_grid_attention_rows_workspace. */
+XFB_API int xfb_grid_attention_rows_routed(const void* x, int64_t rows, int64_t n, int64_t c,
+                                           int64_t heads, const float* mask, const void* bias,
+                                           const void* packed, const void* output_w,
+                                           void* const* out_dst, int world, int rank,
+                                           void* workspace, int64_t workspace_bytes,
+                                           void* stream);
+
+/* Single-track attention of the query rows [row0, row0 + q_rows) of a
+ * row-sharded Pairformer (pairformer.py:102-108 for those rows): LayerNorm and
+ * the q / k / v / gate projections over all n tokens, attention of the query
+ * rows against every key with their pair logits [heads][q_rows][n] bf16 (the
+ * rows xfb_pair_logits_rows gives this rank, so the logits need no exchange),
+ * gated output projection into out rows [row0, row0 + q_rows) (f32 with
+ * accumulate = 1 adds into them).  packed as xfb_pack_attention_weights. */
+XFB_API int64_t xfb_self_attention_rows_workspace(int64_t n, int64_t c, int64_t heads,
+                                                  int64_t q_rows);
+XFB_API int xfb_self_attention_rows(const void* x, int x_dtype, int64_t n, int64_t c,
+                                    int64_t heads, int64_t row0, int64_t q_rows,
+                                    const float* mask, const void* pair_logits,
+                                    const float* norm_weight, const float* norm_bias, double eps,
+                                    const void* packed, const float* q_bias, const void* wo,
+                                    const void* out_gate, void* out, int out_dtype,
+                                    int accumulate, void* workspace, int64_t workspace_bytes,
+                                    void* stream);
+
 /* One block of an exchange between GPUs of a row-sharded pair: copy
  * [d0][d1][d2_bytes] from src to dst with byte strides (runs of d2_bytes are
  * contiguous on both sides).  dst may be another GPU's receive buffer mapped

@@ -12,7 +12,7 @@ points (a, b and z channel-major [c, rows, n]; bias [heads, rows, n]):
 * GridSelfAttention.forward, xfold/nn/attention.py:80-105 (LN and bias :86-98,
   attention on rows :61-78 with the un-transposed mask :99-100);
 * Transition, xfold/nn/primitives.py:33-37;
-* the single track, xfold/nn/pairformer.py:102-112.
+* the single track, xfold/nn/pairformer.py:102-112, by query rows.
 """
 
 from __future__ import annotations
@@ -80,7 +80,16 @@ class OracleStages:
         x = layer_norm(pair_rows, norm.weight, norm.bias)
         return linear(x, block.single_pair_logits_projection.weight).permute(2, 0, 1).contiguous()
 
-    def single_track(self, block, single, seq_mask, logits):
-        single += self_attention(single, seq_mask, logits, _sd(block.single_attention_), None,
-                                 block.n_heads, False)
-        single += transition(single, _sd(block.single_transition))
+    def single_attention_rows(self, block, x, seq_mask, logits_rows, row0, out):
+        """The single attention update of query rows [row0, row0 + q_rows): the
+        whole-track restatement with those rows' logits (queries are
+        independent, so the other logit rows do not matter)."""
+        heads, q_rows, n = logits_rows.shape
+        logits = torch.zeros((heads, n, n), dtype=torch.float32)
+        logits[:, row0:row0 + q_rows] = logits_rows.float()
+        upd = self_attention(x, seq_mask, logits, _sd(block.single_attention_), None,
+                             block.n_heads, False)
+        out[row0:row0 + q_rows] += upd[row0:row0 + q_rows]
+
+    def single_transition_rows(self, block, single_rows):
+        single_rows += transition(single_rows, _sd(block.single_transition))

@@ -123,8 +123,9 @@ def _problem(n, seed=17):
     return block, pair, single, seq, pmask
 
 
+@pytest.mark.parametrize("routed", [False, True])
 @pytest.mark.parametrize("world,n", [(2, 64), (4, 128)])
-def test_sharded_block_on_one_gpu(world, n):
+def test_sharded_block_on_one_gpu(world, n, routed):
     block, pair, single, seq, pmask = _problem(n)
     params = {k: v.detach().clone() for k, v in block.state_dict().items()}
     ref_p, ref_s = oracle.pairformer_block(pair, pmask, single, seq, params)
@@ -133,7 +134,7 @@ def test_sharded_block_on_one_gpu(world, n):
     s = single.to(DEV)
     with torch.inference_mode():
         sharded.pairformer_block(block, pairs, pmask.to(DEV), s, seq.to(DEV),
-                                 sharded.LocalExchange(world))
+                                 sharded.LocalExchange(world, routed=routed))
         whole_p, whole_s = pair.to(DEV), single.to(DEV)
         block(whole_p, pmask.to(DEV), whole_s, seq.to(DEV))
     got = torch.cat([p.cpu() for p in pairs])
@@ -141,6 +142,51 @@ def test_sharded_block_on_one_gpu(world, n):
     assert oracle.relative_error(s.cpu() - single, ref_s - single) < TOL
     # and close to the single-GPU block (same kernels, different blocking)
     assert oracle.relative_error(got - pair, whole_p.cpu() - pair) < TOL
+
+
+@pytest.mark.parametrize("world,n", [(2, 96), (4, 128), (8, 256)])
+def test_routed_stages_match_copy_exchange(world, n):
+    """The routed stages store exactly what the copy exchanges move: two
+    blocks, shards on one GPU, bit-identical pair and single."""
+    block, pair, single, seq, pmask = _problem(n, seed=29)
+    block = block.to(DEV)
+    out = {}
+    for routed in (False, True):
+        pairs = [pair[sharded.shard_rows(n, world, r)].to(DEV).contiguous()
+                 for r in range(world)]
+        s = single.to(DEV)
+        ex = sharded.LocalExchange(world, routed=routed)
+        with torch.inference_mode():
+            for _ in range(2):
+                sharded.pairformer_block(block, pairs, pmask.to(DEV), s, seq.to(DEV), ex)
+        out[routed] = (torch.cat(pairs).cpu(), s.cpu())
+    assert torch.equal(out[True][0], out[False][0])
+    assert torch.equal(out[True][1], out[False][1])
+
+
+def test_self_attention_rows_match_whole_track():
+    """Query-row shards of the single attention put together equal the whole
+    track's update (same kernels on the same tokens)."""
+    n, world = 256, 4
+    block, pair, single, seq, pmask = _problem(n, seed=31)
+    block = block.to(DEV)
+    st = sharded.NativeStages()
+    with torch.inference_mode():
+        p = pair.to(DEV)
+        logits = native.pair_logits(p, block.single_pair_logits_norm.weight,
+                                    block.single_pair_logits_norm.bias,
+                                    block.single_pair_logits_norm.eps,
+                                    block.single_pair_logits_projection.weight)
+        whole = single.to(DEV)
+        block.single_attention_.accumulate_(whole, seq.to(DEV), logits)
+        x_in = single.to(DEV)
+        parts = x_in.clone()
+        rows = n // world
+        for r in range(world):
+            st.single_attention_rows(block, x_in, seq.to(DEV),
+                                     logits[:, r * rows:(r + 1) * rows].contiguous(),
+                                     r * rows, parts)
+    assert _rel(parts - single.to(DEV), (whole - single.to(DEV)).cpu()) < 1e-3
 
 
 def _free_port():
@@ -235,9 +281,17 @@ def _peer_worker(rank, world, port, n, results):
         block = block.to(dev)
         mine = [pair[sharded.shard_rows(n, world, rank)].to(dev).contiguous()]
         s = single.to(dev)
+        copied = [mine[0].clone()]
+        s_copied = s.clone()
+        unrouted = sharded.PeerExchange(routed=False)
         with torch.inference_mode():
             for _ in range(2):  # two blocks: the exchanges reuse their receive buffers
                 sharded.pairformer_block(block, mine, pmask.to(dev), s, seq.to(dev), peer)
+            for _ in range(2):  # the same blocks with copy exchanges instead of routed stages
+                sharded.pairformer_block(block, copied, pmask.to(dev), s_copied, seq.to(dev),
+                                         unrouted)
+            results[f"routed_same{rank}"] = bool(torch.equal(mine[0], copied[0]) and
+                                                 torch.equal(s, s_copied))
             gathered = [torch.empty_like(mine[0]) for _ in range(world)]
             dist.all_gather(gathered, mine[0])
         torch.cuda.synchronize(dev)
@@ -268,5 +322,6 @@ def test_peer_exchange_over_nvlink():
         assert p.exitcode == 0
     for r in range(world):
         assert all(results[f"same{r}"].values()), results[f"same{r}"]
+        assert results[f"routed_same{r}"]
         assert results[f"err{r}"] == 0
     assert results["pair"] < TOL and results["single"] < TOL

@@ -89,6 +89,17 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_grid_attention_core_workspace": (_i64, [_i64, _i64]),
     "xfb_grid_attention_core": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
     "xfb_pair_logits_rows": (_i, [_p, _i, _i64, _i64, _i64, _i64, _p, _p, _d, _p, _p, _p]),
+    "xfb_triangle_projection_routed": (
+        _i, [_p, _i, _i64, _i64, _i64, _p, _p, _p, _d, _p, _p, _p, _i, _i, _p, _p, _i64, _p]),
+    "xfb_triangle_contraction_routed": (_i, [_p, _p, _i64, _i64, _i, _p, _i, _i, _p]),
+    "xfb_grid_attention_prepare_routed": (
+        _i, [_p, _i, _i64, _i64, _i64, _i64, _p, _p, _d, _p, _p, _i, _i, _p, _p]),
+    "xfb_grid_attention_rows_routed": (
+        _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _i64, _p]),
+    "xfb_self_attention_rows_workspace": (_i64, [_i64, _i64, _i64, _i64]),
+    "xfb_self_attention_rows": (
+        _i, [_p, _i, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _d, _p, _p, _p, _p, _p, _i,
+             _i, _p, _i64, _p]),
     "xfb_exchange_copy": (_i, [_p, _i, _p]),
     "xfb_ipc_handle_bytes": (_i64, []),
     "xfb_ipc_handle": (_i, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),

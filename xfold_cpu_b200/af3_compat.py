@@ -30,9 +30,12 @@ packed_weight_api = 0
 
 
 def load_extension():
-    """This module plays the role of af3_kernels._C."""
+    """This module plays the role of af3_kernels._C.  Like the reference's
+    load_native_operator (xfold/fastnn/native.py:7-18) it raises RuntimeError
+    when the native library is missing or lacks a symbol."""
     import sys
 
+    _capi.load()
     return sys.modules[__name__]
 
 

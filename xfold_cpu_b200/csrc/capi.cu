@@ -299,6 +299,25 @@ int linear_core(const bf16* x, int64_t m, int64_t k, int64_t ldx, const bf16* w,
                                                        accumulate, st);
 }
 
+// ------------------------------------------------------------------ routed exchanges
+
+// Destinations of a routed exchange as the C ABI passes them: dst[s] = rank s's
+// receive buffer as mapped in this process (dst[rank] is this GPU's own).
+struct Route {
+  void* const* dst;
+  int world, rank;
+};
+
+int check_route(void* const* dst, int world, int rank) {
+  XFB_REQUIRE(world >= 1 && world <= xfb::kMaxRoute, "routed exchanges take 1..16 ranks");
+  XFB_REQUIRE(rank >= 0 && rank < world, "rank out of range");
+  XFB_REQUIRE(dst != nullptr, "routed destinations missing");
+  for (int s = 0; s < world; ++s)
+    XFB_REQUIRE(dst[s] != nullptr && aligned16(dst[s]),
+                "routed destinations must be non-null and 16-byte aligned");
+  return XFB_OK;
+}
+
 // ------------------------------------------------------------------ LayerNorm launcher
 
 int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t ldx,
@@ -306,7 +325,8 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
                    const bf16* mod_scale, const bf16* mod_shift, const bf16* wh, int heads,
                    bf16* head_out, int64_t head_ld, cudaStream_t st, float head_scale = 1.f,
                    const int64_t* gather_idx = nullptr, const uint8_t* gather_valid = nullptr,
-                   int64_t src_rows = 0, int64_t perm_outer = 0, int64_t perm_inner = 0) {
+                   int64_t src_rows = 0, int64_t perm_outer = 0, int64_t perm_inner = 0,
+                   const Route* y_route = nullptr, int64_t route_n = 0) {
   if (rows <= 0) return XFB_OK;
   XFB_REQUIRE(x_dtype == XFB_F32 || x_dtype == XFB_BF16, "LayerNorm input must be f32 or bf16");
   XFB_REQUIRE(heads >= 0 && heads <= 16, "head projection supports at most 16 heads");
@@ -335,6 +355,21 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
   XFB_REQUIRE(gather_idx == nullptr || heads == 0, "row gather excludes the head projection");
   XFB_REQUIRE(perm_outer == 0 || (heads == 0 && perm_inner > 0 && perm_outer * perm_inner == rows),
               "row permutation must cover the rows and excludes the head projection");
+  if (y_route != nullptr) {
+    // the row <-> column transpose of a row-sharded pair (ln_heads_tc_kernel only)
+    XFB_REQUIRE(c == 128 && heads > 0 && mod_scale == nullptr && mod_shift == nullptr &&
+                    ldx % 4 == 0 && ldy % 4 == 0 && y != nullptr,
+                "a routed LayerNorm output needs c = 128 with a head projection");
+    XFB_REQUIRE(route_n > 0 && route_n % y_route->world == 0 && rows % route_n == 0 &&
+                    rows / route_n == route_n / y_route->world,
+                "a routed LayerNorm takes n / world pair rows of n columns");
+    a.route = 1;
+    a.route_rank = y_route->rank;
+    a.route_rows = static_cast<int>(route_n / y_route->world);
+    a.route_n = static_cast<int>(route_n);
+    for (int s = 0; s < 16; ++s)
+      a.y_dst[s] = s < y_route->world ? static_cast<bf16*>(y_route->dst[s]) : nullptr;
+  }
   int sms;
   XFB_TRY(sm_count(&sms));
   if (c == 128 && heads > 0 && mod_scale == nullptr && mod_shift == nullptr && ldx % 4 == 0 &&
@@ -343,7 +378,13 @@ int run_layer_norm(const void* x, int x_dtype, int64_t rows, int64_t c, int64_t 
     // registers x 256 threads, 36 KB shared memory and 32 TMEM columns each):
     // 184 -> 158 us for the 4-head bias at N = 1024 against four
     const int blocks = static_cast<int>(std::min<int64_t>((rows + 127) / 128, int64_t(sms) * 6));
-    if (x_dtype == XFB_F32) {
+    if (a.route) {
+      if (x_dtype == XFB_F32) {
+        xfb::ln_heads_tc_kernel<float, true><<<blocks, 256, 0, st>>>(a);
+      } else {
+        xfb::ln_heads_tc_kernel<bf16, true><<<blocks, 256, 0, st>>>(a);
+      }
+    } else if (x_dtype == XFB_F32) {
       xfb::ln_heads_tc_kernel<float><<<blocks, 256, 0, st>>>(a);
     } else {
       xfb::ln_heads_tc_kernel<bf16><<<blocks, 256, 0, st>>>(a);
@@ -1536,15 +1577,19 @@ XFB_API int64_t xfb_self_attention_workspace(int64_t n, int64_t c, int64_t heads
   return cv.used;
 }
 
-XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c, int64_t heads,
-                               const float* mask, const void* pair_logits,
-                               const float* norm_weight, const float* norm_bias, double eps,
-                               const void* mod_scale, const void* mod_shift, const void* q_w,
-                               const float* q_bias, const void* k_w, const void* v_w,
-                               const void* gate_w, int weights_packed, const void* packed,
-                               const void* wo, const void* out_gate, void* out, int out_dtype,
-                               int accumulate, void* workspace, int64_t workspace_bytes,
-                               void* stream) {
+namespace {
+// Self-attention of the query rows [row0, row0 + q_rows) against all n keys;
+// LayerNorm and projections run on all n tokens (the keys need them), the
+// attention, output projection and update only on the query rows, whose pair
+// logits are `pair_logits` [heads][q_rows][n].
+int self_attention_impl(const void* x, int x_dtype, int64_t n, int64_t c, int64_t heads,
+                        int64_t row0, int64_t q_rows, const float* mask, const void* pair_logits,
+                        const float* norm_weight, const float* norm_bias, double eps,
+                        const void* mod_scale, const void* mod_shift, const void* q_w,
+                        const float* q_bias, const void* k_w, const void* v_w, const void* gate_w,
+                        int weights_packed, const void* packed, const void* wo,
+                        const void* out_gate, void* out, int out_dtype, int accumulate,
+                        void* workspace, int64_t workspace_bytes, void* stream) {
   XFB_REQUIRE(n >= 0, "token count must be non-negative");
   XFB_REQUIRE(c == 128 || c == 384 || c == 768, "self-attention width must be 128, 384 or 768");
   XFB_REQUIRE(heads > 0 && c % heads == 0 && c / heads <= 64, "heads must divide c, d <= 64");
@@ -1555,15 +1600,19 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
               "attention weights missing");
   XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
   XFB_REQUIRE(aligned16(out), "output must be 16-byte aligned");
-  if (n == 0) return XFB_OK;
+  XFB_REQUIRE(row0 >= 0 && q_rows >= 0 && row0 + q_rows <= n, "query rows out of range");
+  if (n == 0 || q_rows == 0) return XFB_OK;
   XFB_REQUIRE(n <= 16384, "self-attention supports at most 16384 tokens");
+  const bool subset = q_rows != n;
+  XFB_REQUIRE(!subset || (row0 * c) % 8 == 0, "query rows must start on a 16-byte boundary");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
   SaWs w;
   sa_layout(cv, n, c, heads, !weights_packed, &w);
-  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
   const int64_t d = c / heads;
   const int dp = head_pitch(d);
+  bf16* q_sub = subset ? cv.take<bf16>(heads * q_rows * dp) : nullptr;
+  XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
   const bf16* wcat = static_cast<const bf16*>(packed);
   if (!weights_packed) {
     XFB_TRY(launch_pack(q_w, k_w, v_w, gate_w, XFB_BF16, 2, c, c, 4 * c, w.packed, st));
@@ -1595,11 +1644,19 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
     epi.q_bias = q_bias;
     XFB_TRY((run_gemm<128, false, false>(w.x, c, 0, wcat, c, 0, n, 4 * c, c, 1, epi, st)));
   }
+  const bf16* q = w.q;
+  if (subset) {
+    // the query rows of every head, [heads][q_rows][dp]
+    XFB_CUDA(cudaMemcpy2DAsync(q_sub, q_rows * dp * 2, w.q + row0 * dp, n * dp * 2,
+                               q_rows * dp * 2, heads, cudaMemcpyDeviceToDevice, st));
+    q = q_sub;
+  }
+  bf16* o = w.x + row0 * c;  // the LayerNorm'd tokens are no longer needed
   {
     xfb::AttnArgs a;
     a.B = 1;
     a.H = static_cast<int>(heads);
-    a.nq = static_cast<int>(n);
+    a.nq = static_cast<int>(q_rows);
     a.nk = static_cast<int>(n);
     a.d = static_cast<int>(d);
     if (mask != nullptr) XFB_TRY(launch_mask_bits(mask, true, 1, n, n, w.bits, st));
@@ -1607,22 +1664,64 @@ XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c,
     a.mask_sb = 0;
     a.bias = pair_logits;
     a.bias_sb = 0;
-    a.bias_sh = n * n;
+    a.bias_sh = q_rows * n;
     a.bias_sq = n;
     a.bias_batched = 0;
-    a.out = w.x;
+    a.out = o;
     a.out_sb = 0;
     a.out_sh = d;
     a.out_sq = c;
-    a.gate = w.g;
+    a.gate = w.g + row0 * c;
     a.gate_sb = 0;
     a.gate_sh = d;
     a.gate_sq = c;
-    XFB_TRY(run_flash(dp, XFB_BF16, false, w.q, w.k, w.v, a, st));
+    XFB_TRY(run_flash(dp, XFB_BF16, false, q, w.k, w.v, a, st));
   }
-  return linear_core(w.x, n, c, c, static_cast<const bf16*>(wo), c, nullptr,
-                     static_cast<const bf16*>(out_gate), c, out, out_dtype == XFB_F32,
-                     accumulate, c, st);
+  const bf16* og = out_gate ? static_cast<const bf16*>(out_gate) + row0 * c : nullptr;
+  void* out_rows = static_cast<uint8_t*>(out) + row0 * c * (out_dtype == XFB_F32 ? 4 : 2);
+  return linear_core(o, q_rows, c, c, static_cast<const bf16*>(wo), c, nullptr, og, c, out_rows,
+                     out_dtype == XFB_F32, accumulate, c, st);
+}
+}  // namespace
+
+XFB_API int xfb_self_attention(const void* x, int x_dtype, int64_t n, int64_t c, int64_t heads,
+                               const float* mask, const void* pair_logits,
+                               const float* norm_weight, const float* norm_bias, double eps,
+                               const void* mod_scale, const void* mod_shift, const void* q_w,
+                               const float* q_bias, const void* k_w, const void* v_w,
+                               const void* gate_w, int weights_packed, const void* packed,
+                               const void* wo, const void* out_gate, void* out, int out_dtype,
+                               int accumulate, void* workspace, int64_t workspace_bytes,
+                               void* stream) {
+  return self_attention_impl(x, x_dtype, n, c, heads, 0, n, mask, pair_logits, norm_weight,
+                             norm_bias, eps, mod_scale, mod_shift, q_w, q_bias, k_w, v_w, gate_w,
+                             weights_packed, packed, wo, out_gate, out, out_dtype, accumulate,
+                             workspace, workspace_bytes, stream);
+}
+
+XFB_API int64_t xfb_self_attention_rows_workspace(int64_t n, int64_t c, int64_t heads,
+                                                  int64_t q_rows) {
+  if (heads <= 0) return 0;
+  Carver cv{nullptr, 0, 0};
+  SaWs w;
+  sa_layout(cv, n, c, heads, false, &w);
+  cv.take<bf16>(heads * q_rows * head_pitch(c / heads));
+  return cv.used;
+}
+
+XFB_API int xfb_self_attention_rows(const void* x, int x_dtype, int64_t n, int64_t c,
+                                    int64_t heads, int64_t row0, int64_t q_rows,
+                                    const float* mask, const void* pair_logits,
+                                    const float* norm_weight, const float* norm_bias, double eps,
+                                    const void* packed, const float* q_bias, const void* wo,
+                                    const void* out_gate, void* out, int out_dtype,
+                                    int accumulate, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
+  XFB_REQUIRE(packed != nullptr, "packed attention weights are required");
+  return self_attention_impl(x, x_dtype, n, c, heads, row0, q_rows, mask, pair_logits,
+                             norm_weight, norm_bias, eps, nullptr, nullptr, nullptr, q_bias,
+                             nullptr, nullptr, nullptr, 1, packed, wo, out_gate, out, out_dtype,
+                             accumulate, workspace, workspace_bytes, stream);
 }
 
 XFB_API int xfb_pair_logits(const void* pair, int pair_dtype, int64_t n, int64_t c,
@@ -1674,11 +1773,12 @@ XFB_API int64_t xfb_triangle_projection_workspace(int64_t rows, int64_t n, int64
   return cv.used;
 }
 
-XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t rows, int64_t n,
-                                    int64_t c, const float* mask, const float* left_weight,
-                                    const float* left_bias, double left_eps, const void* packed,
-                                    void* a, void* b, void* g, void* workspace,
-                                    int64_t workspace_bytes, void* stream) {
+namespace {
+int triangle_projection_impl(const void* pair, int pair_dtype, int64_t rows, int64_t n, int64_t c,
+                             const float* mask, const float* left_weight, const float* left_bias,
+                             double left_eps, const void* packed, void* a, void* b,
+                             const Route* ra, const Route* rb, void* g, void* workspace,
+                             int64_t workspace_bytes, cudaStream_t st) {
   XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
   XFB_REQUIRE(c == 64 || c == 128, "triangle multiplication supports c in {64, 128}");
   XFB_REQUIRE(packed != nullptr, "packed triangle weights are required");
@@ -1686,21 +1786,38 @@ XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t ro
   XFB_REQUIRE(aligned16(a) && aligned16(b) && aligned16(g), "a, b, g must be 16-byte aligned");
   if (rows == 0 || n == 0) return XFB_OK;
   XFB_REQUIRE(rows * n <= (1ll << 31) - 256, "row block too large");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver cv{static_cast<uint8_t*>(workspace), 0, workspace_bytes};
   bf16* x = cv.take<bf16>(rows * n * c);
   XFB_TRY(check_workspace(cv, workspace, workspace_bytes));
   XFB_TRY(run_layer_norm(pair, pair_dtype, rows * n, c, c, left_weight, left_bias, left_eps, x, c,
                          nullptr, nullptr, nullptr, 0, nullptr, 0, st));
   xfb::EpiTriProj epi;
-  const uint64_t ab_dims[3] = {static_cast<uint64_t>(n), static_cast<uint64_t>(rows),
-                               static_cast<uint64_t>(c)};
-  const uint64_t ab_strides[2] = {static_cast<uint64_t>(n * 2), static_cast<uint64_t>(rows * n * 2)};
-  const uint32_t ab_box[3] = {128, 1, 32};
-  XFB_TRY(make_map_nd(&epi.a_map, false, 3, a, ab_dims, ab_strides, ab_box,
-                      CU_TENSOR_MAP_SWIZZLE_NONE));
-  XFB_TRY(make_map_nd(&epi.b_map, false, 3, b, ab_dims, ab_strides, ab_box,
-                      CU_TENSOR_MAP_SWIZZLE_NONE));
+  if (ra != nullptr) {
+    // rows -> channels by the producer: rank s receives channels [s cs, (s+1) cs)
+    // of every row block as [cs][n][n]
+    XFB_REQUIRE(rows * ra->world == n && c % ra->world == 0,
+                "a routed row block holds n / world rows and c / world channels per rank");
+    std::memset(&epi.a_map, 0, sizeof(epi.a_map));
+    std::memset(&epi.b_map, 0, sizeof(epi.b_map));
+    epi.route = 1;
+    epi.rank = ra->rank;
+    epi.route_rows = static_cast<int>(rows);
+    epi.route_cs = static_cast<int>(c / ra->world);
+    for (int s = 0; s < xfb::kMaxRoute; ++s) {
+      epi.a_dst[s] = s < ra->world ? ra->dst[s] : nullptr;
+      epi.b_dst[s] = s < rb->world ? rb->dst[s] : nullptr;
+    }
+  } else {
+    const uint64_t ab_dims[3] = {static_cast<uint64_t>(n), static_cast<uint64_t>(rows),
+                                 static_cast<uint64_t>(c)};
+    const uint64_t ab_strides[2] = {static_cast<uint64_t>(n * 2),
+                                    static_cast<uint64_t>(rows * n * 2)};
+    const uint32_t ab_box[3] = {128, 1, 32};
+    XFB_TRY(make_map_nd(&epi.a_map, false, 3, a, ab_dims, ab_strides, ab_box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE));
+    XFB_TRY(make_map_nd(&epi.b_map, false, 3, b, ab_dims, ab_strides, ab_box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
   const uint64_t g_dims[3] = {static_cast<uint64_t>(c), static_cast<uint64_t>(n),
                               static_cast<uint64_t>(rows)};
   const uint64_t g_strides[2] = {static_cast<uint64_t>(c * 2), static_cast<uint64_t>(n * c * 2)};
@@ -1712,6 +1829,64 @@ XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t ro
   epi.n_proj_tiles = static_cast<int>(2 * c / 64);
   epi.c = static_cast<int>(c);
   return run_gemm<128, false, false>(x, c, n * c, packed, c, 0, n, 5 * c, c, rows, epi, st, true);
+}
+}  // namespace
+
+XFB_API int xfb_triangle_projection(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                    int64_t c, const float* mask, const float* left_weight,
+                                    const float* left_bias, double left_eps, const void* packed,
+                                    void* a, void* b, void* g, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
+  return triangle_projection_impl(pair, pair_dtype, rows, n, c, mask, left_weight, left_bias,
+                                  left_eps, packed, a, b, nullptr, nullptr, g, workspace,
+                                  workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+XFB_API int xfb_triangle_projection_routed(const void* pair, int pair_dtype, int64_t rows,
+                                           int64_t n, int64_t c, const float* mask,
+                                           const float* left_weight, const float* left_bias,
+                                           double left_eps, const void* packed,
+                                           void* const* a_dst, void* const* b_dst, int world,
+                                           int rank, void* g, void* workspace,
+                                           int64_t workspace_bytes, void* stream) {
+  XFB_TRY(check_route(a_dst, world, rank));
+  XFB_TRY(check_route(b_dst, world, rank));
+  const Route ra{a_dst, world, rank}, rb{b_dst, world, rank};
+  return triangle_projection_impl(pair, pair_dtype, rows, n, c, mask, left_weight, left_bias,
+                                  left_eps, packed, a_dst[rank], b_dst[rank], &ra, &rb, g,
+                                  workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+XFB_API int xfb_triangle_contraction_routed(const void* a, const void* b, int64_t cs, int64_t n,
+                                            int outgoing, void* const* z_dst, int world, int rank,
+                                            void* stream) {
+  XFB_TRY(check_route(z_dst, world, rank));
+  XFB_REQUIRE(cs >= 0 && n >= 0 && n % 8 == 0, "the contraction needs n % 8 == 0");
+  XFB_REQUIRE(n % world == 0, "a routed contraction splits n rows evenly over the ranks");
+  XFB_REQUIRE(aligned16(a) && aligned16(b), "a and b must be 16-byte aligned");
+  if (cs == 0 || n == 0) return XFB_OK;
+  xfb::EpiDirect<256> epi;
+  epi.out = z_dst[rank];
+  epi.ld_out = n;
+  epi.bstride_out = n * n;
+  epi.out_f32 = 0;
+  epi.accumulate = 0;
+  epi.bias = nullptr;
+  epi.gate = nullptr;
+  epi.ld_gate = 0;
+  epi.M = static_cast<int>(n);
+  epi.N = static_cast<int>(n);
+  epi.route = 1;
+  epi.rank = rank;
+  epi.route_rows = static_cast<int>(n / world);
+  epi.route_batch = static_cast<int>(cs);
+  epi.route_n = static_cast<int>(n);
+  for (int s = 0; s < xfb::kMaxRoute; ++s) epi.dst[s] = s < world ? z_dst[s] : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t bs = n * n;
+  // outgoing z[c,i,j] = sum_k a[c,i,k] b[c,j,k]; incoming sum_k a[c,k,j] b[c,k,i]
+  if (outgoing) return run_gemm<256, false, false>(a, n, bs, b, n, bs, n, n, n, cs, epi, st);
+  return run_gemm<256, true, true>(b, n, bs, a, n, bs, n, n, n, cs, epi, st);
 }
 
 XFB_API int64_t xfb_triangle_output_workspace(int64_t rows, int64_t n, int64_t c) {
@@ -1747,10 +1922,11 @@ XFB_API int xfb_triangle_output(const void* z, int64_t rows, int64_t n, int64_t 
                            accumulate, w, st);
 }
 
-XFB_API int xfb_grid_attention_prepare(const void* pair, int pair_dtype, int64_t rows, int64_t n,
-                                       int64_t c, int64_t heads, const float* norm_weight,
-                                       const float* norm_bias, double eps, const void* bias_weight,
-                                       void* x, void* bias, void* stream) {
+namespace {
+int grid_attention_prepare_impl(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                int64_t c, int64_t heads, const float* norm_weight,
+                                const float* norm_bias, double eps, const void* bias_weight,
+                                void* x, const Route* x_route, void* bias, void* stream) {
   XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
   XFB_REQUIRE(c == 64 || c == 128, "grid self-attention supports c in {64, 128}");
   XFB_REQUIRE(heads > 0 && heads <= 16 && c % heads == 0, "heads must divide c (<= 16)");
@@ -1763,7 +1939,29 @@ XFB_API int xfb_grid_attention_prepare(const void* pair, int pair_dtype, int64_t
                         static_cast<bf16*>(x), c, nullptr, nullptr,
                         static_cast<const bf16*>(bias_weight), static_cast<int>(heads),
                         static_cast<bf16*>(bias), rows * n, static_cast<cudaStream_t>(stream),
-                        scale);
+                        scale, nullptr, nullptr, 0, 0, 0, x_route, n);
+}
+}  // namespace
+
+XFB_API int xfb_grid_attention_prepare(const void* pair, int pair_dtype, int64_t rows, int64_t n,
+                                       int64_t c, int64_t heads, const float* norm_weight,
+                                       const float* norm_bias, double eps, const void* bias_weight,
+                                       void* x, void* bias, void* stream) {
+  return grid_attention_prepare_impl(pair, pair_dtype, rows, n, c, heads, norm_weight, norm_bias,
+                                     eps, bias_weight, x, nullptr, bias, stream);
+}
+
+XFB_API int xfb_grid_attention_prepare_routed(const void* pair, int pair_dtype, int64_t rows,
+                                              int64_t n, int64_t c, int64_t heads,
+                                              const float* norm_weight, const float* norm_bias,
+                                              double eps, const void* bias_weight,
+                                              void* const* x_dst, int world, int rank, void* bias,
+                                              void* stream) {
+  XFB_TRY(check_route(x_dst, world, rank));
+  XFB_REQUIRE(rows * world == n, "a routed row block holds n / world rows");
+  const Route r{x_dst, world, rank};
+  return grid_attention_prepare_impl(pair, pair_dtype, rows, n, c, heads, norm_weight, norm_bias,
+                                     eps, bias_weight, x_dst[rank], &r, bias, stream);
 }
 
 XFB_API int64_t xfb_grid_attention_rows_workspace(int64_t rows, int64_t n, int64_t c,
@@ -1775,11 +1973,12 @@ XFB_API int64_t xfb_grid_attention_rows_workspace(int64_t rows, int64_t n, int64
   return cv.used;
 }
 
-XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int64_t c,
-                                    int64_t heads, const float* mask, const void* bias,
-                                    const void* packed, const void* output_w, void* out,
-                                    int out_dtype, int accumulate, void* workspace,
-                                    int64_t workspace_bytes, void* stream) {
+namespace {
+int grid_attention_rows_impl(const void* x, int64_t rows, int64_t n, int64_t c, int64_t heads,
+                             const float* mask, const void* bias, const void* packed,
+                             const void* output_w, void* out, int out_dtype, int accumulate,
+                             const Route* out_route, void* workspace, int64_t workspace_bytes,
+                             void* stream) {
   XFB_REQUIRE(rows >= 0 && n >= 0 && n % 8 == 0, "row blocks need n % 8 == 0 columns");
   XFB_REQUIRE(c == 64 || c == 128, "grid self-attention supports c in {64, 128}");
   XFB_REQUIRE(heads > 0 && heads <= 16 && c % heads == 0, "heads must divide c (<= 16)");
@@ -1868,8 +2067,55 @@ XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int6
   a.gate_sh = a.out_sh;
   a.gate_sq = a.out_sq;
   XFB_TRY(run_flash(dp, XFB_BF16, pre, w.q, w.k, w.v, a, st));
+  if (out_route != nullptr) {
+    // the update of column block jj, pair row i, goes back to the owner of row i
+    xfb::EpiDirect<128> epi;
+    epi.out = out;
+    epi.ld_out = c;
+    epi.bstride_out = 0;
+    epi.out_f32 = 0;
+    epi.accumulate = 0;
+    epi.bias = nullptr;
+    epi.gate = nullptr;
+    epi.ld_gate = 0;
+    epi.M = static_cast<int>(rows * n);
+    epi.N = static_cast<int>(c);
+    epi.route = 2;
+    epi.rank = out_route->rank;
+    epi.route_rows = static_cast<int>(rows);
+    epi.route_batch = 0;
+    epi.route_n = static_cast<int>(n);
+    for (int s = 0; s < xfb::kMaxRoute; ++s)
+      epi.dst[s] = s < out_route->world ? out_route->dst[s] : nullptr;
+    return run_gemm<128, false, false>(w.o, c, 0, output_w, c, 0, rows * n, c, c, 1, epi, st);
+  }
   return linear_core(w.o, rows * n, c, c, static_cast<const bf16*>(output_w), c, nullptr, nullptr,
                      0, out, out_dtype == XFB_F32, accumulate, c, st);
+}
+}  // namespace
+
+XFB_API int xfb_grid_attention_rows(const void* x, int64_t rows, int64_t n, int64_t c,
+                                    int64_t heads, const float* mask, const void* bias,
+                                    const void* packed, const void* output_w, void* out,
+                                    int out_dtype, int accumulate, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
+  return grid_attention_rows_impl(x, rows, n, c, heads, mask, bias, packed, output_w, out,
+                                  out_dtype, accumulate, nullptr, workspace, workspace_bytes,
+                                  stream);
+}
+
+XFB_API int xfb_grid_attention_rows_routed(const void* x, int64_t rows, int64_t n, int64_t c,
+                                           int64_t heads, const float* mask, const void* bias,
+                                           const void* packed, const void* output_w,
+                                           void* const* out_dst, int world, int rank,
+                                           void* workspace, int64_t workspace_bytes,
+                                           void* stream) {
+  XFB_TRY(check_route(out_dst, world, rank));
+  XFB_REQUIRE(rows * world == n, "a routed row block holds n / world rows");
+  const Route r{out_dst, world, rank};
+  return grid_attention_rows_impl(x, rows, n, c, heads, mask, bias, packed, output_w,
+                                  out_dst[rank], XFB_BF16, 0, &r, workspace, workspace_bytes,
+                                  stream);
 }
 
 XFB_API int64_t xfb_grid_attention_core_workspace(int64_t rows, int64_t n) {

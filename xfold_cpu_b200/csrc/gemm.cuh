@@ -49,6 +49,34 @@ struct EpiGroupsOf<E, std::void_t<decltype(E::kGroups)>> {
   static constexpr int value = E::kGroups;
 };
 
+// Epilogues with `route` (an int member) may store into other GPUs' receive
+// buffers: the kernel then ends with a system-scope fence in every thread, so
+// the exchange barrier that follows on the stream publishes those stores.
+template <class E, class = void>
+struct EpiRoutedOf {
+  static constexpr bool value = false;
+};
+template <class E>
+struct EpiRoutedOf<E, std::void_t<decltype(E::route)>> {
+  static constexpr bool value = true;
+};
+
+// Epilogues with kLaneStores = true have all 32 lanes of the store warp call
+// Epi::store_lanes(ctx, lane) after Epi::store (lane 0): plain 16-byte stores
+// from the staged tile, for destinations no tensor map describes.
+template <class E, class = void>
+struct EpiLaneStoresOf {
+  static constexpr bool value = false;
+};
+template <class E>
+struct EpiLaneStoresOf<E, std::void_t<decltype(E::kLaneStores)>> {
+  static constexpr bool value = E::kLaneStores;
+};
+
+// Destinations of a routed store: one receive buffer per rank of the exchange
+// (this GPU's own buffer among them), as mapped in this process.
+constexpr int kMaxRoute = 16;
+
 // Warp layout of the GEMM kernel for epilogue Epi: the epilogue group(s), then
 // the TMA producer, the MMA issuer and the bulk-store issuer.
 template <class Epi>
@@ -255,7 +283,38 @@ __global__ void __launch_bounds__(GemmWarps<Epi>::kThreads, 1)
     // Takes each staged tile once every epilogue thread has written it, issues
     // the epilogue's TMA store, and frees the staging buffer as soon as that
     // store has read it.  The epilogue warps never wait for one another.
-    if constexpr (Epi::kStagingBytes > 0) {
+    if constexpr (Epi::kStagingBytes > 0 && EpiLaneStoresOf<Epi>::value) {
+      // every lane takes part: lane 0 issues the TMA stores, then all lanes
+      // copy what the epilogue routes elsewhere out of the staged tile
+      constexpr int NB = Epi::kStagingBufs;
+      int iter = 0;
+      EpiCtx ctx;
+      ctx.row = 0;
+      ctx.half = 0;
+      ctx.tmem = 0;
+      ctx.aux = nullptr;
+      for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
+        const int b = iter % NB;
+        const uint32_t ph = (iter / NB) & 1;
+        const bool ok = mbar_wait(&staging_full[b], ph, kErrWaitEpilogue, abort_flag);
+        const int bat = tile / tiles_per_batch;
+        const int rem = tile - bat * tiles_per_batch;
+        ctx.bat = bat;
+        ctx.m0 = (rem / shape.n_tiles) * kGemmBM;
+        ctx.n0 = (rem % shape.n_tiles) * BN;
+        ctx.staging = smem + L::kStagingOff + b * L::kStagingStride;
+        const bool go = ok && !*abort_flag;
+        if (lane == 0) {
+          if (go) epi.store(ctx);
+          bulk_commit();
+        }
+        if (go) epi.store_lanes(ctx, lane);
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();  // every lane's shared-memory reads of this buffer are done
+        if (lane == 0) mbar_arrive(&staging_free[b]);
+      }
+      if (lane == 0) bulk_wait<0>();
+    } else if constexpr (Epi::kStagingBytes > 0) {
       if (lane == 0) {
         constexpr int NB = Epi::kStagingBufs;
         int iter = 0;
@@ -334,6 +393,9 @@ __global__ void __launch_bounds__(GemmWarps<Epi>::kThreads, 1)
     }
   }
 
+  if constexpr (EpiRoutedOf<Epi>::value) {
+    if (epi.route) __threadfence_system();
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == kGemmMmaWarp) {
@@ -529,6 +591,16 @@ struct EpiOutLnGated : EpiOutGated<BN, OUT_F32> {
 // Direct per-thread stores (no staging): out [bat][m][ld] bf16 or f32.  Used by
 // the batched contraction (whose rows are 512-byte contiguous runs) and by odd
 // shapes the TMA layouts do not cover.
+//
+// With route != 0 each output row goes to the receive buffer of the rank that
+// owns it (dst[s], s = that rank; this rank is `rank`) instead of `out`:
+//   route 1, channels -> rows: row i of channel `bat` (a contraction over this
+//     rank's route_batch channels) is row i % route_rows of channel
+//     rank * route_batch + bat on rank s = i / route_rows
+//     (receive buffer [G * route_batch][route_rows][ld_out]);
+//   route 2, transpose: row jj * route_n + i (this rank's column block jj, pair
+//     row i) is row (i % route_rows) * route_n + rank * route_rows + jj on rank
+//     s = i / route_rows (receive buffer [route_rows][route_n][ld_out]).
 template <int BN>
 struct EpiDirect {
   static constexpr int kStagingBytes = 0;
@@ -543,6 +615,9 @@ struct EpiDirect {
   const __nv_bfloat16* gate;
   int64_t ld_gate;
   int M, N;
+  int route = 0;
+  int rank, route_rows, route_batch, route_n;
+  void* dst[kMaxRoute];
 
   __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
   __device__ void store(const EpiCtx&) const {}
@@ -551,7 +626,23 @@ struct EpiDirect {
     constexpr int kHalf = BN / 2;
     const int row = c.m0 + c.row;
     const bool row_ok = row < M;
-    const int64_t row_off = c.bat * bstride_out + static_cast<int64_t>(row) * ld_out;
+    int64_t row_off = c.bat * bstride_out + static_cast<int64_t>(row) * ld_out;
+    void* obase = out;
+    if (route != 0 && row_ok) {
+      if (route == 1) {
+        const int s = row / route_rows;
+        obase = dst[s];
+        row_off = (static_cast<int64_t>(rank * route_batch + c.bat) * route_rows +
+                   (row - s * route_rows)) * ld_out;
+      } else {
+        const int jj = row / route_n;
+        const int i = row - jj * route_n;
+        const int s = i / route_rows;
+        obase = dst[s];
+        row_off = (static_cast<int64_t>(i - s * route_rows) * route_n + rank * route_rows + jj) *
+                  ld_out;
+      }
+    }
     const __nv_bfloat16* grow = gate ? gate + static_cast<int64_t>(row) * ld_gate : nullptr;
 #pragma unroll 1
     for (int c0 = 0; c0 < kHalf; c0 += 16) {
@@ -574,7 +665,7 @@ struct EpiDirect {
         }
       }
       if (out_f32) {
-        float* orow = reinterpret_cast<float*>(out) + row_off;
+        float* orow = reinterpret_cast<float*>(obase) + row_off;
         if (full) {
           float4* dst = reinterpret_cast<float4*>(orow + col);
 #pragma unroll
@@ -595,7 +686,7 @@ struct EpiDirect {
             if (col + i < N) orow[col + i] = accumulate ? orow[col + i] + v[i] : v[i];
         }
       } else {
-        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(out) + row_off;
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(obase) + row_off;
         if (full) {
           store16_bf16(orow + col, v);
         } else {
@@ -643,14 +734,24 @@ struct EpiGLU {
 //   g[i][j][c'] = sigmoid(x . w_gating[c'])
 // a / b maps: 3-D {n (j), n (i), c}, box {128, 1, 32}, no swizzle;
 // g map: 3-D {c, n (j), n (i)}, box {64, 128, 1}, 128-byte swizzle.
+// With route = 1 (a row block of a row-sharded pair: pair row i = rank *
+// route_rows + bat) a and b skip their maps: the store warp's lanes write
+// channel ch straight into rank s = ch / route_cs's receive buffer
+// a_dst[s] / b_dst[s] [route_cs][n][n] at [ch % route_cs][i][j] -- the rows ->
+// channels exchange done by the producer.
 struct EpiTriProj {
   static constexpr int kStagingBytes = 32768;
   static constexpr int kStagingBufs = 2;
   static constexpr int kGroups = 2;
   static constexpr int kAuxBytes = 0;
+  static constexpr bool kLaneStores = true;
   CUtensorMap a_map, b_map, g_map;
   const float* mask;  // [n][n] or null
   int n, n_proj_tiles, c;
+  int route = 0;
+  int rank, route_rows, route_cs;
+  void* a_dst[kMaxRoute];
+  void* b_dst[kMaxRoute];
 
   __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
 
@@ -692,11 +793,36 @@ struct EpiTriProj {
   __device__ void store(const EpiCtx& c) const {
     const int tile = c.n0 / 128;
     if (tile < n_proj_tiles) {
+      if (route) return;  // store_lanes
       tma_store_3d(&a_map, c.staging, c.m0, c.bat, tile * 32);
       tma_store_3d(&b_map, c.staging + 8192, c.m0, c.bat, tile * 32);
     } else {
       tma_store_3d(&g_map, c.staging, 0, c.m0, c.bat);
       if (this->c > 64) tma_store_3d(&g_map, c.staging + 16384, 64, c.m0, c.bat);
+    }
+  }
+
+  // a / b tile [32 channels][128 j] bf16 each: 16-byte pieces, channel by
+  // channel, into the owners' receive buffers (n % 8 == 0, so a piece never
+  // straddles the end of a row)
+  __device__ void store_lanes(const EpiCtx& c, int lane) const {
+    const int tile = c.n0 / 128;
+    if (!route || tile >= n_proj_tiles) return;
+    const int64_t i = static_cast<int64_t>(rank) * route_rows + c.bat;
+#pragma unroll 4
+    for (int idx = lane; idx < 2 * 32 * 16; idx += 32) {
+      const int which = idx >> 9;  // 0: a, 1: b
+      const int ch = (idx >> 4) & 31;
+      const int piece = idx & 15;
+      const int j = c.m0 + piece * 8;
+      if (j >= n) continue;
+      const int gch = tile * 32 + ch;
+      const int s = gch / route_cs;
+      const uint4 v =
+          *reinterpret_cast<const uint4*>(c.staging + which * 8192 + (ch * 128 + piece * 8) * 2);
+      __nv_bfloat16* base = static_cast<__nv_bfloat16*>(which ? b_dst[s] : a_dst[s]);
+      *reinterpret_cast<uint4*>(base + (static_cast<int64_t>(gch - s * route_cs) * n + i) * n + j) =
+          v;
     }
   }
 };

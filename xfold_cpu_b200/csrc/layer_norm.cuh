@@ -64,6 +64,13 @@ struct LnArgs {
   const uint8_t* gather_valid;     // [rows] zero = the output row reads zeros; or null
   int64_t src_rows;                // rows of x that gather_idx may address
   int64_t perm_outer, perm_inner;  // > 0: input row b*inner + k writes y row k*outer + b
+  // ln_heads_tc_kernel only: with route = 1, y row r = i * route_n + j (pair row
+  // i of this rank's block, column j) goes to rank s = j / route_rows as row
+  // (j % route_rows) * route_n + route_rank * route_rows + i of y_dst[s] -- the
+  // row <-> column transpose of a row-sharded pair, done by the producer.
+  int route = 0;
+  int route_rank, route_rows, route_n;
+  __nv_bfloat16* y_dst[16];
 };
 
 // C = 32 * 4 * R channels: each lane holds R groups of 4 consecutive channels.
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(256) ln_rows64_kernel(LnArgs a) {
 // back, one row per thread, and store them head-major, coalesced along rows.
 // The products are those of ln_rows_kernel's head path: bf16(normalised x) times
 // bf16 weights, accumulated in f32.
-template <typename InT>
+template <typename InT, bool ROUTE = false>
 __global__ void __launch_bounds__(256) ln_heads_tc_kernel(LnArgs a) {
   __shared__ __align__(1024) uint8_t sA[2 * 16384];  // k-halves of 64 channels
   __shared__ __align__(1024) uint8_t sB[2 * 2048];   // 16 heads x 64 channels per half
@@ -446,7 +453,17 @@ __global__ void __launch_bounds__(256) ln_heads_tc_kernel(LnArgs a) {
         for (int e = 0; e < 4; ++e) v[e] = (v[e] - mean) * rstd * wv[e] + bv[e];
         pk.x = pack_bf16x2(v[0], v[1]);
         pk.y = pack_bf16x2(v[2], v[3]);
-        if (a.y != nullptr) *reinterpret_cast<uint2*>(a.y + row * a.ldy + lane * 4) = pk;
+        if (a.y != nullptr) {
+          __nv_bfloat16* yrow = a.y + row * a.ldy;
+          if constexpr (ROUTE) {
+            const int64_t i = row / a.route_n;
+            const int64_t j = row - i * a.route_n;
+            const int s = static_cast<int>(j / a.route_rows);
+            yrow = a.y_dst[s] + ((j - static_cast<int64_t>(s) * a.route_rows) * a.route_n +
+                                 static_cast<int64_t>(a.route_rank) * a.route_rows + i) * a.ldy;
+          }
+          *reinterpret_cast<uint2*>(yrow + lane * 4) = pk;
+        }
       }
       *reinterpret_cast<uint2*>(sA + half * 16384 + trow * 128 + ((chunk ^ (trow & 7)) << 4) +
                                 within) = pk;
@@ -495,6 +512,7 @@ __global__ void __launch_bounds__(256) ln_heads_tc_kernel(LnArgs a) {
     tc_fence_before();
     __syncthreads();  // TMEM and the A tile are reused by the next tile
   }
+  if constexpr (ROUTE) __threadfence_system();  // publish the routed rows before the exchange barrier
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 32);

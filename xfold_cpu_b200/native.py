@@ -564,6 +564,133 @@ def pair_logits_rows(pair: torch.Tensor, norm_weight: torch.Tensor | None,
     return logits
 
 
+# ----------------------------------------------------------------------------- routed stages
+# Row-block stages whose following exchange is done by the producing kernel:
+# every output row is stored straight into the receive buffer of the rank that
+# needs it (include/xfold_b200.h, "Routed stages").
+
+
+class Route:
+    """Destinations of a routed stage: dst[s] = device address of rank s's
+    receive buffer as mapped in this process (dst[rank] is this GPU's own)."""
+
+    def __init__(self, dst, rank: int) -> None:
+        import ctypes
+
+        if not 1 <= len(dst) <= 16 or not 0 <= rank < len(dst):
+            raise ValueError("a route has 1..16 ranks and this rank among them")
+        self.world = len(dst)
+        self.rank = rank
+        self._array = (ctypes.c_void_p * len(dst))(*dst)
+
+    @property
+    def ptr(self) -> int:
+        import ctypes
+
+        return ctypes.addressof(self._array)
+
+
+def triangle_projection_routed(pair: torch.Tensor, mask: torch.Tensor | None,
+                               left_weight: torch.Tensor, left_bias: torch.Tensor | None,
+                               left_eps: float, packed: torch.Tensor, a_route: Route,
+                               b_route: Route) -> torch.Tensor:
+    """triangle_projection whose a and b go straight to the channel owners
+    (rows -> channels); returns the local output gate g [rows, n, c]."""
+    device = _check_cuda(pair, mask, left_weight, packed)
+    rows, n, c = _rows_of(pair, "pair")
+    pair = _contig(pair)
+    if mask is not None:
+        mask = _contig(mask.expand(rows, n), torch.float32)
+    g = torch.empty((rows, n, c), dtype=torch.bfloat16, device=device)
+    lw, lb = _contig(left_weight, torch.float32), _contig(left_bias, torch.float32)
+    ws = _workspace(_capi.load().xfb_triangle_projection_workspace(rows, n, c), device)
+    _capi.call("xfb_triangle_projection_routed", _ptr(pair), _code(pair), rows, n, c, _ptr(mask),
+               _ptr(lw), _ptr(lb), float(left_eps), _ptr(packed), a_route.ptr, b_route.ptr,
+               a_route.world, a_route.rank, _ptr(g), _ptr(ws), ws.numel(), _stream(device))
+    return g
+
+
+def triangle_contraction_routed(a: torch.Tensor, b: torch.Tensor, outgoing: bool,
+                                z_route: Route) -> None:
+    """triangle_contraction whose rows go straight to their owners (channels ->
+    rows): z_route's buffers are [world * cs, n / world, n] bf16."""
+    device = _check_cuda(a, b)
+    a, b = _contig(a, torch.bfloat16), _contig(b, torch.bfloat16)
+    cs, n, _ = a.shape
+    if b.shape != a.shape:
+        raise ValueError("a and b must have the same [cs, n, n] shape")
+    _capi.call("xfb_triangle_contraction_routed", _ptr(a), _ptr(b), cs, n, int(bool(outgoing)),
+               z_route.ptr, z_route.world, z_route.rank, _stream(device))
+
+
+def grid_attention_prepare_routed(pair: torch.Tensor, norm_weight: torch.Tensor | None,
+                                  norm_bias: torch.Tensor | None, eps: float,
+                                  bias_weight: torch.Tensor, num_head: int,
+                                  x_route: Route) -> torch.Tensor:
+    """grid_attention_prepare for the ending node: the LayerNorm'd rows go
+    straight to the column owners (the transpose); returns the local bias rows."""
+    device = _check_cuda(pair, bias_weight)
+    rows, n, c = _rows_of(pair, "pair")
+    pair = _contig(pair)
+    bias = torch.empty((num_head, rows, n), dtype=torch.bfloat16, device=device)
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    bw = prepare_weight(bias_weight)
+    _capi.call("xfb_grid_attention_prepare_routed", _ptr(pair), _code(pair), rows, n, c, num_head,
+               _ptr(nw), _ptr(nb), float(eps), _ptr(bw), x_route.ptr, x_route.world,
+               x_route.rank, _ptr(bias), _stream(device))
+    return bias
+
+
+def grid_attention_rows_routed(x: torch.Tensor, mask: torch.Tensor | None, bias: torch.Tensor,
+                               packed: torch.Tensor, output_weight: torch.Tensor, num_head: int,
+                               out_route: Route) -> None:
+    """grid_attention_rows for the ending node: the bf16 update goes straight
+    back to the owners of the pair rows (the transpose back)."""
+    device = _check_cuda(x, mask, bias, packed, output_weight)
+    rows, n, c = _rows_of(x, "x")
+    x = _contig(x, torch.bfloat16)
+    if mask is not None:
+        mask = _contig(mask.expand(rows, n), torch.float32)
+    bias = _contig(bias, torch.bfloat16)
+    if bias.shape != (num_head, n, n):
+        raise ValueError("bias must be [heads, n, n]")
+    ow = prepare_weight(output_weight)
+    ws = _workspace(_capi.load().xfb_grid_attention_rows_workspace(rows, n, c, num_head), device)
+    _capi.call("xfb_grid_attention_rows_routed", _ptr(x), rows, n, c, num_head, _ptr(mask),
+               _ptr(bias), _ptr(packed), _ptr(ow), out_route.ptr, out_route.world,
+               out_route.rank, _ptr(ws), ws.numel(), _stream(device))
+
+
+def self_attention_rows(x: torch.Tensor, mask: torch.Tensor | None, logits_rows: torch.Tensor,
+                        row0: int, norm_weight: torch.Tensor | None,
+                        norm_bias: torch.Tensor | None, eps: float, packed: torch.Tensor,
+                        q_bias: torch.Tensor | None, wo: torch.Tensor, num_head: int,
+                        out: torch.Tensor, accumulate: bool = True) -> torch.Tensor:
+    """The single track's attention for query rows [row0, row0 + q_rows) of x
+    [n, c] (pairformer.py:102-108 for those rows) with their pair logits
+    [heads, q_rows, n]; the update of those rows is written (or added) into
+    `out` [n, c]."""
+    device = _check_cuda(x, mask, logits_rows, packed, wo, out)
+    n, c = x.shape
+    q_rows = logits_rows.shape[1]
+    if logits_rows.shape != (num_head, q_rows, n):
+        raise ValueError("logits_rows must be [heads, q_rows, n]")
+    x = _contig(x)
+    if mask is not None:
+        mask = _contig(mask.expand(n), torch.float32)
+    logits_rows = _contig(logits_rows, torch.bfloat16)
+    if not out.is_contiguous() or out.shape != (n, c):
+        raise ValueError("out must be a contiguous [n, c] tensor")
+    nw, nb = _contig(norm_weight, torch.float32), _contig(norm_bias, torch.float32)
+    qb, wo = _contig(q_bias, torch.float32), prepare_weight(wo)
+    ws = _workspace(_capi.load().xfb_self_attention_rows_workspace(n, c, num_head, q_rows), device)
+    _capi.call("xfb_self_attention_rows", _ptr(x), _code(x), n, c, num_head, row0, q_rows,
+               _ptr(mask), _ptr(logits_rows), _ptr(nw), _ptr(nb), float(eps), _ptr(packed),
+               _ptr(qb), _ptr(wo), None, _ptr(out), _code(out), 1 if accumulate else 0,
+               _ptr(ws), ws.numel(), _stream(device))
+    return out
+
+
 def conditioning(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, chunk: int,
                  sig_mode: int) -> torch.Tensor:
     """act(x @ weight^T + bias) as [n / chunk, m, chunk] bf16 (one contiguous

@@ -18,8 +18,19 @@ the arithmetic crosses rows:
   over those columns with the un-transposed mask rows of the same indices (as
   the reference, attention.py:99-100), and the transpose back of the update.
 * Transition: row-local.
-* Single track: the pair-logit rows are all-gathered; the single representation
-  (N x 384) is replicated and every process updates its own copy identically.
+* Single track: sharded by query rows.  A rank's pair-logit rows are the bias
+  rows of its own queries, so each rank attends for its rows against every key
+  (LayerNorm and projections of all N tokens are repeated on every rank, which
+  is cheap), runs the single transition on them, and the updated rows of the
+  single representation (N x 384 f32) are all-gathered.
+
+Routed stages: where the exchange class supports it (`routes`) and the stages
+do (`NativeStages`), the producer of each exchanged tensor stores it straight
+into the receive buffers of the ranks that need it -- the TriMul projection
+writes a and b by channel owner, the contraction writes z rows by row owner,
+the ending node's LayerNorm writes the transposed rows and its output
+projection the transposed update -- and a barrier follows, so no separate copy
+runs.
 
 Exchanges go through one of three classes with the same four patterns:
 `PeerExchange` (one shard per GPU: the library's copy kernel stores each chunk
@@ -123,11 +134,22 @@ class ProcessGroupExchange(CollectiveExchange):
 
 
 class LocalExchange(CollectiveExchange):
-    """All G shards in this process (tensor copies stand in for the transfers)."""
+    """All G shards in this process (tensor copies stand in for the transfers).
+    With routed=True (CUDA tensors) the routed stages store into G receive
+    buffers on this device, as they would into G GPUs' buffers."""
 
-    def __init__(self, world: int) -> None:
+    def __init__(self, world: int, routed: bool = False) -> None:
         self.world = world
         self.ranks = list(range(world))
+        self.routes = routed
+
+    def route(self, kind, shape, dtype, device):
+        bufs = [torch.empty(shape, dtype=dtype, device=device) for _ in range(self.world)]
+        ptrs = [b.data_ptr() for b in bufs]
+        return [(bufs[r], native.Route(ptrs, r)) for r in range(self.world)]
+
+    def complete(self, device):
+        pass  # one stream: the stores are in order
 
     def all_to_all(self, bufs):
         g = self.world
@@ -155,11 +177,15 @@ class PeerExchange:
     The returned tensors are views of those buffers: valid until the same
     pattern with the same shape has run twice more."""
 
-    def __init__(self, group=None, barrier: str | None = None) -> None:
+    def __init__(self, group=None, barrier: str | None = None, routed: bool | None = None) -> None:
         import os
 
         import torch.distributed as dist
 
+        # routed stages (producers store straight into the peers' buffers) unless
+        # routed=False or XFB_EXCHANGE_ROUTED=0
+        self.routes = (os.environ.get("XFB_EXCHANGE_ROUTED", "1") != "0"
+                       if routed is None else bool(routed))
         self._dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
@@ -192,6 +218,18 @@ class PeerExchange:
         entry["next"] ^= 1
         return local, peers
 
+    # -- routed stages: the producing kernels store into the receive buffers
+    def route(self, kind, shape, dtype, device):
+        """[(this rank's next receive buffer of `kind`, the route to every rank's
+        copy of it)] for a routed stage; complete() (or the next exchange's
+        barrier) publishes what the stage stored."""
+        local, peers = self._recv(kind, shape, dtype, device)
+        return [(local, native.Route(peers, self.rank))]
+
+    def complete(self, device):
+        """The exchange barrier after routed stores."""
+        self._sync(device)
+
     def _copy_and_sync(self, boxes, device):
         import ctypes
 
@@ -200,6 +238,14 @@ class PeerExchange:
         stream = torch.cuda.current_stream(device).cuda_stream
         arr = (_capi.CopyBox * len(boxes))(*boxes)
         _capi.call("xfb_exchange_copy", ctypes_addressof(arr), len(boxes), stream)
+        self._sync(device)
+
+    def _sync(self, device):
+        import ctypes
+
+        from . import _capi
+
+        stream = torch.cuda.current_stream(device).cuda_stream
         if self.barrier == "nccl":
             if self._flag is None:
                 self._flag = torch.zeros(1, dtype=torch.int32, device=device)
@@ -372,9 +418,47 @@ class NativeStages:
         return native.pair_logits_rows(pair_rows, norm.weight, norm.bias, norm.eps,
                                        _bf16(block._logits_w, block.single_pair_logits_projection.weight))
 
-    def single_track(self, block: PairformerBlock, single, seq_mask, logits):
-        block.single_attention_.accumulate_(single, seq_mask, logits)
-        block.single_transition.accumulate_(single)
+    def single_attention_rows(self, block: PairformerBlock, x, seq_mask, logits_rows, row0, out):
+        att = block.single_attention_
+        packed = att._packed.get(
+            (att.q_projection.weight, att.k_projection.weight, att.v_projection.weight,
+             att.gating_query.weight), native.pack_attention_weights)
+        ln = att.adaptive_layernorm.layer_norm
+        native.self_attention_rows(x, seq_mask, logits_rows, row0, ln.weight, ln.bias, ln.eps,
+                                   packed, att.q_projection.bias,
+                                   _bf16(att._wo, att.adaptive_zero_init.transition2.weight),
+                                   att.num_head, out, accumulate=True)
+
+    def single_transition_rows(self, block: PairformerBlock, single_rows):
+        block.single_transition.accumulate_(single_rows)
+
+    # -- routed forms (the exchange after the stage done by its kernel)
+    routed = True
+
+    def trimul_project_routed(self, mod: TriangleMultiplication, pair_rows, mask_rows, a_route,
+                              b_route):
+        packed = mod._packed.get(
+            (mod.projection.weight, mod.gate.weight, mod.gating_linear.weight),
+            native.pack_triangle_weights)
+        return native.triangle_projection_routed(pair_rows, mask_rows, mod.left_norm_input.weight,
+                                                 mod.left_norm_input.bias,
+                                                 mod.left_norm_input.eps, packed, a_route, b_route)
+
+    def trimul_contract_routed(self, mod: TriangleMultiplication, a, b, z_route):
+        native.triangle_contraction_routed(a, b, mod.outgoing, z_route)
+
+    def attention_prepare_routed(self, mod: GridSelfAttention, pair_rows, x_route):
+        return native.grid_attention_prepare_routed(
+            pair_rows, mod.act_norm.weight, mod.act_norm.bias, mod.act_norm.eps,
+            _bf16(mod._bias_w, mod.pair_bias_projection.weight), mod.num_head, x_route)
+
+    def attention_rows_routed(self, mod: GridSelfAttention, x_rows, mask_rows, bias, out_route):
+        packed = mod._packed.get(
+            (mod.q_projection.weight, mod.k_projection.weight, mod.v_projection.weight,
+             mod.gating_query.weight), native.pack_attention_weights)
+        native.grid_attention_rows_routed(x_rows, mask_rows, bias, packed,
+                                          _bf16(mod._out_w, mod.output_projection.weight),
+                                          mod.num_head, out_route)
 
 
 # ----------------------------------------------------------------------------- the block
@@ -393,9 +477,29 @@ def check_sharding(n: int, c: int, world: int) -> None:
         raise ValueError("a row-sharded pair needs N % 8 == 0")
 
 
+def _routed(exchange, stages) -> bool:
+    return bool(getattr(exchange, "routes", False) and getattr(stages, "routed", False))
+
+
 def _triangle(mod, pairs, pair_mask, exchange, stages):
     g = exchange.world
     rows, n, c = pairs[0].shape
+    if _routed(exchange, stages):
+        dev = pairs[0].device
+        # projection -> (rows -> channels) -> contraction -> (channels -> rows),
+        # each exchange stored by its producer, then one barrier
+        ra = exchange.route("r2c", (c // g, n, n), torch.bfloat16, dev)
+        rb = exchange.route("r2c_b", (c // g, n, n), torch.bfloat16, dev)
+        gates = [stages.trimul_project_routed(mod, pair, pair_mask[shard_rows(n, g, r)], ta, tb)
+                 for pair, r, (_, ta), (_, tb) in zip(pairs, exchange.ranks, ra, rb)]
+        exchange.complete(dev)
+        rz = exchange.route("c2r", (c, rows, n), torch.bfloat16, dev)
+        for (a, _), (b, _), (_, tz) in zip(ra, rb, rz):
+            stages.trimul_contract_routed(mod, a, b, tz)
+        exchange.complete(dev)
+        for pair, (z, _), gate in zip(pairs, rz, gates):
+            stages.trimul_output(mod, z, gate, pair)
+        return
     projected = [stages.trimul_project(mod, pair, pair_mask[shard_rows(n, g, r)])
                  for pair, r in zip(pairs, exchange.ranks)]
     a_full, b_full = exchange.rows_to_channels_pair([a for a, _, _ in projected],
@@ -409,14 +513,31 @@ def _triangle(mod, pairs, pair_mask, exchange, stages):
 
 def _attention(mod, pairs, pair_mask, exchange, stages):
     g = exchange.world
-    rows, n, _ = pairs[0].shape
-    prepared = [stages.attention_prepare(mod, pair) for pair in pairs]
-    biases = exchange.gather_rows([bias for _, bias in prepared])
+    rows, n, c = pairs[0].shape
     if not mod.transpose:
+        prepared = [stages.attention_prepare(mod, pair) for pair in pairs]
+        biases = exchange.gather_rows([bias for _, bias in prepared])
         for pair, (x, _), bias, r in zip(pairs, prepared, biases, exchange.ranks):
             stages.attention_rows(mod, x, pair_mask[shard_rows(n, g, r)], bias, out=pair)
         return
     # ending node: attention runs over pair columns; mask rows indexed by the column
+    if _routed(exchange, stages):
+        dev = pairs[0].device
+        # the LayerNorm'd rows go to the column owners from the prepare kernel;
+        # the bias gather's barrier publishes them too
+        rx = exchange.route("transpose", (rows, n, c), torch.bfloat16, dev)
+        bias_rows = [stages.attention_prepare_routed(mod, pair, tx)
+                     for pair, (_, tx) in zip(pairs, rx)]
+        biases = exchange.gather_rows(bias_rows)
+        ru = exchange.route("transpose", (rows, n, c), torch.bfloat16, dev)
+        for (xt, _), bias, r, (_, tu) in zip(rx, biases, exchange.ranks, ru):
+            stages.attention_rows_routed(mod, xt, pair_mask[shard_rows(n, g, r)], bias, tu)
+        exchange.complete(dev)
+        for pair, (upd, _) in zip(pairs, ru):
+            pair += upd
+        return
+    prepared = [stages.attention_prepare(mod, pair) for pair in pairs]
+    biases = exchange.gather_rows([bias for _, bias in prepared])
     cols = exchange.transpose([x for x, _ in prepared])
     del prepared
     updates = [stages.attention_rows(mod, xt, pair_mask[shard_rows(n, g, r)], bias)
@@ -447,6 +568,15 @@ def pairformer_block(block: PairformerBlock, pairs: list[torch.Tensor], pair_mas
         stages.transition(block, pair)
     if not block.with_single:
         return pairs
-    logits = exchange.gather_rows([stages.pair_logits_rows(block, pair) for pair in pairs])
-    stages.single_track(block, single, seq_mask, logits[0])
+    # single track sharded by query rows: each rank's pair-logit rows are the
+    # bias rows of its own queries, so only the updated single rows are gathered
+    logits = [stages.pair_logits_rows(block, pair) for pair in pairs]
+    x_in = single.clone() if len(pairs) > 1 else single  # every shard reads the old single
+    for lg, r in zip(logits, exchange.ranks):
+        stages.single_attention_rows(block, x_in, seq_mask, lg, r * rows, single)
+    for r in exchange.ranks:
+        stages.single_transition_rows(block, single[r * rows:(r + 1) * rows])
+    gathered = exchange.gather_rows([single[r * rows:(r + 1) * rows].unsqueeze(0)
+                                     for r in exchange.ranks])
+    single.copy_(gathered[0][0])
     return pairs, single
