@@ -596,6 +596,75 @@ XFB_API int xfb_af3_dot_product_attention(const void* q, const void* k, const vo
                                           void* workspace, int64_t workspace_bytes,
                                           void* stream);
 
+/* ------------------------------------------------------------------ float32 path
+ * The reference's float32 route (no autocast: xfold/fastnn/native.py:31-43 keeps
+ * fp32; torch matmul, LayerNorm and softmax in fp32) on the CUDA cores, for the
+ * 1e-4 precision contract.  All tensors are float32; every operand is given by
+ * strides in elements, so transposes, head splits and the triangle
+ * multiplication's channel interleave need no copies. */
+
+/* C[b](i, j) (=, or += with accumulate) ((act(sum_k A[b](i,k) B[b](j,k) + bias[j]))
+ * * row_scale[b](i)) * mul[b](i, j); act 0 = none, 1 = sigmoid; null pointers
+ * skip their step.  Replaces the fp32 matmuls / einsums of
+ * triangle_multiplication.py:71-105, attention.py:61-105, primitives.py:33-37,
+ * diffusion_transformer.py:51-217. */
+typedef struct xfb_f32_gemm_args {
+  const float* a;
+  int64_t a_sb, a_si, a_sk;
+  const float* b;
+  int64_t b_sb, b_sj, b_sk;
+  float* c;
+  int64_t c_sb, c_si, c_sj;
+  int64_t m, n, k, batch;
+  const float* bias;
+  int act;
+  const float* row_scale;
+  int64_t rs_sb, rs_si;
+  const float* mul;
+  int64_t mul_sb, mul_si, mul_sj;
+  int accumulate;
+} xfb_f32_gemm_args;
+XFB_API int xfb_f32_gemm(const xfb_f32_gemm_args* args, void* stream);
+
+/* LayerNorm over rows of cols <= 1024 fp32 values (fastnn/layer_norm.py:14-80,
+ * F.layer_norm): weight / bias optional. */
+XFB_API int xfb_f32_layer_norm(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                               const float* weight, const float* bias, double eps, float* y,
+                               int64_t ldy, void* stream);
+
+/* out[b][h][i][:] = gate * softmax_k(q[b][h][i] . k[b][h][k] * scale + bias[b][h][i][k],
+ * mask[b][k]) v[b][h][k][:] in fp32 (fastnn/attention.py:45-66): masked keys
+ * (mask value 0) get -1e9 after the bias; rows of each tensor contiguous in the
+ * head dimension (d, dv <= 64); strides of 0 broadcast. */
+typedef struct xfb_f32_attention_args {
+  const float* q;
+  int64_t q_sb, q_sh, q_si;
+  const float* k;
+  int64_t k_sb, k_sh, k_si;
+  const float* v;
+  int64_t v_sb, v_sh, v_si;
+  const float* bias;
+  int64_t bias_sb, bias_sh, bias_si;
+  const float* mask;
+  int64_t mask_sb;
+  float* out;
+  int64_t out_sb, out_sh, out_si;
+  const float* gate;
+  int64_t gate_sb, gate_sh, gate_si;
+  int64_t batch, heads, nq, nk, d, dv;
+  double scale;
+} xfb_f32_attention_args;
+XFB_API int xfb_f32_attention(const xfb_f32_attention_args* args, void* stream);
+
+/* y[r][c] = silu(h[r][c]) * h[r][f + c] for h [rows][2f] (gated_linear_unit_torch,
+ * fastnn/gated_linear_unit.py:103-107). */
+XFB_API int xfb_f32_silu_mul(const float* h, int64_t rows, int64_t f, float* y, void* stream);
+
+/* y[t] = y[t] * scale[t] + shift[t] over n values (AdaptiveLayerNorm modulation,
+ * diffusion_transformer.py:57-62). */
+XFB_API int xfb_f32_scale_shift(float* y, const float* scale, const float* shift, int64_t n,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

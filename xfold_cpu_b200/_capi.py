@@ -139,7 +139,35 @@ SIGNATURES: dict[str, tuple] = {
         [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _i, _p, _i, _i, _i64, _i, _p, _p,
          _i64, _p],
     ),
+    "xfb_f32_gemm": (_i, [_p, _p]),
+    "xfb_f32_layer_norm": (_i, [_p, _i64, _i64, _i64, _p, _p, _d, _p, _i64, _p]),
+    "xfb_f32_attention": (_i, [_p, _p]),
+    "xfb_f32_silu_mul": (_i, [_p, _i64, _i64, _p, _p]),
+    "xfb_f32_scale_shift": (_i, [_p, _p, _p, _i64, _p]),
 }
+
+
+def _fields(spec: str) -> list:
+    """ctypes fields from 'name:type ...' (p = pointer, l = int64, i = int, d = double)."""
+    kinds = {"p": ctypes.c_void_p, "l": ctypes.c_int64, "i": ctypes.c_int, "d": ctypes.c_double}
+    return [(name, kinds[t]) for name, t in (f.split(":") for f in spec.split())]
+
+
+class F32GemmArgs(ctypes.Structure):
+    """xfb_f32_gemm_args (include/xfold_b200.h)."""
+
+    _fields_ = _fields("a:p a_sb:l a_si:l a_sk:l b:p b_sb:l b_sj:l b_sk:l c:p c_sb:l c_si:l "
+                       "c_sj:l m:l n:l k:l batch:l bias:p act:i row_scale:p rs_sb:l rs_si:l "
+                       "mul:p mul_sb:l mul_si:l mul_sj:l accumulate:i")
+
+
+class F32AttentionArgs(ctypes.Structure):
+    """xfb_f32_attention_args (include/xfold_b200.h)."""
+
+    _fields_ = _fields("q:p q_sb:l q_sh:l q_si:l k:p k_sb:l k_sh:l k_si:l v:p v_sb:l v_sh:l "
+                       "v_si:l bias:p bias_sb:l bias_sh:l bias_si:l mask:p mask_sb:l out:p "
+                       "out_sb:l out_sh:l out_si:l gate:p gate_sb:l gate_sh:l gate_si:l batch:l "
+                       "heads:l nq:l nk:l d:l dv:l scale:d")
 
 
 class CopyBox(ctypes.Structure):

@@ -24,6 +24,7 @@
 #include "layer_norm.cuh"
 #include "window_attention.cuh"
 #include "msa.cuh"
+#include "fp32.cuh"
 
 #ifndef XFB_NVCC_FLAGS
 #define XFB_NVCC_FLAGS "unknown"
@@ -1865,15 +1866,8 @@ XFB_API int xfb_triangle_contraction_routed(const void* a, const void* b, int64_
   XFB_REQUIRE(n % world == 0, "a routed contraction splits n rows evenly over the ranks");
   XFB_REQUIRE(aligned16(a) && aligned16(b), "a and b must be 16-byte aligned");
   if (cs == 0 || n == 0) return XFB_OK;
-  xfb::EpiDirect<256> epi;
-  epi.out = z_dst[rank];
+  xfb::EpiRowsRouted<128> epi;
   epi.ld_out = n;
-  epi.bstride_out = n * n;
-  epi.out_f32 = 0;
-  epi.accumulate = 0;
-  epi.bias = nullptr;
-  epi.gate = nullptr;
-  epi.ld_gate = 0;
   epi.M = static_cast<int>(n);
   epi.N = static_cast<int>(n);
   epi.route = 1;
@@ -1885,8 +1879,8 @@ XFB_API int xfb_triangle_contraction_routed(const void* a, const void* b, int64_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t bs = n * n;
   // outgoing z[c,i,j] = sum_k a[c,i,k] b[c,j,k]; incoming sum_k a[c,k,j] b[c,k,i]
-  if (outgoing) return run_gemm<256, false, false>(a, n, bs, b, n, bs, n, n, n, cs, epi, st);
-  return run_gemm<256, true, true>(b, n, bs, a, n, bs, n, n, n, cs, epi, st);
+  if (outgoing) return run_gemm<128, false, false>(a, n, bs, b, n, bs, n, n, n, cs, epi, st);
+  return run_gemm<128, true, true>(b, n, bs, a, n, bs, n, n, n, cs, epi, st);
 }
 
 XFB_API int64_t xfb_triangle_output_workspace(int64_t rows, int64_t n, int64_t c) {
@@ -2069,15 +2063,8 @@ int grid_attention_rows_impl(const void* x, int64_t rows, int64_t n, int64_t c, 
   XFB_TRY(run_flash(dp, XFB_BF16, pre, w.q, w.k, w.v, a, st));
   if (out_route != nullptr) {
     // the update of column block jj, pair row i, goes back to the owner of row i
-    xfb::EpiDirect<128> epi;
-    epi.out = out;
+    xfb::EpiRowsRouted<128> epi;
     epi.ld_out = c;
-    epi.bstride_out = 0;
-    epi.out_f32 = 0;
-    epi.accumulate = 0;
-    epi.bias = nullptr;
-    epi.gate = nullptr;
-    epi.ld_gate = 0;
     epi.M = static_cast<int>(rows * n);
     epi.N = static_cast<int>(c);
     epi.route = 2;
@@ -2838,6 +2825,149 @@ XFB_API int xfb_af3_dot_product_attention(const void* q, const void* k, const vo
   return xfb_dot_product_attention(q, k, v, B, H, nq, nk, d, mask, mask_dtype, mask_batched,
                                    bias, bias_dtype, bias_batched, q_pre_scaled, out, workspace,
                                    workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- float32 path
+
+extern "C" {
+
+XFB_API int xfb_f32_gemm(const xfb_f32_gemm_args* g, void* stream) {
+  XFB_REQUIRE(g != nullptr, "gemm arguments missing");
+  XFB_REQUIRE(g->m >= 0 && g->n >= 0 && g->k >= 0 && g->batch >= 0, "negative gemm extent");
+  XFB_REQUIRE(g->act == 0 || g->act == 1, "act must be 0 (none) or 1 (sigmoid)");
+  if (g->m == 0 || g->n == 0 || g->batch == 0) return XFB_OK;
+  XFB_REQUIRE(g->a && g->b && g->c, "gemm operands missing");
+  XFB_REQUIRE(g->m < (1ll << 31) && g->n < (1ll << 31) && g->k < (1ll << 31) &&
+                  (g->m + 63) / 64 <= 65535 && g->batch <= 65535,
+              "fp32 gemm too large");
+  xfb::F32Gemm k;
+  k.A = g->a;
+  k.a_sb = g->a_sb;
+  k.a_si = g->a_si;
+  k.a_sk = g->a_sk;
+  k.B = g->b;
+  k.b_sb = g->b_sb;
+  k.b_sj = g->b_sj;
+  k.b_sk = g->b_sk;
+  k.C = g->c;
+  k.c_sb = g->c_sb;
+  k.c_si = g->c_si;
+  k.c_sj = g->c_sj;
+  k.M = static_cast<int>(g->m);
+  k.N = static_cast<int>(g->n);
+  k.K = static_cast<int>(g->k);
+  k.batch = static_cast<int>(g->batch);
+  k.bias = g->bias;
+  k.act = g->act;
+  k.row_scale = g->row_scale;
+  k.rs_sb = g->rs_sb;
+  k.rs_si = g->rs_si;
+  k.mul = g->mul;
+  k.m_sb = g->mul_sb;
+  k.m_si = g->mul_si;
+  k.m_sj = g->mul_sj;
+  k.accumulate = g->accumulate;
+  const dim3 grid(static_cast<unsigned>((g->n + 63) / 64), static_cast<unsigned>((g->m + 63) / 64),
+                  static_cast<unsigned>(g->batch));
+  xfb::f32_gemm_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(k);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+XFB_API int xfb_f32_layer_norm(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                               const float* weight, const float* bias, double eps, float* y,
+                               int64_t ldy, void* stream) {
+  XFB_REQUIRE(rows >= 0 && cols > 0 && cols <= 1024, "fp32 LayerNorm takes 1..1024 columns");
+  XFB_REQUIRE(std::isfinite(eps) && eps >= 0, "LayerNorm eps must be finite and non-negative");
+  if (rows == 0) return XFB_OK;
+  XFB_REQUIRE(x != nullptr && y != nullptr, "LayerNorm tensors missing");
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int blocks = static_cast<int>(std::min<int64_t>((rows + 7) / 8, int64_t(sms) * 8));
+  xfb::f32_layer_norm_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, rows, static_cast<int>(cols), ldx, weight, bias, static_cast<float>(eps), y, ldy);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+XFB_API int xfb_f32_attention(const xfb_f32_attention_args* a, void* stream) {
+  XFB_REQUIRE(a != nullptr, "attention arguments missing");
+  XFB_REQUIRE(a->batch >= 0 && a->heads >= 0 && a->nq >= 0 && a->nk >= 0, "negative extent");
+  XFB_REQUIRE(a->d > 0 && a->d <= 64 && a->dv > 0 && a->dv <= 64, "head dims must be 1..64");
+  if (a->batch == 0 || a->heads == 0 || a->nq == 0) return XFB_OK;
+  XFB_REQUIRE(a->q && a->k && a->v && a->out, "attention tensors missing");
+  XFB_REQUIRE(a->nk > 0, "attention over no keys");
+  XFB_REQUIRE(a->batch * a->heads <= 65535 && a->nq < (1ll << 31) && a->nk < (1ll << 31),
+              "fp32 attention too large");
+  xfb::F32Attn k;
+  k.q = a->q;
+  k.q_sb = a->q_sb;
+  k.q_sh = a->q_sh;
+  k.q_si = a->q_si;
+  k.k = a->k;
+  k.k_sb = a->k_sb;
+  k.k_sh = a->k_sh;
+  k.k_si = a->k_si;
+  k.v = a->v;
+  k.v_sb = a->v_sb;
+  k.v_sh = a->v_sh;
+  k.v_si = a->v_si;
+  k.bias = a->bias;
+  k.bias_sb = a->bias_sb;
+  k.bias_sh = a->bias_sh;
+  k.bias_si = a->bias_si;
+  k.mask = a->mask;
+  k.mask_sb = a->mask_sb;
+  k.out = a->out;
+  k.o_sb = a->out_sb;
+  k.o_sh = a->out_sh;
+  k.o_si = a->out_si;
+  k.gate = a->gate;
+  k.g_sb = a->gate_sb;
+  k.g_sh = a->gate_sh;
+  k.g_si = a->gate_si;
+  k.B = static_cast<int>(a->batch);
+  k.H = static_cast<int>(a->heads);
+  k.Q = static_cast<int>(a->nq);
+  k.K = static_cast<int>(a->nk);
+  k.d = static_cast<int>(a->d);
+  k.dv = static_cast<int>(a->dv);
+  k.scale = static_cast<float>(a->scale);
+  const dim3 grid(static_cast<unsigned>((a->nq + xfb::kF32AttnWarps - 1) / xfb::kF32AttnWarps),
+                  static_cast<unsigned>(a->batch * a->heads));
+  xfb::f32_attention_kernel<<<grid, 32 * xfb::kF32AttnWarps, 0,
+                              static_cast<cudaStream_t>(stream)>>>(k);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+XFB_API int xfb_f32_silu_mul(const float* h, int64_t rows, int64_t f, float* y, void* stream) {
+  XFB_REQUIRE(rows >= 0 && f > 0 && f < (1ll << 30), "silu_mul extents out of range");
+  if (rows == 0) return XFB_OK;
+  XFB_REQUIRE(h != nullptr && y != nullptr, "silu_mul tensors missing");
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int blocks = static_cast<int>(std::min<int64_t>((rows * f + 255) / 256, int64_t(sms) * 16));
+  xfb::f32_silu_mul_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      h, rows, static_cast<int>(f), y);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+XFB_API int xfb_f32_scale_shift(float* y, const float* scale, const float* shift, int64_t n,
+                                void* stream) {
+  XFB_REQUIRE(n >= 0, "negative length");
+  if (n == 0) return XFB_OK;
+  XFB_REQUIRE(y && scale && shift, "scale_shift tensors missing");
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, int64_t(sms) * 16));
+  xfb::f32_scale_shift_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, scale,
+                                                                                     shift, n);
+  XFB_LAUNCHED();
+  return XFB_OK;
 }
 
 }  // extern "C"

@@ -61,16 +61,19 @@ struct EpiRoutedOf<E, std::void_t<decltype(E::route)>> {
   static constexpr bool value = true;
 };
 
-// Epilogues with kLaneStores = true have all 32 lanes of the store warp call
-// Epi::store_lanes(ctx, lane) after Epi::store (lane 0): plain 16-byte stores
-// from the staged tile, for destinations no tensor map describes.
+// Epilogues with kGroupCopy = true get Epi::group_copy(ctx, t) called by every
+// thread t (0..255) of the epilogue group after the tile is staged, between two
+// group barriers: plain 16-byte stores of the staged tile by all 256 threads,
+// for destinations no tensor map describes (another GPU's receive buffer).
+// Both barriers are reached by every thread whatever its waits returned, so an
+// aborting CTA cannot strand a barrier.
 template <class E, class = void>
-struct EpiLaneStoresOf {
+struct EpiGroupCopyOf {
   static constexpr bool value = false;
 };
 template <class E>
-struct EpiLaneStoresOf<E, std::void_t<decltype(E::kLaneStores)>> {
-  static constexpr bool value = E::kLaneStores;
+struct EpiGroupCopyOf<E, std::void_t<decltype(E::kGroupCopy)>> {
+  static constexpr bool value = E::kGroupCopy;
 };
 
 // Destinations of a routed store: one receive buffer per rank of the exchange
@@ -283,38 +286,7 @@ __global__ void __launch_bounds__(GemmWarps<Epi>::kThreads, 1)
     // Takes each staged tile once every epilogue thread has written it, issues
     // the epilogue's TMA store, and frees the staging buffer as soon as that
     // store has read it.  The epilogue warps never wait for one another.
-    if constexpr (Epi::kStagingBytes > 0 && EpiLaneStoresOf<Epi>::value) {
-      // every lane takes part: lane 0 issues the TMA stores, then all lanes
-      // copy what the epilogue routes elsewhere out of the staged tile
-      constexpr int NB = Epi::kStagingBufs;
-      int iter = 0;
-      EpiCtx ctx;
-      ctx.row = 0;
-      ctx.half = 0;
-      ctx.tmem = 0;
-      ctx.aux = nullptr;
-      for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
-        const int b = iter % NB;
-        const uint32_t ph = (iter / NB) & 1;
-        const bool ok = mbar_wait(&staging_full[b], ph, kErrWaitEpilogue, abort_flag);
-        const int bat = tile / tiles_per_batch;
-        const int rem = tile - bat * tiles_per_batch;
-        ctx.bat = bat;
-        ctx.m0 = (rem / shape.n_tiles) * kGemmBM;
-        ctx.n0 = (rem % shape.n_tiles) * BN;
-        ctx.staging = smem + L::kStagingOff + b * L::kStagingStride;
-        const bool go = ok && !*abort_flag;
-        if (lane == 0) {
-          if (go) epi.store(ctx);
-          bulk_commit();
-        }
-        if (go) epi.store_lanes(ctx, lane);
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();  // every lane's shared-memory reads of this buffer are done
-        if (lane == 0) mbar_arrive(&staging_free[b]);
-      }
-      if (lane == 0) bulk_wait<0>();
-    } else if constexpr (Epi::kStagingBytes > 0) {
+    if constexpr (Epi::kStagingBytes > 0) {
       if (lane == 0) {
         constexpr int NB = Epi::kStagingBufs;
         int iter = 0;
@@ -383,6 +355,12 @@ __global__ void __launch_bounds__(GemmWarps<Epi>::kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if constexpr (kAux) mbar_arrive(&aux_empty[acc]);
+      if constexpr (EpiGroupCopyOf<Epi>::value) {
+        // the accumulator is free again; now the group stores the staged tile
+        named_barrier(1 + group, kGemmEpiThreads);  // the whole tile is staged
+        if (ok && !*abort_flag) epi.group_copy(ctx, threadIdx.x & (kGemmEpiThreads - 1));
+        named_barrier(1 + group, kGemmEpiThreads);  // and read before it is reused
+      }
       if constexpr (Epi::kStagingBytes > 0) mbar_arrive(&staging_full[iter % NB]);
       if constexpr (G == 2) {
         acc_phase ^= 1;
@@ -699,6 +677,80 @@ struct EpiDirect {
   }
 };
 
+// bf16 output rows routed to the ranks that own them (the channels -> rows and
+// transpose exchanges of a row-sharded pair, done by the producer), through a
+// staged tile: the epilogue threads write their row's BN values into a
+// swizzled [128][BN] bf16 staging tile, then copy it out together 16 bytes per
+// thread, consecutive threads on consecutive bytes of a row, so every store
+// instruction writes whole rows (BN * 2 contiguous bytes) over NVLink.
+// Destinations as EpiDirect's route 1 / route 2; N % 8 == 0.
+template <int BN>
+struct EpiRowsRouted {
+  static constexpr int kStagingBytes = 128 * BN * 2;
+  static constexpr int kStagingBufs = 2;
+  static constexpr int kAuxBytes = 0;
+  static constexpr bool kGroupCopy = true;
+  static constexpr int kChunks = BN / 8;  // 16-byte chunks per staged row
+  int64_t ld_out;
+  int M, N;
+  int route;  // 1: channels -> rows, 2: transpose
+  int rank, route_rows, route_batch, route_n;
+  void* dst[kMaxRoute];
+
+  __device__ void load_aux(void*, uint64_t*, int, int, int) const {}
+  __device__ void store(const EpiCtx&) const {}
+
+  __device__ __forceinline__ uint4* chunk(uint8_t* base, int row, int q) const {
+    return reinterpret_cast<uint4*>(base + row * (BN * 2) + ((q ^ (row % kChunks)) << 4));
+  }
+
+  __device__ void compute(const EpiCtx& c) const {
+    constexpr int kHalf = BN / 2;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kHalf; c0 += 16) {
+      float v[16];
+      tmem_ld16(c.tmem + c.half * kHalf + c0, v);
+      const int q = (c.half * kHalf + c0) / 8;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint4 w;
+        w.x = pack_bf16x2(v[8 * h + 0], v[8 * h + 1]);
+        w.y = pack_bf16x2(v[8 * h + 2], v[8 * h + 3]);
+        w.z = pack_bf16x2(v[8 * h + 4], v[8 * h + 5]);
+        w.w = pack_bf16x2(v[8 * h + 6], v[8 * h + 7]);
+        *chunk(c.staging, c.row, q + h) = w;
+      }
+    }
+  }
+
+  __device__ void group_copy(const EpiCtx& c, int t) const {
+    constexpr int kRowsPerStep = kGemmEpiThreads / kChunks;
+    const int q = t % kChunks;
+    const int col = c.n0 + q * 8;
+    if (col >= N) return;
+#pragma unroll 4
+    for (int r = t / kChunks; r < 128; r += kRowsPerStep) {
+      const int row = c.m0 + r;
+      if (row >= M) break;
+      int64_t off;
+      int s;
+      if (route == 1) {
+        s = row / route_rows;
+        off = (static_cast<int64_t>(rank * route_batch + c.bat) * route_rows +
+               (row - s * route_rows)) * ld_out;
+      } else {
+        const int jj = row / route_n;
+        const int i = row - jj * route_n;
+        s = i / route_rows;
+        off = (static_cast<int64_t>(i - s * route_rows) * route_n + rank * route_rows + jj) *
+              ld_out;
+      }
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst[s]) + off + col) =
+          *chunk(c.staging, r, q);
+    }
+  }
+};
+
 // Gated linear unit.  The packed weight places, in every 128-wide tile, 64 gate
 // units followed by the 64 value units of the same output columns.
 //   h[row][n0/2 + j] = bf16( silu(gate_j) * value_j )
@@ -744,7 +796,7 @@ struct EpiTriProj {
   static constexpr int kStagingBufs = 2;
   static constexpr int kGroups = 2;
   static constexpr int kAuxBytes = 0;
-  static constexpr bool kLaneStores = true;
+  static constexpr bool kGroupCopy = true;
   CUtensorMap a_map, b_map, g_map;
   const float* mask;  // [n][n] or null
   int n, n_proj_tiles, c;
@@ -793,7 +845,7 @@ struct EpiTriProj {
   __device__ void store(const EpiCtx& c) const {
     const int tile = c.n0 / 128;
     if (tile < n_proj_tiles) {
-      if (route) return;  // store_lanes
+      if (route) return;  // group_copy wrote them
       tma_store_3d(&a_map, c.staging, c.m0, c.bat, tile * 32);
       tma_store_3d(&b_map, c.staging + 8192, c.m0, c.bat, tile * 32);
     } else {
@@ -804,13 +856,13 @@ struct EpiTriProj {
 
   // a / b tile [32 channels][128 j] bf16 each: 16-byte pieces, channel by
   // channel, into the owners' receive buffers (n % 8 == 0, so a piece never
-  // straddles the end of a row)
-  __device__ void store_lanes(const EpiCtx& c, int lane) const {
+  // straddles the end of a row); 16 threads write one channel's 256 bytes
+  __device__ void group_copy(const EpiCtx& c, int t) const {
     const int tile = c.n0 / 128;
     if (!route || tile >= n_proj_tiles) return;
     const int64_t i = static_cast<int64_t>(rank) * route_rows + c.bat;
-#pragma unroll 4
-    for (int idx = lane; idx < 2 * 32 * 16; idx += 32) {
+#pragma unroll
+    for (int idx = t; idx < 2 * 32 * 16; idx += kGemmEpiThreads) {
       const int which = idx >> 9;  // 0: a, 1: b
       const int ch = (idx >> 4) & 31;
       const int piece = idx & 15;

@@ -29,7 +29,7 @@ from typing import Optional
 import torch
 import torch.nn as nn
 
-from .. import native
+from .. import fp32, native
 from . import atom_layout
 from ..fastnn import LayerNorm, WeightCache
 from ..fastnn import config
@@ -37,6 +37,17 @@ from ..fastnn import config
 
 def _bf16(cache: WeightCache, weight: torch.Tensor) -> torch.Tensor:
     return cache.get((weight,), native.prepare_weight)
+
+
+def _f32_result(update: torch.Tensor, out, accumulate):
+    """Hands an fp32-path update back the way the bf16 entry points do."""
+    if out is None:
+        return update
+    if accumulate:
+        out += update
+    else:
+        out.copy_(update)
+    return out
 
 
 def _fused_target(x: torch.Tensor) -> bool:
@@ -64,6 +75,8 @@ class TriangleMultiplication(nn.Module):
 
     def _run(self, pair, mask, out, accumulate):
         config.require_cuda("triangle_multiplication_implementation")
+        if config.float32():
+            return _f32_result(fp32.triangle_multiplication(self, pair, mask), out, accumulate)
         packed = self._packed.get(
             (self.projection.weight, self.gate.weight, self.gating_linear.weight),
             native.pack_triangle_weights)
@@ -104,6 +117,8 @@ class GridSelfAttention(nn.Module):
 
     def _run(self, pair, mask, out, accumulate):
         config.require_cuda("dot_product_attention_implementation")
+        if config.float32():
+            return _f32_result(fp32.grid_self_attention(self, pair, mask), out, accumulate)
         packed = self._packed.get(
             (self.q_projection.weight, self.k_projection.weight, self.v_projection.weight,
              self.gating_query.weight), native.pack_attention_weights)
@@ -136,6 +151,8 @@ class Transition(nn.Module):
 
     def _run(self, x, out, accumulate):
         config.require_cuda("gated_linear_unit_implementation")
+        if config.float32():
+            return _f32_result(fp32.transition(self, x), out, accumulate)
         w1 = self._glu_weight_cache.get((self.transition1.weight,), native.pack_glu_weight)
         return native.transition(x, self.input_layer_norm.weight, self.input_layer_norm.bias,
                                  self.input_layer_norm.eps, w1,
@@ -229,6 +246,8 @@ class DiffusionTransition(nn.Module):
     def _run(self, x, single_cond, out, accumulate, cond=None):
         config.require_cuda("gated_linear_unit_implementation")
         assert (single_cond is None) == (self.use_single_cond is False)
+        if config.float32():
+            return _f32_result(fp32.diffusion_transition(self, x, single_cond), out, accumulate)
         w1 = self._glu_weight_cache.get((self.transition1.weight,), native.pack_glu_weight)
         ln = self.adaptive_layernorm.layer_norm
         scale = shift = gate = None
@@ -273,6 +292,9 @@ class SelfAttention(nn.Module):
     def _run(self, x, mask, pair_logits, single_cond, out, accumulate, cond=None):
         config.require_cuda("dot_product_attention_implementation")
         assert (single_cond is None) == (self.use_single_cond is False)
+        if config.float32():
+            return _f32_result(fp32.self_attention(self, x, mask, pair_logits, single_cond), out,
+                               accumulate)
         packed = self._packed.get(
             (self.q_projection.weight, self.k_projection.weight, self.v_projection.weight,
              self.gating_query.weight), native.pack_attention_weights)
@@ -397,14 +419,27 @@ class DiffusionTransformer(nn.Module):
                          for p in self.pair_logits_projection))
         except RuntimeError:  # inference tensors carry no version counter: no reuse
             key = None
+        if key is not None:
+            key = (key, config.compute_dtype)
         if key is None or key != self._logits_key:
             ln = self.pair_input_layer_norm
             logits = []
-            for proj in self.pair_logits_projection:
-                w = proj.weight  # [(b h), c]: block j uses rows [j*H, (j+1)*H)
-                logits.append([native.pair_logits(pair_cond, ln.weight, ln.bias, ln.eps,
-                                                  w[j * self.num_head:(j + 1) * self.num_head])
-                               for j in range(self.super_block_size)])
+            if config.float32():
+                n = pair_cond.shape[0]
+                x = fp32.layer_norm(pair_cond, ln.weight, ln.bias, ln.eps)
+                for proj in self.pair_logits_projection:
+                    w = proj.weight.float()  # [(b h), c]: block j uses rows [j*H, (j+1)*H)
+                    out = torch.empty((w.shape[0], n, n), dtype=torch.float32, device=x.device)
+                    fp32.gemm(x.view(1, n * n, -1), w.unsqueeze(0),
+                              out.view(w.shape[0], n * n).t().unsqueeze(0))
+                    logits.append([out[j * self.num_head:(j + 1) * self.num_head]
+                                   for j in range(self.super_block_size)])
+            else:
+                for proj in self.pair_logits_projection:
+                    w = proj.weight  # [(b h), c]: block j uses rows [j*H, (j+1)*H)
+                    logits.append([native.pair_logits(pair_cond, ln.weight, ln.bias, ln.eps,
+                                                      w[j * self.num_head:(j + 1) * self.num_head])
+                                   for j in range(self.super_block_size)])
             self._logits, self._logits_key = logits, key
         return self._logits
 
@@ -412,13 +447,15 @@ class DiffusionTransformer(nn.Module):
                    logits: list[list[torch.Tensor]]) -> torch.Tensor:
         """The blocks of forward() with the pair logits given (act updated in place);
         the conditioning of all blocks is computed first, in one pass."""
-        cond = self.conditioning(single_cond)
+        # the fp32 path conditions each block from single_cond itself
+        cond = None if config.float32() else self.conditioning(single_cond)
         for s in range(self.num_super_blocks):
             for j in range(self.super_block_size):
                 i = s * self.super_block_size + j
                 self.self_attention[i].accumulate_(act, mask, logits[s][j], single_cond,
-                                                   cond=cond[i][0])
-                self.transition_block[i].accumulate_(act, single_cond, cond=cond[i][1])
+                                                   cond=None if cond is None else cond[i][0])
+                self.transition_block[i].accumulate_(act, single_cond,
+                                                     cond=None if cond is None else cond[i][1])
         return act
 
     def forward(self, act: torch.Tensor, mask: torch.Tensor, single_cond: torch.Tensor,
@@ -818,8 +855,12 @@ class PairformerBlock(nn.Module):
         if not self.with_single:
             return pair
         norm = self.single_pair_logits_norm
-        logits = native.pair_logits(pair, norm.weight, norm.bias, norm.eps,
-                                    _bf16(self._logits_w, self.single_pair_logits_projection.weight))
+        if config.float32():
+            logits = fp32.pair_logits(self, pair)
+        else:
+            logits = native.pair_logits(pair, norm.weight, norm.bias, norm.eps,
+                                        _bf16(self._logits_w,
+                                              self.single_pair_logits_projection.weight))
         self.single_attention_.accumulate_(single, seq_mask, logits)
         self.single_transition.accumulate_(single)
         return pair, single
