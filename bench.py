@@ -389,6 +389,7 @@ def run_reference(args) -> None:
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) pair/single, random-init N(0,0.02) weights)",
             "config": {"workload": "48-block Pairformer trunk, N_token=1024 (BASELINE config C4)",
+                   "trunk_cuda_graph": graph is not None,
                        "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR,
                        "c_single": C_SINGLE, "heads_pair": 4, "heads_single": 16, "seed": SEED,
                        "mask": "64-token padded tail", "parallelism": "host CPU"},
@@ -974,6 +975,28 @@ def run_cuda(args) -> None:
         torch.cuda.synchronize(dev)
         if _capi.device_error(clear=True):
             raise RuntimeError("a device wait expired during warm-up")
+        # Row-sharded over N GPUs a block is ~1/N of the GPU work but the same
+        # host work (some 25 stage calls, 50 launches), so the trunk is captured
+        # into one CUDA graph and replayed: the exchanges' barriers keep their
+        # epochs on the device, every rank replays the same graph.
+        use_graph = (os.environ.get("XFB_TRUNK_GRAPH", "1" if world > 1 else "0") == "1"
+                     and args.warmup > 0)  # the exchanges set up their buffers eagerly
+        graph = None
+        graph_launches = 0
+        if use_graph:
+            graph = torch.cuda.CUDAGraph()
+            c0 = _capi.launch_count()
+            with torch.cuda.graph(graph):
+                trunk(pair, single, pair_mask, seq_mask)
+            graph_launches = _capi.launch_count() - c0  # kernels in one replay
+            torch.cuda.synchronize(dev)
+            _barrier(world)
+
+        def step():
+            if graph is not None:
+                graph.replay()
+            else:
+                trunk(pair, single, pair_mask, seq_mask)
 
         # ---- device-resident timing
         sampler = ClockSampler(dev.index if dev.index is not None else 0)
@@ -985,18 +1008,19 @@ def run_cuda(args) -> None:
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            trunk(pair, single, pair_mask, seq_mask)
+            step()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         clocks = sampler.stop()
         _barrier(world)
-        launches = (_capi.launch_count() - launches0) // args.steps
+        launches = (_capi.launch_count() - launches0) // args.steps + graph_launches
         step_ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
         if args.skip_extras:
             if rank == 0:
                 print(json.dumps({"profile_run": True, "n_token": n_tok, "blocks": n_blocks,
-                                  "ms_per_block": step_ms / n_blocks, "gpu_launches": int(launches)}))
+                                  "ms_per_block": step_ms / n_blocks, "gpu_launches": int(launches),
+                                  "graph": graph is not None}))
             return
         # ---- end-to-end through the module API with host buffers
         out_pair = torch.empty_like(pair_h).pin_memory()
@@ -1009,11 +1033,19 @@ def run_cuda(args) -> None:
         f1 = torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for _ in range(args.steps):
-            p = pair_h.to(dev, non_blocking=True)
-            s = single_h.to(dev, non_blocking=True)
-            pm = pair_mask_h.to(dev, non_blocking=True)
-            sm = seq_mask_h.to(dev, non_blocking=True)
-            p, s = trunk(p, s, pm, sm)
+            if graph is not None:  # the graph's own input buffers
+                pair.copy_(pair_h, non_blocking=True)
+                single.copy_(single_h, non_blocking=True)
+                pair_mask.copy_(pair_mask_h, non_blocking=True)
+                seq_mask.copy_(seq_mask_h, non_blocking=True)
+                graph.replay()
+                p, s = pair, single
+            else:
+                p = pair_h.to(dev, non_blocking=True)
+                s = single_h.to(dev, non_blocking=True)
+                pm = pair_mask_h.to(dev, non_blocking=True)
+                sm = seq_mask_h.to(dev, non_blocking=True)
+                p, s = trunk(p, s, pm, sm)
             out_pair.copy_(p, non_blocking=True)
             out_single.copy_(s, non_blocking=True)
         f1.record(stream)
@@ -1046,6 +1078,7 @@ def run_cuda(args) -> None:
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) pair/single, random-init N(0,0.02) weights)",
         "config": {"workload": "48-block Pairformer trunk, N_token=1024 (BASELINE config C4)",
+                   "trunk_cuda_graph": graph is not None,
                    "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR, "c_single": C_SINGLE,
                    "heads_pair": 4, "heads_single": 16, "seed": SEED, "mask": "64-token padded tail",
                    "l2": "inputs larger than L2 (pair f32 = 512 MiB)",

@@ -431,6 +431,17 @@ XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, ui
                                 void* stream);
 XFB_API int xfb_exchange_wait(const void* flags, int world, uint32_t epoch, void* stream);
 
+/* The same barrier with the epoch kept on the device: `counter` is a uint32 in
+ * this GPU's memory, zero before the first barrier; xfb_exchange_signal_counted
+ * advances it and signals its new value, xfb_exchange_wait_counted waits for
+ * that value.  Nothing of the barrier is a launch argument that changes from
+ * one exchange to the next, so a stream segment of exchanges can be captured
+ * into a CUDA graph and replayed (every rank must replay the same segments). */
+XFB_API int xfb_exchange_signal_counted(void* const* peer_flags, int world, int rank,
+                                        uint32_t* counter, void* stream);
+XFB_API int xfb_exchange_wait_counted(const void* flags, int world, const uint32_t* counter,
+                                      void* stream);
+
 /* CUDA IPC for the exchange receive buffers (no counterpart in the reference).
  * xfb_ipc_handle: the IPC handle (xfb_ipc_handle_bytes() bytes) of the device
  * allocation holding ptr, and ptr's byte offset in it.  xfb_ipc_open: maps a

@@ -292,6 +292,21 @@ def _peer_worker(rank, world, port, n, results):
                                          unrouted)
             results[f"routed_same{rank}"] = bool(torch.equal(mine[0], copied[0]) and
                                                  torch.equal(s, s_copied))
+            # one block captured into a CUDA graph (device-side barrier epochs),
+            # replayed twice: the same two blocks again
+            g_pair = [pair[sharded.shard_rows(n, world, rank)].to(dev).contiguous()]
+            g_single = single.to(dev)
+            g_pm, g_seq = pmask.to(dev), seq.to(dev)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                sharded.pairformer_block(block, g_pair, g_pm, g_single, g_seq, peer)
+            for _ in range(2):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            results[f"graph_same{rank}"] = bool(torch.equal(g_pair[0], mine[0]) and
+                                                torch.equal(g_single, s))
+            del graph
             gathered = [torch.empty_like(mine[0]) for _ in range(world)]
             dist.all_gather(gathered, mine[0])
         torch.cuda.synchronize(dev)
@@ -323,5 +338,6 @@ def test_peer_exchange_over_nvlink():
     for r in range(world):
         assert all(results[f"same{r}"].values()), results[f"same{r}"]
         assert results[f"routed_same{r}"]
+        assert results[f"graph_same{r}"]
         assert results[f"err{r}"] == 0
     assert results["pair"] < TOL and results["single"] < TOL

@@ -107,6 +107,8 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_ipc_close": (_i, [_p, _i64]),
     "xfb_exchange_signal": (_i, [_p, _i, _i, ctypes.c_uint32, _p]),
     "xfb_exchange_wait": (_i, [_p, _i, ctypes.c_uint32, _p]),
+    "xfb_exchange_signal_counted": (_i, [_p, _i, _i, _p, _p]),
+    "xfb_exchange_wait_counted": (_i, [_p, _i, _p, _p]),
     "xfb_conditioning": (_i, [_p, _i64, _i64, _p, _i64, _p, _i64, _i, _p, _p]),
     "xfb_cross_pair_logits": (_i, [_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _d, _p,
                                    _p, _p]),

@@ -2663,8 +2663,9 @@ XFB_API int xfb_outer_product_mean(const void* msa, int msa_dtype, int64_t s, in
   return XFB_OK;
 }
 
-XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,
-                                void* stream) {
+namespace {
+int exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,
+                    uint32_t* counter, void* stream) {
   XFB_REQUIRE(world > 0 && world <= xfb::kMaxPeers && rank >= 0 && rank < world,
               "exchange barrier takes 1..16 GPUs");
   XFB_REQUIRE(peer_flags != nullptr, "peer flag pointers missing");
@@ -2678,19 +2679,45 @@ XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, ui
   p.world = world;
   p.rank = rank;
   p.epoch = epoch;
+  p.counter = counter;
   xfb::exchange_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
   XFB_LAUNCHED();
   return XFB_OK;
 }
 
-XFB_API int xfb_exchange_wait(const void* flags, int world, uint32_t epoch, void* stream) {
+int exchange_wait(const void* flags, int world, uint32_t epoch, const uint32_t* counter,
+                  void* stream) {
   XFB_REQUIRE(world > 0 && world <= xfb::kMaxPeers, "exchange barrier takes 1..16 GPUs");
   XFB_REQUIRE(flags != nullptr && (reinterpret_cast<uintptr_t>(flags) & 3) == 0,
               "flag array must be a 4-byte aligned device pointer");
   xfb::exchange_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint32_t*>(flags), world, epoch);
+      static_cast<const uint32_t*>(flags), world, epoch, counter);
   XFB_LAUNCHED();
   return XFB_OK;
+}
+}  // namespace
+
+XFB_API int xfb_exchange_signal(void* const* peer_flags, int world, int rank, uint32_t epoch,
+                                void* stream) {
+  return exchange_signal(peer_flags, world, rank, epoch, nullptr, stream);
+}
+
+XFB_API int xfb_exchange_wait(const void* flags, int world, uint32_t epoch, void* stream) {
+  return exchange_wait(flags, world, epoch, nullptr, stream);
+}
+
+XFB_API int xfb_exchange_signal_counted(void* const* peer_flags, int world, int rank,
+                                        uint32_t* counter, void* stream) {
+  XFB_REQUIRE(counter != nullptr && (reinterpret_cast<uintptr_t>(counter) & 3) == 0,
+              "the epoch counter must be a 4-byte aligned device pointer");
+  return exchange_signal(peer_flags, world, rank, 0, counter, stream);
+}
+
+XFB_API int xfb_exchange_wait_counted(const void* flags, int world, const uint32_t* counter,
+                                      void* stream) {
+  XFB_REQUIRE(counter != nullptr && (reinterpret_cast<uintptr_t>(counter) & 3) == 0,
+              "the epoch counter must be a 4-byte aligned device pointer");
+  return exchange_wait(flags, world, 0, counter, stream);
 }
 
 }  // extern "C"

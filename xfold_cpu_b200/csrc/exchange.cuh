@@ -70,25 +70,44 @@ __global__ void __launch_bounds__(256) exchange_copy_kernel(const __grid_constan
 // kErrWaitPeer and returns, so a peer that never signals cannot hang this GPU.
 constexpr int kMaxPeers = 16;
 
+//
+// With a counter (a uint32 in this GPU's memory, zero at the start) the epoch
+// is not a launch argument: the signal kernel advances the counter and uses
+// its new value, the wait kernel reads it.  Every rank passes the same barriers
+// in the same order, so the counters agree, and a stream segment holding such
+// barriers can be captured into a CUDA graph and replayed.
 struct PeerFlags {
   uint32_t* flags[kMaxPeers];  // each GPU's flag array, as mapped in this process
   int world;
   int rank;
   uint32_t epoch;
+  uint32_t* counter;  // or null: use epoch
 };
 
 __global__ void exchange_signal_kernel(const __grid_constant__ PeerFlags p) {
+  __shared__ uint32_t epoch;
+  if (threadIdx.x == 0) {
+    uint32_t e = p.epoch;
+    if (p.counter != nullptr) {
+      e = *p.counter + 1;
+      *p.counter = e;
+    }
+    epoch = e;
+  }
+  __syncthreads();
   const int s = threadIdx.x;
   if (s < p.world) {
     __threadfence_system();
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[s] + p.rank), "r"(p.epoch)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[s] + p.rank), "r"(epoch)
                  : "memory");
   }
 }
 
-__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch) {
+__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch,
+                                     const uint32_t* counter) {
   const int s = threadIdx.x;
   if (s >= world) return;
+  if (counter != nullptr) epoch = *counter;
   const uint64_t start = global_ns();
   while (true) {
     uint32_t v;

@@ -196,8 +196,7 @@ class PeerExchange:
         self.barrier = barrier or os.environ.get("XFB_EXCHANGE_BARRIER", "flags")
         if self.barrier not in ("flags", "nccl"):
             raise ValueError("barrier must be 'flags' or 'nccl'")
-        self._flags = None  # (local flag array, ctypes array of every GPU's array)
-        self._epoch = 0
+        self._flags = None  # (local flag array, every GPU's array, epoch counter)
 
     # -- receive buffers, shared once per (pattern, shape, dtype)
     def _recv(self, kind, shape, dtype, device):
@@ -259,12 +258,15 @@ class PeerExchange:
                     for r, meta in enumerate(metas)]
             torch.cuda.synchronize(device)  # the zero fill is done before any peer signals
             self._dist.barrier(group=self.group)
-            self._flags = (local, (ctypes.c_void_p * self.world)(*ptrs))
-        self._epoch += 1
-        local, peers = self._flags
-        _capi.call("xfb_exchange_signal", ctypes_addressof(peers), self.world, self.rank,
-                   self._epoch, stream)
-        _capi.call("xfb_exchange_wait", local.data_ptr(), self.world, self._epoch, stream)
+            # the epoch lives on the device (advanced by each signal), so a
+            # captured CUDA graph of exchanges can be replayed
+            counter = torch.zeros(1, dtype=torch.int32, device=device)
+            self._flags = (local, (ctypes.c_void_p * self.world)(*ptrs), counter)
+        local, peers, counter = self._flags
+        _capi.call("xfb_exchange_signal_counted", ctypes_addressof(peers), self.world, self.rank,
+                   counter.data_ptr(), stream)
+        _capi.call("xfb_exchange_wait_counted", local.data_ptr(), self.world, counter.data_ptr(),
+                   stream)
 
     def _box(self, src_ptr, dst_ptr, d0, d1, d2_bytes, s0, s1, t0, t1):
         from . import _capi
