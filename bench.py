@@ -940,6 +940,7 @@ def run_cuda(args) -> None:
         blocks.append(blk.to(dev))
     pair_h, pair_mask_h, single_h, seq_mask_h = _inputs(n_tok, SEED)
     sharded_parity = None
+    single_stream = single_exchange = None
     if world > 1:
         # row-sharded pair: this rank holds rows R_rank of the one N x N trunk
         from xfold_cpu_b200 import sharded
@@ -952,6 +953,12 @@ def run_cuda(args) -> None:
                     else sharded.PeerExchange())
         sharded_parity = _sharded_parity(dev, blocks[0], pair_h, pair_mask_h, single_h,
                                           seq_mask_h, rows, world, exchange)
+        # the single track overlaps the next block's pair operators on its own
+        # stream with its own exchange (XFB_SINGLE_OVERLAP=0: in line)
+        if (isinstance(exchange, sharded.PeerExchange)
+                and os.environ.get("XFB_SINGLE_OVERLAP", "1") == "1"):
+            single_stream = torch.cuda.Stream(dev)
+            single_exchange = sharded.PeerExchange()
         pair_h = pair_h[rows].contiguous()
     pair_h, pair_mask_h = pair_h.pin_memory(), pair_mask_h.pin_memory()
     single_h, seq_mask_h = single_h.pin_memory(), seq_mask_h.pin_memory()
@@ -964,9 +971,13 @@ def run_cuda(args) -> None:
     def trunk(p, s, pm, sm):
         for blk in blocks:
             if world > 1:
-                sharded.pairformer_block(blk, [p], pm, s, sm, exchange)
+                sharded.pairformer_block(blk, [p], pm, s, sm, exchange,
+                                         single_stream=single_stream,
+                                         single_exchange=single_exchange)
             else:
                 blk(p, pm, s, sm)
+        if world > 1 and single_stream is not None:
+            torch.cuda.current_stream(dev).wait_stream(single_stream)
         return p, s
 
     with torch.inference_mode():

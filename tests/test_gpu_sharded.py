@@ -307,6 +307,18 @@ def _peer_worker(rank, world, port, n, results):
             results[f"graph_same{rank}"] = bool(torch.equal(g_pair[0], mine[0]) and
                                                 torch.equal(g_single, s))
             del graph
+            # the single track on its own stream and exchange, overlapping the
+            # next block's pair operators: the same two blocks
+            side, side_ex = torch.cuda.Stream(dev), sharded.PeerExchange()
+            o_pair = [pair[sharded.shard_rows(n, world, rank)].to(dev).contiguous()]
+            o_single = single.to(dev)
+            for _ in range(2):
+                sharded.pairformer_block(block, o_pair, g_pm, o_single, g_seq, peer,
+                                         single_stream=side, single_exchange=side_ex)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            results[f"overlap_same{rank}"] = bool(torch.equal(o_pair[0], mine[0]) and
+                                                  torch.equal(o_single, s))
             gathered = [torch.empty_like(mine[0]) for _ in range(world)]
             dist.all_gather(gathered, mine[0])
         torch.cuda.synchronize(dev)
@@ -339,5 +351,6 @@ def test_peer_exchange_over_nvlink():
         assert all(results[f"same{r}"].values()), results[f"same{r}"]
         assert results[f"routed_same{r}"]
         assert results[f"graph_same{r}"]
+        assert results[f"overlap_same{r}"]
         assert results[f"err{r}"] == 0
     assert results["pair"] < TOL and results["single"] < TOL

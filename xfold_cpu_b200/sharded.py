@@ -550,13 +550,19 @@ def _attention(mod, pairs, pair_mask, exchange, stages):
 
 def pairformer_block(block: PairformerBlock, pairs: list[torch.Tensor], pair_mask: torch.Tensor,
                      single: torch.Tensor | None, seq_mask: torch.Tensor | None,
-                     exchange, stages=None):
+                     exchange, stages=None, single_stream=None, single_exchange=None):
     """One Pairformer block on a row-sharded pair, updated in place.
 
     pairs: this process's row blocks ([N/G, N, c] f32 contiguous, one per local
     shard, in `exchange.ranks` order); pair_mask: the full [N, N] mask (every
     process holds it); single / seq_mask: this process's copy of the single
-    track, updated in place (once per process)."""
+    track, updated in place (once per process).
+
+    The pair track never reads the single track, so with `single_stream` (a
+    CUDA stream) and `single_exchange` (a second exchange of the same ranks,
+    with its own buffers and barrier) the single track runs on that stream
+    after the pair-logit rows and overlaps the next block's pair operators; the
+    caller makes its stream wait for `single_stream` before reading `single`."""
     stages = NativeStages() if stages is None else stages
     rows, n, c = pairs[0].shape
     check_sharding(n, c, exchange.world)
@@ -573,7 +579,20 @@ def pairformer_block(block: PairformerBlock, pairs: list[torch.Tensor], pair_mas
     # single track sharded by query rows: each rank's pair-logit rows are the
     # bias rows of its own queries, so only the updated single rows are gathered
     logits = [stages.pair_logits_rows(block, pair) for pair in pairs]
-    x_in = single.clone() if len(pairs) > 1 else single  # every shard reads the old single
+    if single_stream is None:
+        _single_track(block, single, seq_mask, logits, rows, exchange, stages)
+        return pairs, single
+    main = torch.cuda.current_stream(single.device)
+    single_stream.wait_stream(main)
+    for lg in logits:  # read on the side stream after the main stream drops them
+        lg.record_stream(single_stream)
+    with torch.cuda.stream(single_stream):
+        _single_track(block, single, seq_mask, logits, rows, single_exchange, stages)
+    return pairs, single
+
+
+def _single_track(block, single, seq_mask, logits, rows, exchange, stages):
+    x_in = single.clone() if len(logits) > 1 else single  # every shard reads the old single
     for lg, r in zip(logits, exchange.ranks):
         stages.single_attention_rows(block, x_in, seq_mask, lg, r * rows, single)
     for r in exchange.ranks:
@@ -581,4 +600,3 @@ def pairformer_block(block: PairformerBlock, pairs: list[torch.Tensor], pair_mas
     gathered = exchange.gather_rows([single[r * rows:(r + 1) * rows].unsqueeze(0)
                                      for r in exchange.ranks])
     single.copy_(gathered[0][0])
-    return pairs, single
