@@ -50,3 +50,38 @@ def test_argument_errors_are_reported_without_a_device():
     rc = lib.xfb_linear(None, 4, 7, None, 8, None, None, 0, 0, None)
     assert rc == _capi.ERR_INVALID
     assert "multiples of 8" in _capi.last_error()
+
+
+def _c_layout(struct: str, fields: list[str]) -> list[int]:
+    """sizeof and offsetof of a header struct, from a C program compiled with gcc."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    body = "".join(f'  printf("%zu\\n", offsetof({struct}, {f}));\n' for f in fields)
+    src = ('#include <stdio.h>\n#include <stddef.h>\n'
+           f'#include "{HEADER}"\nint main(void) {{\n'
+           f'  printf("%zu\\n", sizeof({struct}));\n{body}  return 0;\n}}\n')
+    with tempfile.TemporaryDirectory() as tmp:
+        c, exe = Path(tmp) / "layout.c", Path(tmp) / "layout"
+        c.write_text(src)
+        subprocess.run(["gcc", "-o", str(exe), str(c)], check=True, capture_output=True)
+        out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    return [int(v) for v in out.split()]
+
+
+@pytest.mark.parametrize("cls,struct", [(_capi.F32GemmArgs, "xfb_f32_gemm_args"),
+                                        (_capi.F32AttentionArgs, "xfb_f32_attention_args"),
+                                        (_capi.CopyBox, "xfb_copy_box")])
+def test_ctypes_structs_match_header_layout(cls, struct):
+    names = [name for name, _ in cls._fields_]
+    got = [ctypes_sizeof(cls)] + [getattr(cls, n).offset for n in names]
+    assert got == _c_layout(struct, names)
+
+
+def ctypes_sizeof(cls) -> int:
+    import ctypes
+
+    return ctypes.sizeof(cls)
