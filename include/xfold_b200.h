@@ -676,6 +676,17 @@ XFB_API int xfb_f32_silu_mul(const float* h, int64_t rows, int64_t f, float* y, 
 XFB_API int xfb_f32_scale_shift(float* y, const float* scale, const float* shift, int64_t n,
                                 void* stream);
 
+/* ------------------------------------------------------------------ checkpoint upload
+ * Scatter of a parameter record stream (xfold/params.py:39-95, read by
+ * get_alphafold3_params :245-256) already on the device as one blob: record r's
+ * array bytes [spans[3r], + spans[3r+2]) of src go to dst + spans[3r+1] (4-byte
+ * aligned; the caller picks 256-byte aligned slots so every array is a typed
+ * view).  `spans` is the device copy of `host_spans`; the host copy is used to
+ * check every span against src_bytes / dst_bytes before the launch. */
+XFB_API int xfb_gather_bytes(const void* src, int64_t src_bytes, void* dst, int64_t dst_bytes,
+                             const int64_t* spans, const int64_t* host_spans, int64_t count,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

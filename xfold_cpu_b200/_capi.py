@@ -146,6 +146,7 @@ SIGNATURES: dict[str, tuple] = {
     "xfb_f32_attention": (_i, [_p, _p]),
     "xfb_f32_silu_mul": (_i, [_p, _i64, _i64, _p, _p]),
     "xfb_f32_scale_shift": (_i, [_p, _p, _p, _i64, _p]),
+    "xfb_gather_bytes": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p]),
 }
 
 

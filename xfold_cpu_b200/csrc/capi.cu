@@ -25,6 +25,7 @@
 #include "window_attention.cuh"
 #include "msa.cuh"
 #include "fp32.cuh"
+#include "checkpoint.cuh"
 
 #ifndef XFB_NVCC_FLAGS
 #define XFB_NVCC_FLAGS "unknown"
@@ -2993,6 +2994,34 @@ XFB_API int xfb_f32_scale_shift(float* y, const float* scale, const float* shift
   const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, int64_t(sms) * 16));
   xfb::f32_scale_shift_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, scale,
                                                                                      shift, n);
+  XFB_LAUNCHED();
+  return XFB_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- checkpoint upload
+
+extern "C" {
+
+XFB_API int xfb_gather_bytes(const void* src, int64_t src_bytes, void* dst, int64_t dst_bytes,
+                             const int64_t* spans, const int64_t* host_spans, int64_t count,
+                             void* stream) {
+  XFB_REQUIRE(count >= 0, "negative record count");
+  if (count == 0) return XFB_OK;
+  XFB_REQUIRE(src && dst && spans && host_spans, "gather_bytes pointers missing");
+  // the spans are checked on the host copy the caller also uploaded
+  for (int64_t r = 0; r < count; ++r) {
+    const int64_t so = host_spans[3 * r], dof = host_spans[3 * r + 1], nb = host_spans[3 * r + 2];
+    XFB_REQUIRE(so >= 0 && nb >= 0 && so <= src_bytes - nb, "record outside the source blob");
+    XFB_REQUIRE(dof >= 0 && dof % 4 == 0 && dof <= dst_bytes - nb,
+                "record outside the arena or not 4-byte aligned");
+  }
+  int sms;
+  XFB_TRY(sm_count(&sms));
+  const int blocks = static_cast<int>(std::min<int64_t>(count, int64_t(sms) * 4));
+  xfb::gather_bytes_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), spans, count);
   XFB_LAUNCHED();
   return XFB_OK;
 }
