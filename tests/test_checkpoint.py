@@ -24,6 +24,8 @@ def _encode(scope, name, arr: np.ndarray) -> bytes:
 
 
 def _host_values(blob: bytes, rec: checkpoint.Record) -> np.ndarray:
+    if rec.nbytes == 0:
+        return np.zeros(rec.shape, dtype=np.float32)
     t = torch.frombuffer(bytearray(blob[rec.offset:rec.offset + rec.nbytes]),
                          dtype=checkpoint.DTYPES[rec.dtype])
     return t.reshape(rec.shape).float().numpy()
