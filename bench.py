@@ -1096,10 +1096,15 @@ def run_cuda(args) -> None:
                    "parallelism": (f"row-sharded pair over {world} GPUs ("
                                    + ("NCCL all-to-all / all-gather"
                                       if os.environ.get("XFB_EXCHANGE", "peer") == "collective"
-                                      else "peer-store exchange kernel over NVLink + "
-                                      + ("NCCL barrier"
-                                         if os.environ.get("XFB_EXCHANGE_BARRIER") == "nccl"
-                                         else "flag barrier"))
+                                      else ("routed stages (producers store into the peers' "
+                                            "receive buffers over NVLink)"
+                                            if getattr(exchange, "routes", False)
+                                            else "peer-store exchange kernel over NVLink")
+                                      + " + " + ("NCCL barrier"
+                                                 if os.environ.get("XFB_EXCHANGE_BARRIER") == "nccl"
+                                                 else "flag barrier")
+                                      + ("; single track on its own stream"
+                                         if single_stream is not None else ""))
                                    + ")") if world > 1 else "single GPU"},
         "e2e": {"value": round(e2e_ms / n_blocks, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
