@@ -107,6 +107,19 @@ struct EpiCtx {
   uint32_t tmem;      // TMEM address of tile column 0 in this thread's lane quarter
   uint8_t* staging;   // staging buffer of this tile
   const uint8_t* aux; // auxiliary input tile (nullptr when the epilogue has none)
+  float pre;          // Epi::prefetch(ctx), read before the accumulator was ready
+};
+
+// Epilogues with a `float prefetch(const EpiCtx&) const` method get it called
+// for each tile before the epilogue waits for the tile's accumulator, so a
+// global load it issues overlaps the main loop; compute() reads it as ctx.pre.
+template <class E, class = void>
+struct EpiPrefetchOf {
+  static constexpr bool value = false;
+};
+template <class E>
+struct EpiPrefetchOf<E, std::void_t<decltype(&E::prefetch)>> {
+  static constexpr bool value = true;
 };
 
 template <int BN, int STAGES, class Epi>
@@ -334,6 +347,7 @@ __global__ void __launch_bounds__(GemmWarps<Epi>::kThreads, 1)
       ctx.bat = bat;
       ctx.m0 = (rem / shape.n_tiles) * kGemmBM;
       ctx.n0 = (rem % shape.n_tiles) * BN;
+      if constexpr (EpiPrefetchOf<Epi>::value) ctx.pre = epi.prefetch(ctx);
       // Every epilogue thread runs every tile and arrives on every barrier: a
       // wait that gave up (the CTA is aborting) skips the work, not the arrivals.
       bool ok = mbar_wait(&tfull[acc], acc_phase, kErrWaitEpilogue, abort_flag);
@@ -812,11 +826,15 @@ struct EpiTriProj {
     return (mask != nullptr && j < n) ? __ldg(mask + static_cast<int64_t>(bat) * n + j) : 1.f;
   }
 
+  // the tile row's mask value, loaded while the tile's MMAs run
+  __device__ float prefetch(const EpiCtx& c) const {
+    return c.n0 / 128 < n_proj_tiles ? row_mask(c.bat, c.m0 + c.row) : 1.f;
+  }
+
   __device__ void compute(const EpiCtx& c) const {
     const int tile = c.n0 / 128;
-    const int j = c.m0 + c.row;
     if (tile < n_proj_tiles) {
-      const float mval = row_mask(c.bat, j);
+      const float mval = c.pre;
       __nv_bfloat16* sa = reinterpret_cast<__nv_bfloat16*>(c.staging);
       __nv_bfloat16* sb = sa + 32 * 128;
       // projection and gate columns with one TMEM round trip
