@@ -107,10 +107,10 @@ struct EpiCtx {
   uint32_t tmem;      // TMEM address of tile column 0 in this thread's lane quarter
   uint8_t* staging;   // staging buffer of this tile
   const uint8_t* aux; // auxiliary input tile (nullptr when the epilogue has none)
-  float pre;          // Epi::prefetch(ctx), read before the accumulator was ready
+  float2 pre;         // Epi::prefetch(ctx), read before the accumulator was ready
 };
 
-// Epilogues with a `float prefetch(const EpiCtx&) const` method get it called
+// Epilogues with a `float2 prefetch(const EpiCtx&) const` method get it called
 // for each tile before the epilogue waits for the tile's accumulator, so a
 // global load it issues overlaps the main loop; compute() reads it as ctx.pre.
 template <class E, class = void>
@@ -557,9 +557,12 @@ struct EpiOutLnGated : EpiOutGated<BN, OUT_F32> {
   const float* colbias;  // [N]
   int rows;
 
+  // the row's statistics, loaded while the tile's MMAs run
+  __device__ float2 prefetch(const EpiCtx& c) const { return stats[min(c.m0 + c.row, rows - 1)]; }
+
   __device__ void compute(const EpiCtx& c) const {
     constexpr int kHalf = BN / 2;
-    const float2 st = stats[min(c.m0 + c.row, rows - 1)];
+    const float2 st = c.pre;
 #pragma unroll 1
     for (int c0 = 0; c0 < kHalf; c0 += 16) {
       const int col = c.half * kHalf + c0;
@@ -827,14 +830,14 @@ struct EpiTriProj {
   }
 
   // the tile row's mask value, loaded while the tile's MMAs run
-  __device__ float prefetch(const EpiCtx& c) const {
-    return c.n0 / 128 < n_proj_tiles ? row_mask(c.bat, c.m0 + c.row) : 1.f;
+  __device__ float2 prefetch(const EpiCtx& c) const {
+    return make_float2(c.n0 / 128 < n_proj_tiles ? row_mask(c.bat, c.m0 + c.row) : 1.f, 0.f);
   }
 
   __device__ void compute(const EpiCtx& c) const {
     const int tile = c.n0 / 128;
     if (tile < n_proj_tiles) {
-      const float mval = c.pre;
+      const float mval = c.pre.x;
       __nv_bfloat16* sa = reinterpret_cast<__nv_bfloat16*>(c.staging);
       __nv_bfloat16* sb = sa + 32 * 128;
       // projection and gate columns with one TMEM round trip
