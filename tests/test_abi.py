@@ -85,3 +85,34 @@ def ctypes_sizeof(cls) -> int:
     import ctypes
 
     return ctypes.sizeof(cls)
+
+
+@pytest.mark.skipif(not LIB_PATH.exists(), reason="library not built")
+def test_new_entry_points_reject_bad_arguments_without_a_device():
+    """Argument checks of the routed stages, the float32 path and the checkpoint
+    scatter run before any device work."""
+    import ctypes
+
+    lib = _capi.load()
+    p = ctypes.c_void_p
+    dst = (p * 2)(16, 32)
+    # routed contraction: rank outside the world
+    assert lib.xfb_triangle_contraction_routed(None, None, 4, 64, 1, dst, 2, 5, None) == \
+        _capi.ERR_INVALID
+    assert "rank" in _capi.last_error()
+    # routed destinations must be non-null
+    null_dst = (p * 2)(16, None)
+    assert lib.xfb_grid_attention_prepare_routed(None, 0, 32, 64, 128, 4, None, None, 1e-5, None,
+                                                 null_dst, 2, 0, None, None) == _capi.ERR_INVALID
+    # float32 GEMM: unknown activation
+    args = _capi.F32GemmArgs()
+    args.m = args.n = args.k = args.batch = 4
+    args.act = 2
+    assert lib.xfb_f32_gemm(ctypes.addressof(args), None) == _capi.ERR_INVALID
+    # float32 LayerNorm wider than 1024 columns
+    assert lib.xfb_f32_layer_norm(None, 4, 2048, 2048, None, None, 1e-5, None, 2048, None) == \
+        _capi.ERR_INVALID
+    # checkpoint scatter: a span past the end of the source blob
+    spans = (ctypes.c_int64 * 3)(100, 0, 64)
+    assert lib.xfb_gather_bytes(16, 128, 32, 1024, spans, spans, 1, None) == _capi.ERR_INVALID
+    assert "outside the source" in _capi.last_error()
