@@ -14,17 +14,23 @@ the trunk (48 blocks); the metric is ms per block = step time / 48.
   roofline  the dominant kernels timed live with CUDA events (same shapes as
          inside the block): the triangle-attention flash kernel and the
          triangle contraction GEMM, FLOPs / time against the measured bf16 peak.
-  cpu_baseline  the CPU oracle (a restatement of the reference torch path) on
-         this host's cores, one block at N = 256 in float32, scaled to N = 1024
-         by the algorithmic FLOP ratio.
+  cpu_baseline  the reference's own PairformerBlock (baseline/_ref, torch
+         backend, CPU bf16 autocast) on this host's cores, one C4 block at
+         N = 1024, each of its seven sub-modules timed once (the CPU oracle
+         under the same autocast when the reference is not installed).
+  parity / parity_fp32  checkers after the timed regions: block 0 at N = 1024
+         against the CPU oracle (bf16 bar 1e-2), and BASELINE C1 (N = 256,
+         float32 path) against the reference's own block in float32 (1e-4).
 
 `--impl reference` times that CPU path alone on the same metric (the reference
 arm); under torchrun only rank 0 runs it.
 
 Multi-GPU (--gpus N under torchrun): one N = 1024 trunk with its pair
-row-sharded over the N GPUs (rank r holds rows [rN/G, (r+1)N/G)), exchanges
-by the peer-store kernel over NVLink ("scaling": "strong"); value = the
-per-block time of the slowest rank.
+row-sharded over the N GPUs (rank r holds rows [rN/G, (r+1)N/G)); the routed
+stages store each exchanged tensor straight into the peers' receive buffers
+over NVLink, the single track runs on its own stream, and the trunk is
+replayed as one CUDA graph ("scaling": "strong"); value = the per-block time
+of the slowest rank.
 """
 
 from __future__ import annotations
@@ -348,6 +354,63 @@ def block_parity(dev, blk) -> dict:
             "reference_bf16_per_update": ref_bf16,
             "what": "block 0 at N=1024 (C4), each update vs the CPU oracle on the same input, "
                     "sampled pair rows, single track in full"}
+
+
+def fp32_parity(dev) -> dict:
+    """BASELINE config C1 in float32: one Pairformer block at N = 256, seed 0,
+    masks all ones, random init N(0, 0.02), run with the library's float32
+    path (fastnn.config.compute_dtype = "float32") and with the reference's own
+    PairformerBlock on the CPU in float32 (baseline/_ref; the CPU oracle when
+    the reference is not installed); max |got - ref| / max |ref| of the pair
+    and single updates (the north_star's fp32 bar is 1e-4).  Checker only: runs
+    after the timed regions."""
+    import torch
+
+    from xfold_cpu_b200.fastnn import config
+    from xfold_cpu_b200.nn import PairformerBlock, init_params_
+
+    n = 256
+    blk = PairformerBlock(c_pair=C_PAIR, c_single=C_SINGLE).eval()
+    init_params_(blk, seed=0)
+    g = torch.Generator().manual_seed(0)
+    pair = torch.randn(n, n, C_PAIR, generator=g)
+    single = torch.randn(n, C_SINGLE, generator=g)
+    seq_mask = torch.ones(n)
+    pair_mask = torch.ones(n, n)
+    state = {k: v.detach().float().cpu().clone() for k, v in blk.state_dict().items()}
+    with torch.inference_mode():
+        if (REF_DIR / "xfold").is_dir():
+            if str(REF_DIR) not in sys.path:
+                sys.path.insert(0, str(REF_DIR))
+            from xfold.nn.pairformer import PairformerBlock as RefBlock
+
+            ref_blk = RefBlock(c_pair=C_PAIR, c_single=C_SINGLE).eval()
+            ref_blk.load_state_dict(state, strict=True)
+            ref_p, ref_s = ref_blk(pair.clone(), pair_mask, single.clone(), seq_mask)
+            against = "the reference's PairformerBlock (torch backend, CPU float32)"
+        else:
+            import oracle
+
+            ref_p, ref_s = oracle.pairformer_block(pair, pair_mask, single, seq_mask, state)
+            against = "the CPU float32 oracle (baseline/_ref not installed)"
+        old = config.compute_dtype
+        config.compute_dtype = config.FLOAT32
+        try:
+            blk = blk.to(dev)
+            p, s = pair.to(dev), single.to(dev)
+            blk(p, pair_mask.to(dev), s, seq_mask.to(dev))
+            torch.cuda.synchronize(dev)
+        finally:
+            config.compute_dtype = old
+        import oracle
+
+        pair_err = oracle.relative_error(p.cpu() - pair, ref_p - pair)
+        single_err = oracle.relative_error(s.cpu() - single, ref_s - single)
+    return {"pair_update_rel_err": float(f"{pair_err:.3g}"),
+            "single_update_rel_err": float(f"{single_err:.3g}"), "tolerance": 1e-4,
+            "ok": max(pair_err, single_err) <= 1e-4,
+            "what": f"BASELINE C1 (one block, N=256, fp32, seed 0) with compute_dtype float32 "
+                    f"vs {against}"}
 
 
 def run_reference(args) -> None:
@@ -1077,6 +1140,7 @@ def run_cuda(args) -> None:
         return
     base = cpu_baseline() if world == 1 else None
     parity = block_parity(dev, blocks[0]) if world == 1 and n_tok == N_TOKEN else None
+    parity_fp32 = fp32_parity(dev) if world == 1 and n_tok == N_TOKEN else None
     if atom is not None:
         atom["cpu_port"] = cpu_baseline_atom()
     if evo is not None:
@@ -1120,6 +1184,7 @@ def run_cuda(args) -> None:
         "cpu_baseline": base,
         "finite": finite,
         "parity": parity,
+        "parity_fp32": parity_fp32,
         "sharded_parity": sharded_parity,
         "extras": {"diffusion_c5_5x200": {**c5_run, "ms": round(c5_ms, 1), "gpus": world,
                                           "ms_note": "max over ranks of each rank's samples"},
