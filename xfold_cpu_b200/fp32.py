@@ -114,7 +114,13 @@ def attention(q, k, v, out, bias=None, mask=None, gate=None, scale=None) -> torc
             bias = bias.contiguous()
         args.bias, (args.bias_sb, args.bias_sh, args.bias_si, _) = bias.data_ptr(), bias.stride()
     if mask is not None:
+        if mask.dim() > 2:
+            if mask.dim() != 4 or mask.shape[1] != 1 or mask.shape[2] != 1:
+                raise ValueError("the float32 attention takes key masks [K], [B, K] or "
+                                 "[B, 1, 1, K]")
         mask = mask.reshape(-1, nk)
+        if mask.shape[0] not in (1, bsz):
+            raise ValueError("mask batch must be 1 or the attention batch")
         if mask.stride(-1) != 1:
             mask = mask.contiguous()
         args.mask = mask.data_ptr()
