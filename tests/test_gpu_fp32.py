@@ -174,3 +174,60 @@ def test_diffusion_transformer_fp32():
     with torch.inference_mode():
         mod.to(DEV)(a, seq.to(DEV), cond.to(DEV), pair_cond.to(DEV))
     assert _err(a - act.to(DEV), ref - act) < TOL
+
+
+def test_small_triangle_directions_fp32():
+    """The reference's own small-case check (3 tokens, c = 8, an identity mask;
+    tests/test_cpu_runtime.py:104-115 of the reference): each direction equals
+    the explicit per-channel contraction, in float32."""
+    for outgoing in (False, True):
+        mod = TriangleMultiplication(8, _outgoing=outgoing).eval()
+        init_params_(mod, seed=21, std=0.3, perturb_layer_norm=True)
+        g = torch.Generator().manual_seed(22)
+        pair, mask = torch.randn(3, 3, 8, generator=g), torch.eye(3)
+        p = {k: v.detach().float() for k, v in mod.state_dict().items()}
+        with torch.no_grad():
+            x = torch.nn.functional.layer_norm(pair, (8,), p["left_norm_input.weight"],
+                                               p["left_norm_input.bias"])
+            proj = (x @ p["projection.weight"].T) * mask[..., None] * torch.sigmoid(
+                x @ p["gate.weight"].T)
+            a, b = proj[..., 0::2], proj[..., 1::2]
+            prod = torch.stack([a[..., c] @ b[..., c].T if outgoing else b[..., c].T @ a[..., c]
+                                for c in range(8)], dim=-1)
+            z = torch.nn.functional.layer_norm(prod, (8,), p["center_norm.weight"],
+                                               p["center_norm.bias"])
+            want = (z @ p["output_projection.weight"].T) * torch.sigmoid(
+                x @ p["gating_linear.weight"].T)
+        with torch.inference_mode():
+            got = mod.to(DEV)(pair.to(DEV), mask.to(DEV))
+        assert _err(got, want) < 1e-5
+
+
+def test_small_pairformer_block_fp32():
+    """3 tokens, c_pair = c_single = 8, two heads each (the reference's
+    end-to-end smoke shape, tests/test_cpu_runtime.py:117-125), against the
+    float32 oracle."""
+    block = PairformerBlock(n_heads=2, c_pair=8, c_single=8, n_heads_pair=2).eval()
+    init_params_(block, seed=23, std=0.3, perturb_layer_norm=True)
+    g = torch.Generator().manual_seed(24)
+    pair, single = torch.randn(3, 3, 8, generator=g), torch.randn(3, 8, generator=g)
+    ref_p, ref_s = oracle.pairformer_block(pair, torch.ones(3, 3), single, torch.ones(3),
+                                           _params(block), n_heads=2, n_heads_pair=2)
+    block = block.to(DEV)
+    p, s = pair.to(DEV), single.to(DEV)
+    with torch.inference_mode():
+        block(p, torch.ones(3, 3, device=DEV), s, torch.ones(3, device=DEV))
+    assert torch.isfinite(p).all() and torch.isfinite(s).all()
+    assert _err(p - pair.to(DEV), ref_p - pair) < TOL
+    assert _err(s - single.to(DEV), ref_s - single) < TOL
+
+
+def test_f32_layer_norm_matches_torch():
+    g = torch.Generator(device="cuda").manual_seed(25)
+    for c in (8, 128, 384, 768):
+        x = torch.randn(257, c, device=DEV, generator=g) * 3 + 1
+        w = torch.randn(c, device=DEV, generator=g)
+        b = torch.randn(c, device=DEV, generator=g)
+        got = fp32.layer_norm(x, w, b, 1e-5)
+        want = torch.nn.functional.layer_norm(x, (c,), w, b, 1e-5)
+        assert oracle.relative_error(got.cpu(), want.cpu()) < 1e-5
