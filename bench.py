@@ -427,7 +427,8 @@ def run_reference(args) -> None:
 
     threads = _host_threads()
     torch.set_num_threads(threads)
-    kind, parts = _reference_parts(N_TOKEN)
+    n = args.n  # N_TOKEN unless a smaller --n is asked for (a quick check)
+    kind, parts = _reference_parts(n)
     order = [BLOCK_PARTS[i % len(BLOCK_PARTS)] for i in range(args.warmup + args.steps)]
     warm = _time_parts(parts, order[:args.warmup])
     t0 = time.perf_counter()
@@ -444,16 +445,16 @@ def run_reference(args) -> None:
     value = sum(per.values()) * 1e3
     who = ("the reference's own torch modules (xfold.nn.pairformer from baseline/_ref)"
            if kind == "reference" else "the CPU oracle (restated reference torch path)")
-    sample = (f"one step = one of the block's 7 sub-modules at N={N_TOKEN} in rotation under CPU "
+    sample = (f"one step = one of the block's 7 sub-modules at N={n} in rotation under CPU "
               f"bf16 autocast, {who}; value = sum of the sub-modules' mean times")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(wall / max(args.steps, 1) * 1e3, 1),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) pair/single, random-init N(0,0.02) weights)",
-            "config": {"workload": "48-block Pairformer trunk, N_token=1024 (BASELINE config C4)",
-                   "trunk_cuda_graph": graph is not None,
-                       "n_token": N_TOKEN, "blocks": N_BLOCKS, "c_pair": C_PAIR,
+            "config": {"workload": f"48-block Pairformer trunk, N_token={n}"
+                                   + (" (BASELINE config C4)" if n == N_TOKEN else ""),
+                       "n_token": n, "blocks": N_BLOCKS, "c_pair": C_PAIR,
                        "c_single": C_SINGLE, "heads_pair": 4, "heads_single": 16, "seed": SEED,
                        "mask": "64-token padded tail", "parallelism": "host CPU"},
             "per_part_ms": {k: round(v * 1e3, 1) for k, v in per.items()},

@@ -115,3 +115,27 @@ def test_af3_compat_mirrors_the_reference_argument_checks():
         af3_compat.triangle_multiplication(*([None] * 11), weights_packed=True)
     assert af3_compat.packed_weight_api == 0
     assert af3_compat.load_extension() is af3_compat
+
+
+def test_bench_reference_arm_prints_its_line(tmp_path):
+    """`bench.py --impl reference` end to end on the CPU at a small N (the
+    driver runs it at the default N = 1024): one JSON line with the reference
+    arm's keys."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference",
+                          "--steps", "7", "--warmup", "1", "--n", "64"],
+                         capture_output=True, text=True, timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["e2e"]["value"] == line["value"] and line["cpu_baseline"]["kind"] in (
+        "reference", "port")
+    assert set(line["per_part_ms"]) == {"triangle_multiplication_outgoing",
+                                        "triangle_multiplication_incoming", "pair_attention1",
+                                        "pair_attention2", "pair_transition",
+                                        "single_attention", "single_transition"}
